@@ -1,0 +1,498 @@
+#!/usr/bin/env python3
+"""Benchmark of the quantized linear-layer path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = the DiT attention-projection GEMM sweep, int8 fused-dequant:
+K = 3072, N in {3072 (out-proj), 9216 (fused QKV)}, M in {8192, 32768, 112640}
+tokens -- six launches of the tcgen05 GEMM per step.  `value` is whole-job
+TOPS (2*M*N*K summed over the six shapes, all ranks) with inputs resident in
+HBM; `e2e` is the same metric through the public API with host (pinned)
+activations copied in and every output copied back inside the timed region.
+Secondary figures timed in the same run (not part of `value`): the fp8 e4m3
+GEMM sweep, fused RMSNorm + adaLN modulation + per-token quant on
+[2, 56320, 3072] (fp8 and int8), fused SwiGLU + per-token int8 quant on the
+[32768, 24576] fc1 output, and, with N > 1, an NCCL all-gather of one output.
+
+Under torchrun (N > 1) each rank runs the same per-rank workload on its own
+GPU (token-sharded DiT: weights replicated, no collective on the data path):
+weak scaling, timed as the max over ranks.
+
+`--impl reference` times the reference's CPU path (torch `_int_mm` + float32
+eager epilogue, src/ck_int8_patch_intmm.py:63-71, restated by oracle/) on the
+host cores, on bounded M-slices of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+K_DIM = 3072
+N_SWEEP = (3072, 9216)
+M_SWEEP = (8192, 32768, 112640)
+SHAPES = [(M, N, K_DIM) for N in N_SWEEP for M in M_SWEEP]
+METRIC = "INT8 fused-dequant GEMM TOPS (DiT shapes) and fused norm/quant HBM GB/s"
+WORKLOAD = "dit_attn_proj_gemm_sweep_int8"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def ops_of(shapes):
+    return float(sum(2 * M * N * K for M, N, K in shapes))
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true")
+    return ap.parse_args()
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def read_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return d, "measured"
+    except (OSError, ValueError):
+        return dict(FALLBACK_PEAKS), "fallback"
+
+
+def read_traffic(name):
+    """DRAM traffic per launch from a committed ncu summary (profiles/traffic.json)."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+            return json.load(f).get(name)
+    except (OSError, ValueError):
+        return None
+
+
+# --------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi sampled every 200 ms while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+
+    def __init__(self, gpu_id: str):
+        self.gpu_id = gpu_id
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu_id}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.3)
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        rows = [r.split(",") for r in out.strip().splitlines() if r.count(",") >= 8]
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
+        smax = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
+        power = [float(r[3]) for r in rows if r[3].strip().replace(".", "").isdigit()]
+        reasons = set()
+        for r in rows:
+            for name, v in zip(self.REASONS, r[5:9]):
+                if v.strip().lower() == "active":
+                    reasons.add(name)
+        loaded = [s for s in sm if smax and s > 0.5 * max(smax)] or sm
+        return {"sm_mhz": statistics.median(loaded) if loaded else None,
+                "sm_max_mhz": max(smax) if smax else None,
+                "power_w_max": max(power) if power else None,
+                "samples": len(rows), "reasons": sorted(reasons)}
+
+
+def gpu_smi_id(torch, dev):
+    props = torch.cuda.get_device_properties(dev)
+    uuid = getattr(props, "uuid", None)
+    if uuid is not None:
+        s = str(uuid)
+        return s if s.startswith("GPU-") else f"GPU-{s}"
+    return str(dev.index)
+
+
+# --------------------------------------------------------------------- inputs
+def make_activation(torch, ops, M, K, gen, dev, outlier_idx, kind):
+    """bf16 N(0,1) activations with 1% outlier channels x20, per-token quantised."""
+    x = torch.randn(M, K, generator=gen, device=dev, dtype=torch.float32)
+    x[:, outlier_idx] *= 20.0
+    x = x.to(torch.bfloat16)
+    q, s = ops.quant_rows(x, kind)
+    del x
+    return q, s
+
+
+def make_weight(torch, ops, N, K, gen, dev, kind):
+    """N(0, 0.02) weights, per-output-channel quantised."""
+    w = (torch.randn(N, K, generator=gen, device=dev, dtype=torch.float32) * 0.02).to(torch.bfloat16)
+    q, s = ops.quant_rows(w, kind)
+    return q, s
+
+
+def build_gemm_set(torch, ops, dev, kind, seed):
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(seed)
+    outliers = torch.randperm(K_DIM, generator=gen, device=dev)[: K_DIM // 100]
+    weights = {}
+    for N in N_SWEEP:
+        wq, ws = make_weight(torch, ops, N, K_DIM, gen, dev, kind)
+        bias = (torch.randn(N, generator=gen, device=dev) * 0.01).to(torch.bfloat16)
+        weights[N] = (wq, ws, bias)
+    acts = {M: make_activation(torch, ops, M, K_DIM, gen, dev, outliers, kind) for M in M_SWEEP}
+    items = []
+    for M, N, K in SHAPES:
+        xq, xs = acts[M]
+        wq, ws, bias = weights[N]
+        out = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+        items.append({"M": M, "N": N, "K": K, "x": xq, "xs": xs, "w": wq, "ws": ws, "bias": bias, "out": out})
+    return items
+
+
+# --------------------------------------------------------------------- timing
+def time_gemm_sweep(torch, ops, items, steps, warmup, stream):
+    """Device time of `steps` sweeps (events around every launch on the launch stream)."""
+    with torch.cuda.stream(stream):
+        for _ in range(warmup):
+            for it in items:
+                ops.gemm_dequant(it["x"], it["w"], it["xs"], it["ws"], it["bias"], out=it["out"], stream=stream)
+        stream.synchronize()
+        ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in items]
+              for _ in range(steps)]
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for s in range(steps):
+            for i, it in enumerate(items):
+                ev[s][i][0].record(stream)
+                ops.gemm_dequant(it["x"], it["w"], it["xs"], it["ws"], it["bias"], out=it["out"], stream=stream)
+                ev[s][i][1].record(stream)
+        t1.record(stream)
+        t1.synchronize()
+    total_ms = t0.elapsed_time(t1)
+    per_shape = [statistics.mean(ev[s][i][0].elapsed_time(ev[s][i][1]) for s in range(steps))
+                 for i in range(len(items))]
+    return total_ms, per_shape
+
+
+def time_e2e(torch, ops, items, steps, dev):
+    """Same sweep through the public API with host activations in and outputs out.
+
+    Three streams pipeline the shapes: copy-in of shape i+1 and copy-out of
+    shape i-1 overlap the GEMM of shape i.  Weights stay resident on the device
+    (model parameters); activations + their scales are copied in and every
+    output is copied back, every step."""
+    h2d, comp, d2h = (torch.cuda.Stream(dev) for _ in range(3))
+    host_x = [it["x"].cpu().pin_memory() for it in items]
+    host_xs = [it["xs"].cpu().pin_memory() for it in items]
+    host_out = [torch.empty(it["M"], it["N"], dtype=torch.bfloat16, pin_memory=True) for it in items]
+    dx = [torch.empty_like(it["x"]) for it in items]
+    dxs = [torch.empty_like(it["xs"]) for it in items]
+    n = len(items)
+    ev_in = [torch.cuda.Event() for _ in range(n)]
+    ev_gemm = [torch.cuda.Event() for _ in range(n)]
+    ev_out = [torch.cuda.Event() for _ in range(n)]
+    first = [True] * n
+
+    def one_step():
+        for i, it in enumerate(items):
+            with torch.cuda.stream(h2d):
+                if not first[i]:
+                    h2d.wait_event(ev_gemm[i])
+                dx[i].copy_(host_x[i], non_blocking=True)
+                dxs[i].copy_(host_xs[i], non_blocking=True)
+                ev_in[i].record(h2d)
+            comp.wait_event(ev_in[i])
+            if not first[i]:
+                comp.wait_event(ev_out[i])
+            ops.gemm_dequant(dx[i], it["w"], dxs[i], it["ws"], it["bias"], out=it["out"], stream=comp)
+            ev_gemm[i].record(comp)
+            with torch.cuda.stream(d2h):
+                d2h.wait_event(ev_gemm[i])
+                host_out[i].copy_(it["out"], non_blocking=True)
+                ev_out[i].record(d2h)
+            first[i] = False
+
+    one_step()
+    torch.cuda.synchronize(dev)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(h2d)
+    for _ in range(steps):
+        one_step()
+    d2h.wait_event(ev_gemm[-1])
+    t1.record(d2h)
+    t1.synchronize()
+    torch.cuda.synchronize(dev)
+    ms = t0.elapsed_time(t1)
+    h2d_bytes = sum(it["x"].numel() + 4 * it["xs"].numel() for it in items)
+    d2h_bytes = sum(2 * it["M"] * it["N"] for it in items)
+    ok = all(torch.equal(host_out[i], items[i]["out"].cpu()) for i in (0, n - 1))
+    return ms, h2d_bytes, d2h_bytes, ok
+
+
+def time_rows(torch, ops, dev, steps, warmup, stream):
+    """Fused norm/mod/quant (config [2, 56320, 3072]) and SwiGLU/quant ([32768, 24576] in)."""
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(3)
+    B, T, D = 2, 56320, 3072
+    x = torch.randn(B * T, D, generator=gen, device=dev).to(torch.bfloat16)
+    shift = (torch.randn(B, D, generator=gen, device=dev) * 0.1).to(torch.bfloat16)
+    scale = (torch.randn(B, D, generator=gen, device=dev) * 0.1).to(torch.bfloat16)
+    Mf, F = 32768, 12288
+    y = torch.randn(Mf, 2 * F, generator=gen, device=dev).to(torch.bfloat16)
+    res = {}
+
+    def timed(fn, nbytes, key):
+        with torch.cuda.stream(stream):
+            for _ in range(warmup):
+                fn()
+            stream.synchronize()
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            for _ in range(steps):
+                fn()
+            b.record(stream)
+            b.synchronize()
+        ms = a.elapsed_time(b) / steps
+        res[key] = {"ms": round(ms, 4), "gbs": round(nbytes / ms / 1e6, 1), "bytes": nbytes}
+
+    norm_bytes = 2 * B * T * D + B * T * D + 4 * B * T + 2 * 2 * B * D
+    for kind in ("fp8_e4m3", "int8"):
+        timed(lambda: ops.rms_mod_quant(x, shift, scale, rows_per_mod=T, eps=1e-6, kind=kind, stream=stream),
+              norm_bytes, f"rms_mod_quant_{kind}")
+    sw_bytes = 4 * Mf * F + Mf * F + 4 * Mf
+    timed(lambda: ops.swiglu_quant_fc1(y, kind="int8", stream=stream), sw_bytes, "swiglu_quant_int8")
+    del x, y
+    return res
+
+
+def cpu_gemm_sample(O, torch, min_seconds=10.0, max_seconds=30.0):
+    """The reference CPU path on M-slices of the sweep: torch._int_mm + float32
+    epilogue (oracle restatement of src/ck_int8_patch_intmm.py:63-71)."""
+    import numpy as np
+    rng = np.random.default_rng(0)
+    m_slice = 2048
+    w = {N: rng.integers(-127, 128, (N, K_DIM)).astype(np.int8) for N in N_SWEEP}
+    ws = {N: (rng.random(N).astype(np.float32) + 0.5) * 1e-3 for N in N_SWEEP}
+    bias = {N: O.round_bf16((rng.standard_normal(N) * 0.01).astype(np.float32)) for N in N_SWEEP}
+    x = rng.integers(-127, 128, (m_slice, K_DIM)).astype(np.int8)
+    xs = (rng.random(m_slice).astype(np.float32) + 0.5) * 1e-3
+    ops_done = 0.0
+    t0 = time.perf_counter()
+    reps = 0
+    while True:
+        for N in N_SWEEP:
+            O.gemm_i8_dequant(x, w[N], xs, ws[N], bias[N], "bf16")
+            ops_done += 2.0 * m_slice * N * K_DIM
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= min_seconds or el >= max_seconds:
+            break
+    return {"value": round(ops_done / el / 1e12, 4), "unit": "TOPS", "cores": torch.get_num_threads(),
+            "kind": "port",
+            "sample": f"{reps} x M-slices of {m_slice} tokens for N in {list(N_SWEEP)}, K={K_DIM}; "
+                      f"torch._int_mm + float32 epilogue ({el:.1f} s)"}
+
+
+# --------------------------------------------------------------------- arms
+def run_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    import torch
+    from oracle import oracle as O
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    budget = max(1.0, 150.0 / max(args.steps + args.warmup, 1))
+    step_s = []
+    for i in range(args.warmup + args.steps):
+        r = cpu_gemm_sample(O, torch, min_seconds=min(budget, 3.0), max_seconds=budget)
+        if i >= args.warmup:
+            step_s.append(r)
+    v = statistics.mean(r["value"] for r in step_s)
+    line = {"impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": "TOPS", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "shapes_MNK": SHAPES, "sample": "M-slices of 2048 tokens"},
+            "cpu_baseline": {"value": round(v, 4), "unit": "TOPS", "cores": torch.get_num_threads(), "kind": "port",
+                             "sample": step_s[-1]["sample"]},
+            "e2e": {"value": round(v, 4), "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args):
+    import torch
+    rank, world, local = dist_env()
+    if world > 1:
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+
+    from __graft_entry__ import load_package
+    load_package()
+    from thor_int8_gemm_b200 import ops
+
+    stream = torch.cuda.Stream(dev)
+    items = build_gemm_set(torch, ops, dev, "int8", seed=1234 + rank)
+    torch.cuda.synchronize(dev)
+
+    def barrier():
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize(dev)
+
+    clocks = ClockSampler(gpu_smi_id(torch, dev))
+    barrier()
+    clocks.start()
+    barrier()
+    total_ms, per_shape = time_gemm_sweep(torch, ops, items, args.steps, args.warmup, stream)
+    barrier()
+    clk = clocks.stop()
+    status = ops.device_status(dev)
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([total_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+    step_ops = ops_of(SHAPES)
+    value = world * step_ops * args.steps / (total_ms / 1e3) / 1e12
+    launch_ms = sum(per_shape)
+    achieved = step_ops / (launch_ms / 1e3) / 1e12
+    peaks, peak_src = read_peaks()
+    int8_peak = 2.0 * peaks["bf16_tflops"]
+
+    # e2e through the public API with host buffers
+    e2e_ms, h2d_b, d2h_b, e2e_ok = time_e2e(torch, ops, items, args.e2e_steps, dev)
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_value = world * step_ops * args.e2e_steps / (e2e_ms / 1e3) / 1e12
+
+    extras = {}
+    if not args.no_extras:
+        extras["per_shape_tops"] = {f"{it['M']}x{it['N']}x{it['K']}": round(2 * it["M"] * it["N"] * it["K"] / (ms / 1e3) / 1e12, 1)
+                                    for it, ms in zip(items, per_shape)}
+        items8 = None
+        del items8
+        f8 = build_gemm_set(torch, ops, dev, "fp8_e4m3", seed=99 + rank)
+        f8_ms, f8_shape = time_gemm_sweep(torch, ops, f8, max(3, args.steps // 2), args.warmup, stream)
+        extras["fp8_gemm_sweep_tops"] = round(step_ops * max(3, args.steps // 2) / (f8_ms / 1e3) / 1e12, 1)
+        del f8
+        torch.cuda.empty_cache()
+        rows = time_rows(torch, ops, dev, max(5, args.steps), args.warmup, stream)
+        hbm = peaks["hbm_gbs"]
+        for k, v in rows.items():
+            v["frac_of_hbm"] = round(v["gbs"] / hbm, 3)
+        extras["row_kernels"] = rows
+        if world > 1:
+            import torch.distributed as dist
+            shard = items[0]["out"]
+            gathered = torch.empty((world * shard.shape[0], shard.shape[1]), dtype=shard.dtype, device=dev)
+            for _ in range(2):
+                dist.all_gather_into_tensor(gathered, shard)
+            torch.cuda.synchronize(dev)
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record()
+            for _ in range(5):
+                dist.all_gather_into_tensor(gathered, shard)
+            b.record()
+            b.synchronize()
+            ms = a.elapsed_time(b) / 5
+            extras["allgather_out_8192x3072_bf16"] = {"ms": round(ms, 3),
+                                                      "busbw_gbs": round(gathered.numel() * 2 * (world - 1) / world / ms / 1e6, 1)}
+    status |= ops.device_status(dev)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle import oracle as O
+        torch.set_num_threads(os.cpu_count() or 1)
+        cpu = cpu_gemm_sample(O, torch)
+
+    traffic = read_traffic("gemm_i8_sweep_per_step_bytes")
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "TOPS", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "shapes_MNK": SHAPES,
+                       "activations": "bf16 N(0,1), 1% channels x20, per-token int8 (amax/127, RNE, clamp 127)",
+                       "weights": "N(0,0.02) per-channel int8", "bias": "bf16 N(0,0.01)", "out": "bf16",
+                       "parallelism": f"token-sharded x{world} (weights replicated, no data-path collective)",
+                       "l2": "inputs larger than L2: one step touches 0.47 GB of activations and writes "
+                             "3.8 GB of outputs, so each shape's inputs are evicted before it repeats"},
+            "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(int8_peak, 1),
+                         "unit": "TFLOP/s", "frac": round(achieved / int8_peak, 4), "traffic": traffic,
+                         "peak_source": f"2 x {peak_src} cuBLAS bf16 burst ({peaks['bf16_tflops']} TF/s): "
+                                        "dense int8 runs at twice the bf16 rate; int ops counted as FLOP",
+                         "kernel": "gemm_dequant_kernel<int8,bf16>"},
+            "e2e": {"value": round(e2e_value, 2), "unit": "TOPS", "h2d_bytes_per_step": h2d_b,
+                    "d2h_bytes_per_step": d2h_b, "outputs_verified": bool(e2e_ok),
+                    "note": "activations + scales copied in and all outputs copied back every step; "
+                            "weights resident; 3-stream pipeline"},
+            "gpu_launches": len(SHAPES) * args.steps,
+            "clocks": clk,
+            "device_status": status,
+            "cpu_baseline": cpu,
+            "extras": extras,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,183 @@
+"""GPU parity of the int8 / fp8 fused-dequant GEMM against the oracle and the
+reference's own outputs (tests/golden/gemm_golden.npz)."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+DT = {"bf16": torch.bfloat16, "f16": torch.float16, "f32": torch.float32}
+
+
+@pytest.fixture(scope="module")
+def ops():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from thor_int8_gemm_b200 import ops as _ops
+    yield _ops
+    assert _ops.device_status() == 0, "a bounded wait ran out during the GEMM tests"
+
+
+def out_bits(t: torch.Tensor) -> np.ndarray:
+    t = t.cpu()
+    if t.dtype == torch.float32:
+        return t.numpy()
+    return t.view(torch.int16).numpy().view(np.uint16)
+
+
+def run_gemm(ops, x8, w8, xs, ws, bias, dt):
+    dev = "cuda"
+    b = None if bias is None else torch.from_numpy(np.asarray(bias, np.float32)).to(DT[dt]).to(dev)
+    out = ops.gemm_dequant(torch.from_numpy(x8).to(dev), torch.from_numpy(w8).to(dev),
+                           torch.from_numpy(np.asarray(xs, np.float32)).to(dev),
+                           torch.from_numpy(np.asarray(ws, np.float32)).to(dev), b, out_dtype=DT[dt])
+    return out_bits(out)
+
+
+GOLD = np.load(os.path.join(HERE, "golden", "gemm_golden.npz"))
+
+
+@pytest.mark.parametrize("i", range(int(GOLD["n_cases"])))
+def test_gemm_i8_matches_reference_golden(ops, i):
+    p = f"g{i}_"
+    M, N, K, hb, _ = GOLD[p + "meta"]
+    dt = str(GOLD[p + "dtype"])
+    got = run_gemm(ops, GOLD[p + "x8"], GOLD[p + "w8"], GOLD[p + "xs"], GOLD[p + "ws"],
+                   GOLD[p + "bias"] if hb else None, dt)
+    np.testing.assert_array_equal(got, GOLD[p + "out"])
+
+
+CASES = [
+    # M, N, K, bias, dtype, scalar ws
+    (256, 3072, 3072, True, "bf16", False),      # config 0 shape
+    (7777, 520, 208, True, "bf16", False),       # ragged M, N tail, K not a multiple of 128
+    (128, 256, 16, False, "f16", False),         # smallest eligible K
+    (300, 1000, 4096, True, "f32", False),
+    (1, 8, 32, True, "bf16", True),              # single row, tiny N
+    (2048, 9216, 512, False, "bf16", True),      # N = QKV width, many tiles per CTA
+    (333, 24576 // 8, 12288 // 8, True, "bf16", False),
+]
+
+
+@pytest.mark.parametrize("M,N,K,hb,dt,scalar", CASES)
+def test_gemm_i8_matches_oracle(ops, M, N, K, hb, dt, scalar):
+    rng = np.random.default_rng(M * 7 + N * 3 + K)
+    x8 = rng.integers(-127, 128, (M, K)).astype(np.int8)
+    w8 = rng.integers(-127, 128, (N, K)).astype(np.int8)
+    xs = (rng.random(M) + 0.5).astype(np.float32) * 1e-3
+    ws = (rng.random(1 if scalar else N) + 0.5).astype(np.float32) * 1e-2
+    bias = (rng.standard_normal(N) * 0.5).astype(np.float32) if hb else None
+    if bias is not None and dt != "f32":
+        bias = O.out_to_f32(O.cast_out(bias, dt), dt)
+    ref = O.gemm_i8_dequant(x8, w8, xs, ws, bias, dt)
+    got = run_gemm(ops, x8, w8, xs, ws, bias, dt)
+    np.testing.assert_array_equal(got, ref)
+
+
+def test_gemm_i8_extreme_values_exact(ops):
+    """-128/127 operands at the largest K the audit covered (int32 never overflows)."""
+    M, N, K = 130, 200, 65536
+    x8 = np.full((M, K), -128, np.int8)
+    x8[1::2] = 127
+    w8 = np.full((N, K), -128, np.int8)
+    w8[::3] = 127
+    xs = np.full(M, 1e-6, np.float32)
+    ws = np.full(N, 1e-3, np.float32)
+    np.testing.assert_array_equal(run_gemm(ops, x8, w8, xs, ws, None, "f32"),
+                                  O.gemm_i8_dequant(x8, w8, xs, ws, None, "f32"))
+
+
+def test_gemm_i8_strided_rows(ops):
+    """Row strides larger than the row (views into a wider buffer)."""
+    dev = "cuda"
+    M, N, K = 257, 384, 320
+    rng = np.random.default_rng(5)
+    xb = rng.integers(-127, 128, (M, K + 64)).astype(np.int8)
+    wb = rng.integers(-127, 128, (N, K + 32)).astype(np.int8)
+    xs = (rng.random(M) + 0.5).astype(np.float32)
+    ws = (rng.random(N) + 0.5).astype(np.float32) * 1e-3
+    out_buf = torch.zeros(M, N + 64, dtype=torch.bfloat16, device=dev)
+    out = out_buf[:, :N]
+    ops.gemm_dequant(torch.from_numpy(xb).to(dev)[:, :K], torch.from_numpy(wb).to(dev)[:, :K],
+                     torch.from_numpy(xs).to(dev), torch.from_numpy(ws).to(dev), None, out=out)
+    ref = O.gemm_i8_dequant(xb[:, :K], wb[:, :K], xs, ws, None, "bf16")
+    np.testing.assert_array_equal(out_bits(out.contiguous()), ref)
+    assert not torch.any(out_buf[:, N:].float() != 0), "wrote outside the output view"
+
+
+def test_gemm_i8_full_size_row_sampled(ops):
+    """M=32768 x N=9216 x K=3072 (a config-1 QKV shape): every output row of a
+    sample of 48 rows, bit-exact against the oracle."""
+    dev = "cuda"
+    M, N, K = 32768, 9216, 3072
+    g = torch.Generator(device="cpu").manual_seed(11)
+    x8 = torch.randint(-127, 128, (M, K), dtype=torch.int8, generator=g)
+    w8 = torch.randint(-127, 128, (N, K), dtype=torch.int8, generator=g)
+    xs = torch.rand(M, generator=g) * 1e-3 + 1e-4
+    ws = torch.rand(N, generator=g) * 1e-2 + 1e-3
+    bias = (torch.randn(N, generator=g) * 0.01).to(torch.bfloat16)
+    out = ops.gemm_dequant(x8.to(dev), w8.to(dev), xs.to(dev), ws.to(dev), bias.to(dev))
+    rows = np.sort(np.random.default_rng(3).choice(M, 48, replace=False))
+    rows[0], rows[-1] = 0, M - 1
+    ref = O.gemm_i8_dequant(x8.numpy()[rows], w8.numpy(), xs.numpy()[rows], ws.numpy(),
+                            bias.float().numpy(), "bf16")
+    np.testing.assert_array_equal(out_bits(out[torch.from_numpy(rows).to(dev)]), ref)
+
+
+@pytest.mark.parametrize("M,N,K,dt", [(256, 512, 512, "bf16"), (1000, 272, 3072, "f32"), (130, 136, 96, "f16")])
+def test_gemm_fp8_within_accumulation_tolerance(ops, M, N, K, dt):
+    dev = "cuda"
+    rng = np.random.default_rng(M + N + K)
+    a = O.round_bf16(rng.standard_normal((M, K)).astype(np.float32))
+    w = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+    aq, xs = O.quant_rows(a, O.QUANT_FP8)
+    wq, ws = O.quant_rows(w, O.QUANT_FP8)
+    bias = O.out_to_f32(O.cast_out((rng.standard_normal(N) * 0.01).astype(np.float32), dt), dt) if dt != "f32" \
+        else (rng.standard_normal(N) * 0.01).astype(np.float32)
+    out = ops.gemm_dequant(torch.from_numpy(aq).to(dev).view(torch.float8_e4m3fn),
+                           torch.from_numpy(wq).to(dev).view(torch.float8_e4m3fn),
+                           torch.from_numpy(xs).to(dev), torch.from_numpy(ws).to(dev),
+                           torch.from_numpy(bias).to(DT[dt]).to(dev), out_dtype=DT[dt])
+    got = O.out_to_f32(out_bits(out), dt).astype(np.float64)
+    ref = O.out_to_f32(O.gemm_fp8_dequant(aq, wq, xs, ws, bias, dt), dt).astype(np.float64)
+    tol = O.fp8_gemm_tolerance(aq, wq, xs, ws, K)
+    ulp = {"bf16": 2.0 ** -8, "f16": 2.0 ** -11, "f32": 2.0 ** -24}[dt]
+    bound = tol * 1.01 + np.abs(ref) * ulp * 1.01 + 1e-30
+    assert np.all(np.abs(got - ref) <= bound), float(np.max(np.abs(got - ref) / bound))
+
+
+def test_gemm_rejects_bad_arguments(ops):
+    dev = "cuda"
+    x8 = torch.zeros(128, 40, dtype=torch.int8, device=dev)     # K % 16 != 0 -> stride not 16-byte multiple
+    w8 = torch.zeros(64, 40, dtype=torch.int8, device=dev)
+    xs = torch.ones(128, device=dev)
+    ws = torch.ones(64, device=dev)
+    from thor_int8_gemm_b200._lib import T8GError
+    with pytest.raises(T8GError) as ei:
+        ops.gemm_dequant(x8, w8, xs, ws)
+    assert ei.value.code == 1 and "16 bytes" in ei.value.message
+    with pytest.raises(ValueError):
+        ops.gemm_dequant(x8[:, :32], w8[:, :16], xs, ws)
+
+
+def test_gemm_i8_output_beyond_2_31_elements(ops):
+    """M*N > 2^31 (the audit range of the reference's int64-offset fix): the last
+    rows land where the oracle says."""
+    dev = "cuda"
+    M, N, K = 75000, 28672, 256
+    g = torch.Generator(device="cpu").manual_seed(12)
+    x8 = torch.randint(-127, 128, (M, K), dtype=torch.int8, generator=g)
+    w8 = torch.randint(-127, 128, (N, K), dtype=torch.int8, generator=g)
+    xs = torch.rand(M, generator=g) * 1e-3 + 1e-4
+    ws = torch.rand(N, generator=g) * 1e-2 + 1e-3
+    out = ops.gemm_dequant(x8.to(dev), w8.to(dev), xs.to(dev), ws.to(dev))
+    rows = np.array([0, 1, 37449, 74873, M - 2, M - 1])
+    ref = O.gemm_i8_dequant(x8.numpy()[rows], w8.numpy(), xs.numpy()[rows], ws.numpy(), None, "bf16")
+    np.testing.assert_array_equal(out_bits(out[torch.from_numpy(rows).to(dev)]), ref)
+    del out
+    torch.cuda.empty_cache()

@@ -1,0 +1,160 @@
+"""The oracle against the reference's own outputs (tests/golden/*.npz).
+
+The goldens were produced by tests/golden/make_golden.py from the reference
+implementation: `_gemm_intmm` (src/ck_int8_patch_intmm.py:63-71) and the Triton
+kernels of src/ck_int8_patch_thor.py and src/ck_fused_mod_norm_quant.py.
+"""
+import os
+
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+GEMM = np.load(os.path.join(HERE, "golden", "gemm_golden.npz"))
+FUSED = np.load(os.path.join(HERE, "golden", "fused_golden.npz"))
+
+
+def bf16_ulp_diff(a_bits, b_bits):
+    a = np.asarray(a_bits, np.uint16).astype(np.int64)
+    b = np.asarray(b_bits, np.uint16).astype(np.int64)
+    oa = np.where(a & 0x8000, -(a & 0x7FFF), a & 0x7FFF)
+    ob = np.where(b & 0x8000, -(b & 0x7FFF), b & 0x7FFF)
+    return np.abs(oa - ob)
+
+
+def f32_ulp_diff(a, b):
+    a = np.asarray(a, np.float32).view(np.int32).astype(np.int64)
+    b = np.asarray(b, np.float32).view(np.int32).astype(np.int64)
+    return np.abs(a - b)
+
+
+@pytest.mark.parametrize("i", range(int(GEMM["n_cases"])))
+def test_gemm_matches_reference_bit_exact(i):
+    p = f"g{i}_"
+    M, N, K, hb, scalar_ws = GEMM[p + "meta"]
+    dt = str(GEMM[p + "dtype"])
+    out = O.gemm_i8_dequant(GEMM[p + "x8"], GEMM[p + "w8"], GEMM[p + "xs"], GEMM[p + "ws"],
+                            GEMM[p + "bias"] if hb else None, dt)
+    assert out.shape == (M, N)
+    np.testing.assert_array_equal(out, GEMM[p + "out"])
+
+
+def test_int_matmul_matches_int64():
+    rng = np.random.default_rng(0)
+    a = rng.integers(-128, 128, (37, 80)).astype(np.int8)
+    w = rng.integers(-128, 128, (29, 80)).astype(np.int8)
+    ref = a.astype(np.int64) @ w.astype(np.int64).T
+    np.testing.assert_array_equal(O.int_matmul_nt(a, w), ref.astype(np.int32))
+
+
+def test_e4m3_conversion_matches_torch_rne():
+    torch = pytest.importorskip("torch")
+    rng = np.random.default_rng(1)
+    vals = [rng.standard_normal(20000).astype(np.float32) * s for s in (1e-3, 0.05, 1.0, 30.0, 200.0)]
+    # every representable value and every midpoint between neighbours (ties)
+    fin = O._E4M3_FINITE.astype(np.float32)
+    mids = ((O._E4M3_FINITE[1:] + O._E4M3_FINITE[:-1]) / 2).astype(np.float32)
+    vals += [fin, -fin, mids, -mids, np.array([0.0, -0.0, 448.0, -448.0], np.float32)]
+    v = np.concatenate(vals)
+    v = np.clip(v, -448, 448).astype(np.float32)
+    ref = torch.from_numpy(v).to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+    np.testing.assert_array_equal(O.f32_to_e4m3(v), ref)
+    np.testing.assert_array_equal(O.e4m3_to_f32(ref), torch.from_numpy(ref).view(torch.float8_e4m3fn).float().numpy())
+
+
+def test_bf16_rounding_matches_torch():
+    torch = pytest.importorskip("torch")
+    rng = np.random.default_rng(2)
+    v = np.concatenate([rng.standard_normal(50000).astype(np.float32) * 10.0 ** e for e in range(-30, 30, 6)])
+    ref = torch.from_numpy(v).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
+    np.testing.assert_array_equal(O.f32_to_bf16(v), ref)
+
+
+@pytest.mark.parametrize("i", range(int(FUSED["n_rms"])))
+def test_rms_mod_tensorwise_vs_reference(i):
+    p = f"r{i}_"
+    x = O.bf16_to_f32(FUSED[p + "x"])
+    w, s, b = (O.bf16_to_f32(FUSED[p + k]) for k in "wsb")
+    eps = float(FUSED[p + "eps"])
+    q, scale, h, res, amax = O.rms_mod_res_tensorwise(x, w, s, b, eps)
+    # h, res: one-pass vs the Triton reduction order -> within one bf16 ulp
+    assert bf16_ulp_diff(h, FUSED[p + "h"]).max() <= 1
+    assert bf16_ulp_diff(res, FUSED[p + "res"]).max() <= 1
+    # the scale comes from the float32 amax: within one float32 ulp or two
+    assert f32_ulp_diff(scale, FUSED[p + "scale"]).max() <= 2
+    # the quantiser given the reference's own h and scale is bit-exact
+    q_given, _ = O.quantize_with_scale(O.bf16_to_f32(FUSED[p + "h"]), FUSED[p + "scale"][0], O.QUANT_FP8), None
+    np.testing.assert_array_equal(q_given, FUSED[p + "q"])
+    if not np.any(FUSED[p + "x"]):
+        # amax = 0 -> scale = 1e-12 (bench/a3p_device_scale_test.py:119-135)
+        assert FUSED[p + "scale"][0] == np.float32(1e-12) == scale
+        assert not np.any(FUSED[p + "q"] & 0x7F)
+
+
+def test_rms_mod_segments_vs_reference():
+    """The per-segment driver of src/ck_fused_patch.py:105-136 with s = bf16(1+scale)."""
+    x = O.bf16_to_f32(FUSED["seg_x"])
+    shift = O.bf16_to_f32(FUSED["seg_shift"])
+    scale_mod = O.bf16_to_f32(FUSED["seg_scale"])
+    S_seg = int(FUSED["seg_rows"])
+    rows = np.arange(x.shape[0]) // S_seg
+    s = O.mod_multiplier(scale_mod, False)[rows]
+    b = shift[rows]
+    q, scale, h, res, amax = O.rms_mod_res_tensorwise(x, None, s, b, 1e-6)
+    assert bf16_ulp_diff(h, FUSED["seg_h"]).max() <= 1
+    assert bf16_ulp_diff(res, FUSED["seg_res"]).max() <= 1
+    assert f32_ulp_diff(amax, FUSED["seg_amax"]).max() <= 2
+    q_given, _ = O.quant_tensorwise_given(O.bf16_to_f32(FUSED["seg_h"]), FUSED["seg_amax"][0])
+    np.testing.assert_array_equal(q_given, FUSED["seg_q"])
+    # the per-token path uses the same h definition
+    _, _, h_tok, res_tok = O.rms_mod_quant_per_token(x, shift, scale_mod, rows_per_mod=S_seg, eps=1e-6)
+    np.testing.assert_array_equal(h_tok, h)
+    np.testing.assert_array_equal(res_tok, res)
+
+
+@pytest.mark.parametrize("i", range(int(FUSED["n_swiglu"])))
+def test_swiglu_tensorwise_vs_reference(i):
+    p = f"s{i}_"
+    g = O.bf16_to_f32(FUSED[p + "gate"])
+    u = O.bf16_to_f32(FUSED[p + "up"])
+    q, scale, act, amax = O.swiglu_tensorwise(g, u)
+    assert bf16_ulp_diff(act, FUSED[p + "act"]).max() <= 1
+    assert f32_ulp_diff(scale, FUSED[p + "scale"]).max() <= 2
+    q_given = O.quantize_with_scale(O.bf16_to_f32(FUSED[p + "act"]), FUSED[p + "scale"][0], O.QUANT_FP8)
+    np.testing.assert_array_equal(q_given, FUSED[p + "q"])
+
+
+def test_rms_sum_squares_tree_matches_sequential_sum_closely():
+    rng = np.random.default_rng(3)
+    for D in (8, 100, 256, 3072, 5376, 12288, 30000):
+        x = O.round_bf16(rng.standard_normal((3, D)).astype(np.float32))
+        ss = O.rms_sum_squares(x)
+        ref = (x.astype(np.float64) ** 2).sum(axis=1)
+        assert np.all(np.abs(ss - ref) <= 1e-5 * ref)
+
+
+def test_row_threads_rule():
+    assert O.row_threads(3072) == 32
+    assert O.row_threads(12288) == 128
+    assert O.row_threads(8) == 32
+    assert O.row_threads(512 * 8 * 12) == 512
+    with pytest.raises(ValueError):
+        O.row_threads(512 * 8 * 12 + 8)
+
+
+def test_per_token_quant_properties():
+    rng = np.random.default_rng(4)
+    x = O.round_bf16(rng.standard_normal((16, 300)).astype(np.float32))
+    x[3] = 0.0
+    for kind in (O.QUANT_INT8, O.QUANT_FP8):
+        q, s = O.quant_rows(x, kind)
+        assert s[3] == np.float32(1e-12)
+        if kind == O.QUANT_INT8:
+            assert np.abs(q.astype(np.int32)).max() <= 127
+            # every non-zero row reaches +-127 at its amax element
+            assert np.all(np.abs(q[np.arange(16) != 3]).max(axis=1) == 127)
+        else:
+            deq = O.e4m3_to_f32(q)
+            assert np.all(np.abs(deq) <= 448)

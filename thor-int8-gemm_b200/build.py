@@ -1,0 +1,67 @@
+"""Build the C-ABI shared library libthor_int8_gemm_b200.so in place (sm_100a).
+
+    python thor-int8-gemm_b200/build.py [--force]
+
+nvcc cross-compiles for sm_100a on a machine without a GPU; the resulting .so
+sits next to this file and is what the Python layer loads.
+"""
+from __future__ import annotations
+
+import os
+import shutil
+import subprocess
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(HERE)
+CSRC = os.path.join(HERE, "csrc")
+LIB_NAME = "libthor_int8_gemm_b200.so"
+LIB_PATH = os.path.join(HERE, LIB_NAME)
+SOURCES = [os.path.join(CSRC, "t8g.cu")]
+DEPENDS = SOURCES + [os.path.join(CSRC, f) for f in sorted(os.listdir(CSRC)) if f.endswith(".cuh")] + [
+    os.path.join(ROOT, "include", "thor_int8_gemm_b200.h")]
+
+NVCC_FLAGS = [
+    "-gencode", "arch=compute_100a,code=sm_100a",
+    "-O3", "-lineinfo", "-std=c++17",
+    "-Xcompiler", "-fPIC", "-shared",
+    "-Xptxas", "-v",
+]
+
+
+def nvcc_path() -> str:
+    cand = [os.environ.get("NVCC"), shutil.which("nvcc"), "/usr/local/cuda/bin/nvcc"]
+    for c in cand:
+        if c and os.path.exists(c):
+            return c
+    raise RuntimeError("nvcc not found (set NVCC or put CUDA's bin on PATH)")
+
+
+def up_to_date() -> bool:
+    if not os.path.exists(LIB_PATH):
+        return False
+    t = os.path.getmtime(LIB_PATH)
+    return all(os.path.getmtime(p) <= t for p in DEPENDS if os.path.exists(p))
+
+
+def build(force: bool = False, verbose: bool = False) -> str:
+    """Compile the library if any source is newer than it; return its path."""
+    if not force and up_to_date():
+        return LIB_PATH
+    tmp = LIB_PATH + ".tmp"
+    cmd = [nvcc_path(), *NVCC_FLAGS, "-o", tmp, *SOURCES]
+    proc = subprocess.run(cmd, capture_output=True, text=True)
+    log_path = os.path.join(HERE, "build.log")
+    with open(log_path, "w") as f:
+        f.write(" ".join(cmd) + "\n" + proc.stdout + proc.stderr)
+    if proc.returncode != 0:
+        sys.stderr.write(proc.stdout + proc.stderr)
+        raise RuntimeError(f"nvcc failed ({proc.returncode}); see {log_path}")
+    os.replace(tmp, LIB_PATH)
+    if verbose:
+        sys.stdout.write(proc.stderr)
+    return LIB_PATH
+
+
+if __name__ == "__main__":
+    print(build(force="--force" in sys.argv, verbose=True))

@@ -1,0 +1,369 @@
+// Persistent, warp-specialised 8-bit GEMM with a fused dequantisation epilogue
+// for sm_100a (tcgen05 tensor cores, TMEM accumulators, TMA in and out).
+//
+//   out[m, n] = cast( ((f32(acc[m, n]) * xs[m]) * ws[n or 0]) + f32(bias[n]) )
+//   acc[m, n] = sum_k A[m, k] * W[n, k]        (int8 -> int32, or e4m3 -> f32)
+//
+// Replaces the Triton `_kernel` of src/ck_int8_patch_thor.py:67-106 (epilogue
+// :101-106) behind comfy-kitchen's `_C.cutlass_int8_dequant`; the float
+// operations are the reference's, in its order, each rounded separately.
+//
+// CTA layout (192 threads, one CTA per SM, persistent over output tiles):
+//   warp 0      TMA producer: A and W tiles -> 4-stage shared-memory ring
+//   warp 1      MMA issuer:   tcgen05.mma 128x256x32 into one of two TMEM
+//               accumulators (2 x 256 columns), commit frees smem stages
+//   warps 2..5  epilogue:     TMEM -> registers (tcgen05.ld), dequant, convert,
+//               swizzled smem staging, TMA store; releases the accumulator so
+//               the MMA of the next tile overlaps this tile's epilogue
+// Tiles are visited n-fastest, so the whole weight matrix of a DiT projection
+// (<= 75 MB) stays in L2 while activation row panels stream from HBM once.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "ptx.cuh"
+
+namespace t8g {
+namespace gemm {
+
+enum InKind : int { kInI8 = 0, kInE4M3 = 1 };
+enum OutKind : int { kOutBF16 = 0, kOutF16 = 1, kOutF32 = 2 };
+
+constexpr int BM = 128;          // tile rows (tokens)
+constexpr int BN = 256;          // tile columns (output channels)
+constexpr int BK = 128;          // K bytes per stage = one 128-byte swizzle row
+constexpr int MMA_K = 32;        // K of one tcgen05.mma for 8-bit operands
+constexpr int STAGES = 4;
+constexpr int A_BYTES = BM * BK;
+constexpr int B_BYTES = BN * BK;
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int EPI_WARPS = 4;
+constexpr int EPI_COLS = 32;               // columns per epilogue chunk
+constexpr int EPI_BUF_BYTES = 32 * 128;    // 32 rows x (32 cols x <= 4 bytes)
+constexpr int NUM_THREADS = 64 + 32 * EPI_WARPS;
+constexpr uint32_t TMEM_COLS = 2 * BN;     // double-buffered accumulator
+
+struct Smem {
+  uint8_t a[STAGES][A_BYTES];
+  uint8_t b[STAGES][B_BYTES];
+  uint8_t epi[EPI_WARPS][2][EPI_BUF_BYTES];
+  uint64_t full[STAGES];
+  uint64_t empty[STAGES];
+  uint64_t tmem_full[2];
+  uint64_t tmem_empty[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+};
+constexpr size_t SMEM_BYTES = sizeof(Smem) + 1024;   // + slack to align the base to 1024 B
+
+struct Args {
+  const float* xs;    // [M] per-token activation scale
+  const float* ws;    // [N] per-channel weight scale, or [1]
+  const void* bias;   // [N] in the output type, or nullptr
+  int ws_stride;      // 1: per channel, 0: one scalar
+  int vec_ok;         // ws and bias are 16-byte aligned
+  int M, N, K;
+};
+
+template <int OUT>
+struct OutTraits;
+template <>
+struct OutTraits<kOutBF16> {
+  static constexpr int kBytes = 2;
+  __device__ static float to_f32(const void* p, int i) {
+    return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
+  }
+  __device__ static uint32_t pack2(float lo, float hi) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+  }
+};
+template <>
+struct OutTraits<kOutF16> {
+  static constexpr int kBytes = 2;
+  __device__ static float to_f32(const void* p, int i) {
+    return __half2float(reinterpret_cast<const __half*>(p)[i]);
+  }
+  __device__ static uint32_t pack2(float lo, float hi) {
+    __half2 v = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+  }
+};
+template <>
+struct OutTraits<kOutF32> {
+  static constexpr int kBytes = 4;
+  __device__ static float to_f32(const void* p, int i) { return reinterpret_cast<const float*>(p)[i]; }
+};
+
+// Load 32 consecutive per-channel weight scales and biases for columns [n0, n0+32).
+template <int OUT>
+__device__ __forceinline__ void load_channel_params(const Args& a, int n0, float (&wsv)[32], float (&bv)[32]) {
+  const bool full = n0 + 32 <= a.N;
+  if (a.ws_stride == 0) {
+    const float w0 = __ldg(a.ws);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) wsv[j] = w0;
+  } else if (full && a.vec_ok) {
+    const float4* p = reinterpret_cast<const float4*>(a.ws + n0);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const float4 t = __ldg(p + q);
+      wsv[4 * q + 0] = t.x;
+      wsv[4 * q + 1] = t.y;
+      wsv[4 * q + 2] = t.z;
+      wsv[4 * q + 3] = t.w;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) wsv[j] = (n0 + j < a.N) ? __ldg(a.ws + n0 + j) : 0.f;
+  }
+  if (a.bias == nullptr) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) bv[j] = 0.f;
+  } else if (full && a.vec_ok) {
+    if constexpr (OutTraits<OUT>::kBytes == 2) {
+      const uint4* p = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(a.bias) + n0);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint4 t = __ldg(p + q);
+        const uint32_t w[4] = {t.x, t.y, t.z, t.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const uint16_t lo = static_cast<uint16_t>(w[e] & 0xFFFFu), hi = static_cast<uint16_t>(w[e] >> 16);
+          bv[8 * q + 2 * e + 0] = OutTraits<OUT>::to_f32(&lo, 0);
+          bv[8 * q + 2 * e + 1] = OutTraits<OUT>::to_f32(&hi, 0);
+        }
+      }
+    } else {
+      const float4* p = reinterpret_cast<const float4*>(static_cast<const float*>(a.bias) + n0);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float4 t = __ldg(p + q);
+        bv[4 * q + 0] = t.x;
+        bv[4 * q + 1] = t.y;
+        bv[4 * q + 2] = t.z;
+        bv[4 * q + 3] = t.w;
+      }
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) bv[j] = (n0 + j < a.N) ? OutTraits<OUT>::to_f32(a.bias, n0 + j) : 0.f;
+  }
+}
+
+template <int IN, int OUT>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    gemm_dequant_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+                        const __grid_constant__ CUtensorMap tm_out, const Args args) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
+  Smem& s = *reinterpret_cast<Smem*>(smem_raw + pad);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int tiles_n = (args.N + BN - 1) / BN;
+  const int tiles_m = (args.M + BM - 1) / BM;
+  const int num_tiles = tiles_m * tiles_n;
+  const int kblocks = (args.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int i = 0; i < STAGES; ++i) {
+      mbar_init(&s.full[i], 1);
+      mbar_init(&s.empty[i], 1);
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s.tmem_full[i], 1);
+      mbar_init(&s.tmem_empty[i], EPI_WARPS);
+    }
+    mbar_init(&s.drain, 1);
+    fence_mbarrier_init();
+    prefetch_tensormap(&tm_a);
+    prefetch_tensormap(&tm_b);
+    prefetch_tensormap(&tm_out);
+  }
+  if (warp == 1) {
+    tmem_alloc(&s.tmem_base, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = s.tmem_base;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      const uint64_t pol_a = policy_evict_first();
+      const uint64_t pol_b = policy_evict_last();
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+        const int tm = tile / tiles_n;
+        const int tn = tile - tm * tiles_n;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&s.empty[stage], phase ^ 1u, kStatusTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&s.full[stage], STAGE_BYTES);
+          tma_load_2d(s.a[stage], &tm_a, &s.full[stage], kb * BK, tm * BM, pol_a);
+          tma_load_2d(s.b[stage], &tm_b, &s.full[stage], kb * BK, tn * BN, pol_b);
+          ++issued;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // Every issued copy must land before the CTA may exit.
+      for (int i = 0; i < STAGES && i < issued; ++i) {
+        const int n = issued - 1 - i;
+        if (!mbar_wait(&s.full[n % STAGES], static_cast<uint32_t>((n / STAGES) & 1), kStatusTimeoutDrain)) break;
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = (IN == kInI8) ? make_idesc(2, 1, 1, BM, BN)   // s32 <- s8 x s8
+                                               : make_idesc(1, 0, 0, BM, BN);  // f32 <- e4m3 x e4m3
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true, any = false;
+      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = static_cast<uint32_t>((local >> 1) & 1);
+        if (!mbar_wait(&s.tmem_empty[acc], acc_phase ^ 1u, kStatusTimeoutMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&s.full[stage], phase, kStatusTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(s.a[stage]);
+          const uint32_t b0 = smem_u32(s.b[stage]);
+#pragma unroll
+          for (int k = 0; k < BK / MMA_K; ++k) {
+            const uint64_t ad = smem_desc_k_sw128(a0 + k * MMA_K);
+            const uint64_t bd = smem_desc_k_sw128(b0 + k * MMA_K);
+            const uint32_t accumulate = (kb | k) != 0 ? 1u : 0u;
+            if constexpr (IN == kInI8)
+              mma_i8(d_tmem, ad, bd, idesc, accumulate);
+            else
+              mma_f8(d_tmem, ad, bd, idesc, accumulate);
+          }
+          tc_commit(&s.empty[stage]);
+          any = true;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        tc_commit(&s.tmem_full[acc]);
+      }
+      if (any) {
+        // All MMAs (and their shared-memory reads) complete before teardown.
+        tc_commit(&s.drain);
+        mbar_wait(&s.drain, 0, kStatusTimeoutDrain);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int ew = warp - 2;           // staging slot of this warp
+    const int quarter = warp & 3;      // TMEM lanes [32*quarter, 32*quarter+32) are readable by this warp
+    int local = 0;
+    int ebuf = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+      const int tm = tile / tiles_n;
+      const int tn = tile - tm * tiles_n;
+      const int acc = local & 1;
+      const uint32_t acc_phase = static_cast<uint32_t>((local >> 1) & 1);
+      if (!mbar_wait(&s.tmem_full[acc], acc_phase, kStatusTimeoutEpilogue)) break;
+      tc_fence_after();
+      const int row0 = tm * BM + quarter * 32;
+      if (row0 < args.M) {
+        const int row = row0 + lane;
+        const float xs_r = row < args.M ? __ldg(args.xs + row) : 0.f;
+        const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
+        const int n_tile0 = tn * BN;
+        const int nchunks = min(BN / EPI_COLS, (args.N - n_tile0 + EPI_COLS - 1) / EPI_COLS);
+        for (int c = 0; c < nchunks; ++c) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(c * EPI_COLS), r);
+          tmem_ld_wait();
+          const int n0 = n_tile0 + c * EPI_COLS;
+          float wsv[32], bv[32];
+          load_channel_params<OUT>(args, n0, wsv, bv);
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            float f = (IN == kInI8) ? __int2float_rn(static_cast<int>(r[j])) : __uint_as_float(r[j]);
+            f = __fmul_rn(f, xs_r);
+            f = __fmul_rn(f, wsv[j]);
+            if (args.bias != nullptr) f = __fadd_rn(f, bv[j]);
+            v[j] = f;
+          }
+          // the staging buffer used two chunks ago must have been read by its TMA store
+          if (lane == 0) bulk_wait_group_read<1>();
+          __syncwarp();
+          uint8_t* buf = s.epi[ew][ebuf];
+          if constexpr (OutTraits<OUT>::kBytes == 2) {
+            // 32 rows x 64 B, 64-byte swizzle: 16-byte chunk q of row r lives at chunk q ^ ((r >> 1) & 3)
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              uint4 w;
+              w.x = OutTraits<OUT>::pack2(v[8 * q + 0], v[8 * q + 1]);
+              w.y = OutTraits<OUT>::pack2(v[8 * q + 2], v[8 * q + 3]);
+              w.z = OutTraits<OUT>::pack2(v[8 * q + 4], v[8 * q + 5]);
+              w.w = OutTraits<OUT>::pack2(v[8 * q + 6], v[8 * q + 7]);
+              const int pq = q ^ ((lane >> 1) & 3);
+              *reinterpret_cast<uint4*>(buf + lane * 64 + pq * 16) = w;
+            }
+          } else {
+            // 32 rows x 128 B, 128-byte swizzle: chunk q of row r lives at chunk q ^ (r & 7)
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              const float4 w = make_float4(v[4 * q + 0], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+              const int pq = q ^ (lane & 7);
+              *reinterpret_cast<float4*>(buf + lane * 128 + pq * 16) = w;
+            }
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tm_out, buf, n0, row0);
+            bulk_commit_group();
+          }
+          ebuf ^= 1;
+        }
+      }
+      // hand the accumulator back to the MMA warp
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s.tmem_empty[acc]);
+    }
+    if (lane == 0) bulk_wait_group_all();
+    __syncwarp();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+}  // namespace gemm
+}  // namespace t8g

@@ -1,0 +1,499 @@
+// C ABI of the B200 quantized linear-layer path (declared in include/thor_int8_gemm_b200.h).
+//
+// Host side only: argument validation, TMA tensor-map encoding, launch shapes.
+// Single translation unit: the kernels live in the included headers.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdarg.h>
+#include <stdint.h>
+#include <stdio.h>
+
+#include <mutex>
+
+#include "../../include/thor_int8_gemm_b200.h"
+#include "gemm.cuh"
+#include "ptx.cuh"
+#include "rows.cuh"
+
+namespace {
+
+thread_local char g_last_error[512] = "";
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(T8G_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+#define T8G_CHECK_CUDA(expr, what)           \
+  do {                                       \
+    cudaError_t e_ = (expr);                 \
+    if (e_ != cudaSuccess) return cuda_fail(e_, what); \
+  } while (0)
+
+// ----------------------------------------------------------------- devices
+struct DeviceInfo {
+  bool known = false;
+  int sms = 0;
+  int major = 0, minor = 0;
+};
+constexpr int kMaxDevices = 64;
+DeviceInfo g_dev[kMaxDevices];
+std::mutex g_dev_mu;
+
+int current_device(int* dev, DeviceInfo* info) {
+  T8G_CHECK_CUDA(cudaGetDevice(dev), "cudaGetDevice");
+  if (*dev < 0 || *dev >= kMaxDevices) return fail(T8G_ERR_UNSUPPORTED, "device ordinal %d out of range", *dev);
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  DeviceInfo& d = g_dev[*dev];
+  if (!d.known) {
+    T8G_CHECK_CUDA(cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, *dev), "cudaDeviceGetAttribute");
+    T8G_CHECK_CUDA(cudaDeviceGetAttribute(&d.major, cudaDevAttrComputeCapabilityMajor, *dev), "cudaDeviceGetAttribute");
+    T8G_CHECK_CUDA(cudaDeviceGetAttribute(&d.minor, cudaDevAttrComputeCapabilityMinor, *dev), "cudaDeviceGetAttribute");
+    d.known = true;
+  }
+  *info = d;
+  if (d.major != 10 || d.minor != 0)
+    return fail(T8G_ERR_UNSUPPORTED, "device %d is sm_%d%d; this library is built for sm_100a (B200) only", *dev,
+                d.major, d.minor);
+  return T8G_OK;
+}
+
+// Sets the dynamic shared-memory limit of `fn` once per device.
+template <typename F>
+int ensure_smem_attr(F fn, int dev, size_t bytes, bool* done_per_device) {
+  if (done_per_device[dev]) return T8G_OK;
+  T8G_CHECK_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes)),
+                 "cudaFuncSetAttribute");
+  done_per_device[dev] = true;
+  return T8G_OK;
+}
+
+// ----------------------------------------------------------------- tensor maps
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// 2-D row-major tensor [outer, inner] with row pitch `ld_bytes`, box [box_outer, box_inner].
+int encode_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t outer,
+              uint64_t ld_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle sw) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(T8G_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {ld_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(T8G_ERR_CUDA, "cuTensorMapEncodeTiled failed (CUresult %d)", static_cast<int>(r));
+  return T8G_OK;
+}
+
+bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+
+// ----------------------------------------------------------------- GEMM
+template <int IN, int OUT>
+int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to, const t8g::gemm::Args& args,
+                int dev, int sms, cudaStream_t stream) {
+  using namespace t8g::gemm;
+  static bool attr_done[kMaxDevices] = {};
+  auto kern = gemm_dequant_kernel<IN, OUT>;
+  int rc = ensure_smem_attr(kern, dev, SMEM_BYTES, attr_done);
+  if (rc) return rc;
+  const int64_t tiles = static_cast<int64_t>((args.M + BM - 1) / BM) * ((args.N + BN - 1) / BN);
+  const int grid = static_cast<int>(tiles < sms ? tiles : sms);
+  kern<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(ta, tb, to, args);
+  T8G_CHECK_CUDA(cudaGetLastError(), "gemm launch");
+  return T8G_OK;
+}
+
+int gemm_entry(int in_kind, const void* x, const void* w, const float* x_scale, const float* w_scale,
+               int64_t w_scale_numel, const void* bias, int64_t bias_numel, void* out, int out_dtype, int64_t M,
+               int64_t N, int64_t K, int64_t ld_x, int64_t ld_w, int64_t ld_out, void* stream_) {
+  using namespace t8g::gemm;
+  g_last_error[0] = '\0';
+  if (M < 0 || N < 0 || K < 1) return fail(T8G_ERR_INVALID_ARGUMENT, "bad sizes M=%lld N=%lld K=%lld", (long long)M, (long long)N, (long long)K);
+  if (M >= (int64_t(1) << 31) || N >= (int64_t(1) << 31) || K >= (int64_t(1) << 31))
+    return fail(T8G_ERR_UNSUPPORTED, "M, N and K must each be below 2^31");
+  if (out_dtype < T8G_OUT_BF16 || out_dtype > T8G_OUT_F32) return fail(T8G_ERR_INVALID_ARGUMENT, "unknown out_dtype %d", out_dtype);
+  if (M == 0 || N == 0) return T8G_OK;
+  if (!x || !w || !x_scale || !w_scale || !out) return fail(T8G_ERR_INVALID_ARGUMENT, "null operand pointer");
+  if (w_scale_numel != 1 && w_scale_numel != N)
+    return fail(T8G_ERR_INVALID_ARGUMENT, "w_scale numel %lld is neither 1 nor N=%lld", (long long)w_scale_numel, (long long)N);
+  if (bias_numel != 0 && bias_numel != N)
+    return fail(T8G_ERR_INVALID_ARGUMENT, "bias numel %lld is neither 0 nor N=%lld", (long long)bias_numel, (long long)N);
+  if (bias_numel == N && !bias) return fail(T8G_ERR_INVALID_ARGUMENT, "bias numel is N but bias is null");
+  const int esz = out_dtype == T8G_OUT_F32 ? 4 : 2;
+  if (ld_x < K || ld_w < K || ld_out < N) return fail(T8G_ERR_INVALID_ARGUMENT, "row stride smaller than the row");
+  if (ld_x % 16 || ld_w % 16 || (ld_out * esz) % 16)
+    return fail(T8G_ERR_INVALID_ARGUMENT, "row strides must be multiples of 16 bytes (ld_x=%lld ld_w=%lld ld_out=%lld)",
+                (long long)ld_x, (long long)ld_w, (long long)ld_out);
+  if (!aligned(x, 16) || !aligned(w, 16) || !aligned(out, 16))
+    return fail(T8G_ERR_INVALID_ARGUMENT, "x, w and out must be 16-byte aligned");
+  if (!aligned(x_scale, 4) || !aligned(w_scale, 4)) return fail(T8G_ERR_INVALID_ARGUMENT, "scales must be 4-byte aligned");
+
+  int dev;
+  DeviceInfo info;
+  int rc = current_device(&dev, &info);
+  if (rc) return rc;
+
+  const CUtensorMapDataType in_dt = CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  CUtensorMap ta, tb, to;
+  rc = encode_2d(&ta, in_dt, x, K, M, ld_x, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  rc = encode_2d(&tb, in_dt, w, K, N, ld_w, BK, BN, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  const CUtensorMapDataType out_dt = out_dtype == T8G_OUT_BF16  ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                     : out_dtype == T8G_OUT_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                                : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  rc = encode_2d(&to, out_dt, out, N, M, ld_out * esz, EPI_COLS, 32,
+                 esz == 2 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+
+  Args args;
+  args.xs = x_scale;
+  args.ws = w_scale;
+  args.bias = bias_numel ? bias : nullptr;
+  args.ws_stride = w_scale_numel == 1 ? 0 : 1;
+  args.vec_ok = aligned(w_scale, 16) && (bias_numel == 0 || aligned(bias, 16));
+  args.M = static_cast<int>(M);
+  args.N = static_cast<int>(N);
+  args.K = static_cast<int>(K);
+  cudaStream_t st = static_cast<cudaStream_t>(stream_);
+  if (in_kind == kInI8) {
+    switch (out_dtype) {
+      case T8G_OUT_BF16: return launch_gemm<kInI8, kOutBF16>(ta, tb, to, args, dev, info.sms, st);
+      case T8G_OUT_F16: return launch_gemm<kInI8, kOutF16>(ta, tb, to, args, dev, info.sms, st);
+      default: return launch_gemm<kInI8, kOutF32>(ta, tb, to, args, dev, info.sms, st);
+    }
+  }
+  switch (out_dtype) {
+    case T8G_OUT_BF16: return launch_gemm<kInE4M3, kOutBF16>(ta, tb, to, args, dev, info.sms, st);
+    case T8G_OUT_F16: return launch_gemm<kInE4M3, kOutF16>(ta, tb, to, args, dev, info.sms, st);
+    default: return launch_gemm<kInE4M3, kOutF32>(ta, tb, to, args, dev, info.sms, st);
+  }
+}
+
+// ----------------------------------------------------------------- row kernels
+// Threads per row: the smallest power of two in [32, 512] with at most MAX_VEC
+// 16-byte vectors per thread (the oracle restates this rule).
+int row_threads(int64_t D) {
+  const int64_t nvec = (D + 7) / 8;
+  int t = 32;
+  while (t < 512 && (nvec + t - 1) / t > t8g::rows::MAX_VEC) t *= 2;
+  return (nvec + t - 1) / t > t8g::rows::MAX_VEC ? -1 : t;
+}
+
+int check_row_shape(const char* what, int64_t S, int64_t D, int quant_kind) {
+  if (S < 0 || D < 0) return fail(T8G_ERR_INVALID_ARGUMENT, "%s: negative size", what);
+  if (D % 8) return fail(T8G_ERR_INVALID_ARGUMENT, "%s: row length %lld is not a multiple of 8", what, (long long)D);
+  if (row_threads(D) < 0) return fail(T8G_ERR_UNSUPPORTED, "%s: row length %lld exceeds 49152", what, (long long)D);
+  if (quant_kind != T8G_QUANT_INT8 && quant_kind != T8G_QUANT_FP8_E4M3)
+    return fail(T8G_ERR_INVALID_ARGUMENT, "%s: unknown quant_kind %d", what, quant_kind);
+  if (S >= (int64_t(1) << 40)) return fail(T8G_ERR_UNSUPPORTED, "%s: too many rows", what);
+  return T8G_OK;
+}
+
+int check_bf16_matrix(const char* what, const void* p, int64_t ld, int64_t D, bool required) {
+  if (!p) return required ? fail(T8G_ERR_INVALID_ARGUMENT, "%s is null", what) : T8G_OK;
+  if (!aligned(p, 16)) return fail(T8G_ERR_INVALID_ARGUMENT, "%s must be 16-byte aligned", what);
+  if (ld < D || ld % 8) return fail(T8G_ERR_INVALID_ARGUMENT, "%s row stride %lld must be >= D and a multiple of 8", what, (long long)ld);
+  return T8G_OK;
+}
+
+int check_q(const void* q, int64_t ld_q, int64_t D) {
+  if (!q) return fail(T8G_ERR_INVALID_ARGUMENT, "q is null");
+  if (!aligned(q, 8)) return fail(T8G_ERR_INVALID_ARGUMENT, "q must be 8-byte aligned");
+  if (ld_q < D || ld_q % 8) return fail(T8G_ERR_INVALID_ARGUMENT, "q row stride must be >= D and a multiple of 8");
+  return T8G_OK;
+}
+
+template <int T>
+unsigned row_grid(int64_t S) {
+  return static_cast<unsigned>((S + t8g::rows::Geo<T>::kRows - 1) / t8g::rows::Geo<T>::kRows);
+}
+
+#define T8G_DISPATCH_T(t, CALL)                 \
+  switch (t) {                                  \
+    case 32: { constexpr int T = 32; CALL; break; }   \
+    case 64: { constexpr int T = 64; CALL; break; }   \
+    case 128: { constexpr int T = 128; CALL; break; } \
+    case 256: { constexpr int T = 256; CALL; break; } \
+    default: { constexpr int T = 512; CALL; break; }  \
+  }
+
+int launch_checked(const char* what) {
+  T8G_CHECK_CUDA(cudaGetLastError(), what);
+  return T8G_OK;
+}
+
+int rms_common(bool tensorwise, const void* x, int64_t ld_x, const void* w, const void* shift, const void* scale,
+               int64_t ld_mod, const int32_t* mod_index, int64_t rows_per_mod, int scale_is_multiplier, float eps,
+               void* q, int64_t ld_q, float* q_scale, void* h, int64_t ld_h, void* res, int64_t ld_res,
+               float* amax, float* scale_out, int64_t S, int64_t D, int quant_kind, void* stream_) {
+  using namespace t8g::rows;
+  g_last_error[0] = '\0';
+  int rc = check_row_shape("rms_mod_quant", S, D, quant_kind);
+  if (rc) return rc;
+  if (S == 0 || D == 0) return T8G_OK;
+  if ((rc = check_bf16_matrix("x", x, ld_x, D, true))) return rc;
+  if ((rc = check_bf16_matrix("shift", shift, ld_mod, D, true))) return rc;
+  if ((rc = check_bf16_matrix("scale", scale, ld_mod, D, true))) return rc;
+  if (w && !aligned(w, 16)) return fail(T8G_ERR_INVALID_ARGUMENT, "w must be 16-byte aligned");
+  if ((rc = check_bf16_matrix("h", h, ld_h, D, tensorwise))) return rc;
+  if ((rc = check_bf16_matrix("res", res, ld_res, D, false))) return rc;
+  if ((rc = check_q(q, ld_q, D))) return rc;
+  if (!mod_index && rows_per_mod < 1) return fail(T8G_ERR_INVALID_ARGUMENT, "rows_per_mod must be >= 1 without mod_index");
+  if (tensorwise) {
+    if (!amax) return fail(T8G_ERR_INVALID_ARGUMENT, "amax scratch word is null");
+    if (quant_kind != T8G_QUANT_FP8_E4M3 && quant_kind != T8G_QUANT_INT8) return fail(T8G_ERR_INVALID_ARGUMENT, "quant_kind");
+  } else if (!q_scale) {
+    return fail(T8G_ERR_INVALID_ARGUMENT, "q_scale is null");
+  }
+  int dev;
+  DeviceInfo info;
+  if ((rc = current_device(&dev, &info))) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream_);
+
+  RmsArgs a;
+  a.x = static_cast<const __nv_bfloat16*>(x);
+  a.ld_x = ld_x;
+  a.w = static_cast<const __nv_bfloat16*>(w);
+  a.shift = static_cast<const __nv_bfloat16*>(shift);
+  a.scale = static_cast<const __nv_bfloat16*>(scale);
+  a.ld_mod = ld_mod;
+  a.mod_index = mod_index;
+  a.rows_per_mod = rows_per_mod < 1 ? 1 : rows_per_mod;
+  a.scale_is_multiplier = scale_is_multiplier;
+  a.eps = eps;
+  a.q = q;
+  a.ld_q = ld_q;
+  a.q_scale = q_scale;
+  a.h = static_cast<__nv_bfloat16*>(h);
+  a.ld_h = ld_h;
+  a.res = static_cast<__nv_bfloat16*>(res);
+  a.ld_res = ld_res;
+  a.amax = amax;
+  a.S = S;
+  a.D = static_cast<int>(D);
+  const int t = row_threads(D);
+  if (tensorwise) {
+    T8G_CHECK_CUDA(cudaMemsetAsync(amax, 0, sizeof(float), st), "cudaMemsetAsync(amax)");
+    T8G_DISPATCH_T(t, (rms_mod_kernel<T, 2><<<row_grid<T>(S), Geo<T>::kBlock, 0, st>>>(a)));
+    if ((rc = launch_checked("rms_mod phase A launch"))) return rc;
+    QuantGivenArgs b;
+    b.h = a.h;
+    b.ld_h = ld_h;
+    b.q = q;
+    b.ld_q = ld_q;
+    b.amax = amax;
+    b.scale_out = scale_out;
+    b.S = S;
+    b.D = a.D;
+    const int64_t vecs = S * (D / 8);
+    const int64_t want = (vecs + 255) / 256;
+    const unsigned grid = static_cast<unsigned>(want < int64_t(info.sms) * 16 ? want : int64_t(info.sms) * 16);
+    if (quant_kind == T8G_QUANT_FP8_E4M3)
+      quant_given_amax_kernel<kQuantFp8><<<grid, 256, 0, st>>>(b);
+    else
+      quant_given_amax_kernel<kQuantInt8><<<grid, 256, 0, st>>>(b);
+    return launch_checked("quant phase B launch");
+  }
+  if (quant_kind == T8G_QUANT_FP8_E4M3) {
+    T8G_DISPATCH_T(t, (rms_mod_kernel<T, kQuantFp8><<<row_grid<T>(S), Geo<T>::kBlock, 0, st>>>(a)));
+  } else {
+    T8G_DISPATCH_T(t, (rms_mod_kernel<T, kQuantInt8><<<row_grid<T>(S), Geo<T>::kBlock, 0, st>>>(a)));
+  }
+  return launch_checked("rms_mod_quant launch");
+}
+
+int swiglu_common(bool tensorwise, const void* gate, const void* up, int64_t ld_in, void* q, int64_t ld_q,
+                  float* q_scale, void* act, int64_t ld_act, float* amax, float* scale_out, int64_t M, int64_t F,
+                  int quant_kind, void* stream_) {
+  using namespace t8g::rows;
+  g_last_error[0] = '\0';
+  int rc = check_row_shape("swiglu_quant", M, F, quant_kind);
+  if (rc) return rc;
+  if (M == 0 || F == 0) return T8G_OK;
+  if ((rc = check_bf16_matrix("gate", gate, ld_in, F, true))) return rc;
+  if ((rc = check_bf16_matrix("up", up, ld_in, F, true))) return rc;
+  if ((rc = check_bf16_matrix("act", act, ld_act, F, tensorwise))) return rc;
+  if ((rc = check_q(q, ld_q, F))) return rc;
+  if (tensorwise && !amax) return fail(T8G_ERR_INVALID_ARGUMENT, "amax scratch word is null");
+  if (!tensorwise && !q_scale) return fail(T8G_ERR_INVALID_ARGUMENT, "q_scale is null");
+  int dev;
+  DeviceInfo info;
+  if ((rc = current_device(&dev, &info))) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream_);
+  SwigluArgs a;
+  a.gate = static_cast<const __nv_bfloat16*>(gate);
+  a.up = static_cast<const __nv_bfloat16*>(up);
+  a.ld_in = ld_in;
+  a.q = q;
+  a.ld_q = ld_q;
+  a.q_scale = q_scale;
+  a.act = static_cast<__nv_bfloat16*>(act);
+  a.ld_act = ld_act;
+  a.amax = amax;
+  a.M = M;
+  a.F = static_cast<int>(F);
+  const int t = row_threads(F);
+  if (tensorwise) {
+    T8G_CHECK_CUDA(cudaMemsetAsync(amax, 0, sizeof(float), st), "cudaMemsetAsync(amax)");
+    T8G_DISPATCH_T(t, (swiglu_kernel<T, 2><<<row_grid<T>(M), Geo<T>::kBlock, 0, st>>>(a)));
+    if ((rc = launch_checked("swiglu phase A launch"))) return rc;
+    QuantGivenArgs b;
+    b.h = a.act;
+    b.ld_h = ld_act;
+    b.q = q;
+    b.ld_q = ld_q;
+    b.amax = amax;
+    b.scale_out = scale_out;
+    b.S = M;
+    b.D = a.F;
+    const int64_t vecs = M * (F / 8);
+    const int64_t want = (vecs + 255) / 256;
+    const unsigned grid = static_cast<unsigned>(want < int64_t(info.sms) * 16 ? want : int64_t(info.sms) * 16);
+    if (quant_kind == T8G_QUANT_FP8_E4M3)
+      quant_given_amax_kernel<kQuantFp8><<<grid, 256, 0, st>>>(b);
+    else
+      quant_given_amax_kernel<kQuantInt8><<<grid, 256, 0, st>>>(b);
+    return launch_checked("quant phase B launch");
+  }
+  if (quant_kind == T8G_QUANT_FP8_E4M3) {
+    T8G_DISPATCH_T(t, (swiglu_kernel<T, kQuantFp8><<<row_grid<T>(M), Geo<T>::kBlock, 0, st>>>(a)));
+  } else {
+    T8G_DISPATCH_T(t, (swiglu_kernel<T, kQuantInt8><<<row_grid<T>(M), Geo<T>::kBlock, 0, st>>>(a)));
+  }
+  return launch_checked("swiglu_quant launch");
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* t8g_version(void) { return "0.1.0"; }
+
+const char* t8g_last_error(void) { return g_last_error; }
+
+int t8g_device_status(void* stream, int* status) {
+  g_last_error[0] = '\0';
+  if (!status) return fail(T8G_ERR_INVALID_ARGUMENT, "status is null");
+  T8G_CHECK_CUDA(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)), "cudaStreamSynchronize");
+  int v = 0;
+  T8G_CHECK_CUDA(cudaMemcpyFromSymbol(&v, t8g::g_device_status, sizeof(int)), "cudaMemcpyFromSymbol");
+  if (v != 0) {
+    const int zero = 0;
+    T8G_CHECK_CUDA(cudaMemcpyToSymbol(t8g::g_device_status, &zero, sizeof(int)), "cudaMemcpyToSymbol");
+  }
+  *status = v;
+  return T8G_OK;
+}
+
+int t8g_gemm_i8_dequant(const void* x, const void* w, const float* x_scale, const float* w_scale,
+                        int64_t w_scale_numel, const void* bias, int64_t bias_numel, void* out, int out_dtype,
+                        int64_t M, int64_t N, int64_t K, int64_t ld_x, int64_t ld_w, int64_t ld_out, void* stream) {
+  return gemm_entry(t8g::gemm::kInI8, x, w, x_scale, w_scale, w_scale_numel, bias, bias_numel, out, out_dtype, M, N,
+                    K, ld_x, ld_w, ld_out, stream);
+}
+
+int t8g_gemm_fp8_dequant(const void* x, const void* w, const float* x_scale, const float* w_scale,
+                         int64_t w_scale_numel, const void* bias, int64_t bias_numel, void* out, int out_dtype,
+                         int64_t M, int64_t N, int64_t K, int64_t ld_x, int64_t ld_w, int64_t ld_out, void* stream) {
+  return gemm_entry(t8g::gemm::kInE4M3, x, w, x_scale, w_scale, w_scale_numel, bias, bias_numel, out, out_dtype, M,
+                    N, K, ld_x, ld_w, ld_out, stream);
+}
+
+int t8g_quant_rows(const void* x, int64_t ld_x, void* q, int64_t ld_q, float* q_scale, int64_t S, int64_t D,
+                   int quant_kind, void* stream) {
+  using namespace t8g::rows;
+  g_last_error[0] = '\0';
+  int rc = check_row_shape("quant_rows", S, D, quant_kind);
+  if (rc) return rc;
+  if (S == 0 || D == 0) return T8G_OK;
+  if ((rc = check_bf16_matrix("x", x, ld_x, D, true))) return rc;
+  if ((rc = check_q(q, ld_q, D))) return rc;
+  if (!q_scale) return fail(T8G_ERR_INVALID_ARGUMENT, "q_scale is null");
+  int dev;
+  DeviceInfo info;
+  if ((rc = current_device(&dev, &info))) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  QuantRowsArgs a;
+  a.x = static_cast<const __nv_bfloat16*>(x);
+  a.ld_x = ld_x;
+  a.q = q;
+  a.ld_q = ld_q;
+  a.q_scale = q_scale;
+  a.S = S;
+  a.D = static_cast<int>(D);
+  const int t = row_threads(D);
+  if (quant_kind == T8G_QUANT_FP8_E4M3) {
+    T8G_DISPATCH_T(t, (quant_rows_kernel<T, kQuantFp8><<<row_grid<T>(S), Geo<T>::kBlock, 0, st>>>(a)));
+  } else {
+    T8G_DISPATCH_T(t, (quant_rows_kernel<T, kQuantInt8><<<row_grid<T>(S), Geo<T>::kBlock, 0, st>>>(a)));
+  }
+  return launch_checked("quant_rows launch");
+}
+
+int t8g_rms_mod_quant(const void* x, int64_t ld_x, const void* w, const void* shift, const void* scale,
+                      int64_t ld_mod, const int32_t* mod_index, int64_t rows_per_mod, int scale_is_multiplier,
+                      float eps, void* q, int64_t ld_q, float* q_scale, void* h, int64_t ld_h, void* res,
+                      int64_t ld_res, int64_t S, int64_t D, int quant_kind, void* stream) {
+  return rms_common(false, x, ld_x, w, shift, scale, ld_mod, mod_index, rows_per_mod, scale_is_multiplier, eps, q,
+                    ld_q, q_scale, h, ld_h, res, ld_res, nullptr, nullptr, S, D, quant_kind, stream);
+}
+
+int t8g_rms_mod_quant_tensorwise(const void* x, int64_t ld_x, const void* w, const void* shift,
+                                 const void* scale, int64_t ld_mod, const int32_t* mod_index,
+                                 int64_t rows_per_mod, int scale_is_multiplier, float eps, void* q,
+                                 int64_t ld_q, void* h, int64_t ld_h, void* res, int64_t ld_res, float* amax,
+                                 float* scale_out, int64_t S, int64_t D, int quant_kind, void* stream) {
+  return rms_common(true, x, ld_x, w, shift, scale, ld_mod, mod_index, rows_per_mod, scale_is_multiplier, eps, q,
+                    ld_q, nullptr, h, ld_h, res, ld_res, amax, scale_out, S, D, quant_kind, stream);
+}
+
+int t8g_swiglu_quant(const void* gate, const void* up, int64_t ld_in, void* q, int64_t ld_q, float* q_scale,
+                     void* act, int64_t ld_act, int64_t M, int64_t F, int quant_kind, void* stream) {
+  return swiglu_common(false, gate, up, ld_in, q, ld_q, q_scale, act, ld_act, nullptr, nullptr, M, F, quant_kind,
+                       stream);
+}
+
+int t8g_swiglu_quant_tensorwise(const void* gate, const void* up, int64_t ld_in, void* q, int64_t ld_q,
+                                void* act, int64_t ld_act, float* amax, float* scale_out, int64_t M, int64_t F,
+                                int quant_kind, void* stream) {
+  return swiglu_common(true, gate, up, ld_in, q, ld_q, nullptr, act, ld_act, amax, scale_out, M, F, quant_kind,
+                       stream);
+}
+
+int t8g_wait_selftest(uint64_t limit_ns, int* gave_up, void* stream) {
+  g_last_error[0] = '\0';
+  if (!gave_up) return fail(T8G_ERR_INVALID_ARGUMENT, "gave_up is null");
+  if (limit_ns > 2000000000ull) return fail(T8G_ERR_INVALID_ARGUMENT, "limit above 2 s");
+  int dev;
+  DeviceInfo info;
+  int rc = current_device(&dev, &info);
+  if (rc) return rc;
+  t8g::rows::wait_selftest_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(limit_ns, gave_up);
+  return launch_checked("wait_selftest launch");
+}
+
+}  // extern "C"

@@ -1,0 +1,251 @@
+"""torch-facing wrappers of the C ABI.
+
+torch provides device memory and the current stream only; every computation
+runs in the library's sm_100a kernels.  Tensors must be CUDA tensors with a
+unit stride along their last dimension.  Calls are asynchronous on the given
+stream (default: torch's current stream of the tensor's device).
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+
+OUT_CODE = {torch.bfloat16: _lib.OUT_BF16, torch.float16: _lib.OUT_F16, torch.float32: _lib.OUT_F32}
+QUANT_CODE = {"int8": _lib.QUANT_INT8, "fp8_e4m3": _lib.QUANT_FP8_E4M3}
+QUANT_DTYPE = {"int8": torch.int8, "fp8_e4m3": torch.float8_e4m3fn}
+F8_E4M3_MAX = 448.0
+
+
+def _stream_handle(device: torch.device, stream=None) -> ctypes.c_void_p:
+    if stream is None:
+        return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+    if isinstance(stream, torch.cuda.Stream):
+        return ctypes.c_void_p(stream.cuda_stream)
+    return ctypes.c_void_p(int(stream))
+
+
+def _ptr(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _need_cuda(name, t, dtype=None, ndim=None):
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name} must be a torch.Tensor")
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor (the library has no CPU path)")
+    if dtype is not None and t.dtype not in (dtype if isinstance(dtype, tuple) else (dtype,)):
+        raise TypeError(f"{name} has dtype {t.dtype}, expected {dtype}")
+    if ndim is not None and t.dim() != ndim:
+        raise ValueError(f"{name} must be {ndim}-D, got shape {tuple(t.shape)}")
+    if t.dim() >= 1 and t.numel() and t.stride(-1) != 1:
+        raise ValueError(f"{name} must have unit stride in its last dimension")
+
+
+def gemm_dequant(x: torch.Tensor, w: torch.Tensor, x_scale: torch.Tensor, w_scale: torch.Tensor,
+                 bias: torch.Tensor | None = None, out: torch.Tensor | None = None,
+                 out_dtype: torch.dtype = torch.bfloat16, stream=None) -> torch.Tensor:
+    """out = cast(((f32(x @ w^T) * x_scale[:, None]) * w_scale) + bias).
+
+    x [M, K] and w [N, K] are both int8 (exact int32 accumulation) or both
+    float8_e4m3fn (fp32 accumulation); x_scale [M] float32; w_scale [N] or [1]
+    float32; bias [N] in the output dtype or None/empty; out [M, N] bf16/fp16/fp32.
+    """
+    _need_cuda("x", x, (torch.int8, torch.float8_e4m3fn), 2)
+    _need_cuda("w", w, x.dtype, 2)
+    M, K = x.shape
+    N = w.shape[0]
+    if w.shape[1] != K:
+        raise ValueError(f"w has K={w.shape[1]}, x has K={K}")
+    _need_cuda("x_scale", x_scale, torch.float32)
+    _need_cuda("w_scale", w_scale, torch.float32)
+    if x_scale.numel() != M or not x_scale.is_contiguous():
+        raise ValueError("x_scale must be a contiguous float32 tensor with M elements")
+    if w_scale.numel() not in (1, N) or not w_scale.is_contiguous():
+        raise ValueError("w_scale must be a contiguous float32 tensor with 1 or N elements")
+    if out is None:
+        out = torch.empty(M, N, dtype=out_dtype, device=x.device)
+    _need_cuda("out", out, tuple(OUT_CODE), 2)
+    if tuple(out.shape) != (M, N):
+        raise ValueError(f"out has shape {tuple(out.shape)}, expected {(M, N)}")
+    nb = 0 if bias is None else bias.numel()
+    if nb:
+        _need_cuda("bias", bias, out.dtype)
+        if nb != N or not bias.is_contiguous():
+            raise ValueError("bias must be contiguous with N elements, in the output dtype")
+    lib = _lib.load()
+    fn = lib.t8g_gemm_i8_dequant if x.dtype == torch.int8 else lib.t8g_gemm_fp8_dequant
+    with torch.cuda.device(x.device):
+        rc = fn(_ptr(x), _ptr(w), _ptr(x_scale), _ptr(w_scale), w_scale.numel(), _ptr(bias) if nb else None, nb,
+                _ptr(out), OUT_CODE[out.dtype], M, N, K, x.stride(0), w.stride(0), out.stride(0),
+                _stream_handle(x.device, stream))
+    _lib.check(rc)
+    return out
+
+
+def quant_rows(x: torch.Tensor, kind: str = "int8", q: torch.Tensor | None = None,
+               q_scale: torch.Tensor | None = None, stream=None):
+    """Per-token quantisation of a bf16 [S, D] matrix -> (q [S, D], q_scale [S] float32)."""
+    _need_cuda("x", x, torch.bfloat16, 2)
+    S, D = x.shape
+    if q is None:
+        q = torch.empty(S, D, dtype=QUANT_DTYPE[kind], device=x.device)
+    if q_scale is None:
+        q_scale = torch.empty(S, dtype=torch.float32, device=x.device)
+    _need_cuda("q", q, QUANT_DTYPE[kind], 2)
+    with torch.cuda.device(x.device):
+        rc = _lib.load().t8g_quant_rows(_ptr(x), x.stride(0), _ptr(q), q.stride(0), _ptr(q_scale), S, D,
+                                        QUANT_CODE[kind], _stream_handle(x.device, stream))
+    _lib.check(rc)
+    return q, q_scale
+
+
+def _mod_args(x, shift, scale, mod_index, rows_per_mod):
+    S, D = x.shape
+    for name, t in (("shift", shift), ("scale", scale)):
+        _need_cuda(name, t, torch.bfloat16)
+        if t.dim() == 1:
+            if t.shape[0] != D:
+                raise ValueError(f"{name} must have D={D} elements")
+        elif t.dim() != 2 or t.shape[1] != D:
+            raise ValueError(f"{name} must be [n_mod, D]")
+    shift2 = shift.reshape(-1, D)
+    scale2 = scale.reshape(-1, D)
+    if shift2.stride(0) != scale2.stride(0):
+        raise ValueError("shift and scale must share a row stride")
+    if mod_index is not None:
+        _need_cuda("mod_index", mod_index, torch.int32, 1)
+        if mod_index.numel() != S or not mod_index.is_contiguous():
+            raise ValueError("mod_index must be a contiguous int32 tensor with S elements")
+        rows_per_mod = 1
+    elif rows_per_mod is None:
+        n_mod = shift2.shape[0]
+        if S % n_mod:
+            raise ValueError(f"{S} rows do not split evenly over {n_mod} modulation rows; pass mod_index")
+        rows_per_mod = max(S // n_mod, 1)
+    return shift2, scale2, rows_per_mod
+
+
+def rms_mod_quant(x: torch.Tensor, shift: torch.Tensor, scale: torch.Tensor, *, w: torch.Tensor | None = None,
+                  mod_index: torch.Tensor | None = None, rows_per_mod: int | None = None,
+                  scale_is_multiplier: bool = False, eps: float = 1e-6, kind: str = "fp8_e4m3",
+                  return_h: bool = False, return_res: bool = False, stream=None):
+    """One-pass RMSNorm + adaLN modulation + per-token quantisation of x [S, D] bf16.
+
+    h = rms_norm(x) * w * s + shift[row], s = bf16(1 + scale[row]) (or scale itself
+    when scale_is_multiplier); the modulation row of token r is mod_index[r], or
+    r // rows_per_mod (default: S split evenly over the rows of shift/scale).
+    Returns (q, q_scale[, h][, res]).
+    """
+    _need_cuda("x", x, torch.bfloat16, 2)
+    S, D = x.shape
+    shift2, scale2, rpm = _mod_args(x, shift, scale, mod_index, rows_per_mod)
+    if w is not None:
+        _need_cuda("w", w, torch.bfloat16, 1)
+        if w.numel() != D:
+            raise ValueError("w must have D elements")
+    q = torch.empty(S, D, dtype=QUANT_DTYPE[kind], device=x.device)
+    q_scale = torch.empty(S, dtype=torch.float32, device=x.device)
+    h = torch.empty_like(x) if return_h else None
+    res = torch.empty_like(x) if return_res else None
+    with torch.cuda.device(x.device):
+        rc = _lib.load().t8g_rms_mod_quant(
+            _ptr(x), x.stride(0), _ptr(w), _ptr(shift2), _ptr(scale2), shift2.stride(0), _ptr(mod_index), rpm,
+            int(scale_is_multiplier), float(eps), _ptr(q), q.stride(0), _ptr(q_scale), _ptr(h), D, _ptr(res), D,
+            S, D, QUANT_CODE[kind], _stream_handle(x.device, stream))
+    _lib.check(rc)
+    out = [q, q_scale]
+    if return_h:
+        out.append(h)
+    if return_res:
+        out.append(res)
+    return tuple(out)
+
+
+def rms_mod_quant_tensorwise(x, shift, scale, *, w=None, mod_index=None, rows_per_mod=None,
+                             scale_is_multiplier=False, eps=1e-5, kind="fp8_e4m3", want_res=True, stream=None):
+    """The reference's two-phase form: (q, scale 0-d tensor, h, res); one scale for the tensor."""
+    _need_cuda("x", x, torch.bfloat16, 2)
+    S, D = x.shape
+    shift2, scale2, rpm = _mod_args(x, shift, scale, mod_index, rows_per_mod)
+    if w is not None:
+        _need_cuda("w", w, torch.bfloat16, 1)
+    q = torch.empty(S, D, dtype=QUANT_DTYPE[kind], device=x.device)
+    h = torch.empty_like(x)
+    res = torch.empty_like(x) if want_res else None
+    amax = torch.zeros((), dtype=torch.float32, device=x.device)
+    qs = torch.empty((), dtype=torch.float32, device=x.device)
+    with torch.cuda.device(x.device):
+        rc = _lib.load().t8g_rms_mod_quant_tensorwise(
+            _ptr(x), x.stride(0), _ptr(w), _ptr(shift2), _ptr(scale2), shift2.stride(0), _ptr(mod_index), rpm,
+            int(scale_is_multiplier), float(eps), _ptr(q), q.stride(0), _ptr(h), D, _ptr(res), D, _ptr(amax),
+            _ptr(qs), S, D, QUANT_CODE[kind], _stream_handle(x.device, stream))
+    _lib.check(rc)
+    return q, qs, h, res
+
+
+def swiglu_quant(gate: torch.Tensor, up: torch.Tensor, kind: str = "int8", return_act: bool = False, stream=None):
+    """act = bf16(silu(gate) * up), per-token quantised -> (q, q_scale[, act]).
+
+    gate and up are [M, F] bf16 views with the same row stride (for example the
+    two halves of a [M, 2F] fc1 output, read in place)."""
+    _need_cuda("gate", gate, torch.bfloat16, 2)
+    _need_cuda("up", up, torch.bfloat16, 2)
+    if gate.shape != up.shape or gate.stride() != up.stride():
+        raise ValueError("gate and up must have the same shape and strides")
+    M, F = gate.shape
+    q = torch.empty(M, F, dtype=QUANT_DTYPE[kind], device=gate.device)
+    q_scale = torch.empty(M, dtype=torch.float32, device=gate.device)
+    act = torch.empty(M, F, dtype=torch.bfloat16, device=gate.device) if return_act else None
+    with torch.cuda.device(gate.device):
+        rc = _lib.load().t8g_swiglu_quant(_ptr(gate), _ptr(up), gate.stride(0), _ptr(q), q.stride(0), _ptr(q_scale),
+                                          _ptr(act), F, M, F, QUANT_CODE[kind], _stream_handle(gate.device, stream))
+    _lib.check(rc)
+    return (q, q_scale, act) if return_act else (q, q_scale)
+
+
+def swiglu_quant_fc1(y: torch.Tensor, kind: str = "int8", return_act: bool = False, stream=None):
+    """SwiGLU + quant of a [M, 2F] fc1 output whose first half is the gate."""
+    F = y.shape[-1] // 2
+    return swiglu_quant(y[:, :F], y[:, F:], kind=kind, return_act=return_act, stream=stream)
+
+
+def swiglu_quant_tensorwise(gate, up, kind="fp8_e4m3", stream=None):
+    """The reference's two-phase form: (q, scale 0-d tensor, act)."""
+    _need_cuda("gate", gate, torch.bfloat16, 2)
+    _need_cuda("up", up, torch.bfloat16, 2)
+    if gate.shape != up.shape or gate.stride() != up.stride():
+        raise ValueError("gate and up must have the same shape and strides")
+    M, F = gate.shape
+    q = torch.empty(M, F, dtype=QUANT_DTYPE[kind], device=gate.device)
+    act = torch.empty(M, F, dtype=torch.bfloat16, device=gate.device)
+    amax = torch.zeros((), dtype=torch.float32, device=gate.device)
+    qs = torch.empty((), dtype=torch.float32, device=gate.device)
+    with torch.cuda.device(gate.device):
+        rc = _lib.load().t8g_swiglu_quant_tensorwise(_ptr(gate), _ptr(up), gate.stride(0), _ptr(q), q.stride(0),
+                                                     _ptr(act), F, _ptr(amax), _ptr(qs), M, F, QUANT_CODE[kind],
+                                                     _stream_handle(gate.device, stream))
+    _lib.check(rc)
+    return q, qs, act
+
+
+def device_status(device=None, stream=None) -> int:
+    """Synchronise and read/clear the device status word (0 = no wait ran out)."""
+    device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    st = ctypes.c_int(0)
+    with torch.cuda.device(device):
+        rc = _lib.load().t8g_device_status(_stream_handle(device, stream), ctypes.byref(st))
+    _lib.check(rc)
+    return st.value
+
+
+def wait_selftest(limit_ns: int = 20_000_000, device=None) -> int:
+    """Run the bounded-wait self-test kernel; returns 1 if the wait gave up."""
+    device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    flag = torch.zeros(1, dtype=torch.int32, device=device)
+    with torch.cuda.device(device):
+        rc = _lib.load().t8g_wait_selftest(limit_ns, _ptr(flag), _stream_handle(device))
+    _lib.check(rc)
+    return int(flag.item())
