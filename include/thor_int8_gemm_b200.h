@@ -144,6 +144,34 @@ int t8g_swiglu_quant_tensorwise(const void* gate, const void* up, int64_t ld_in,
                                 void* act, int64_t ld_act, float* amax, float* scale_out, int64_t M, int64_t F,
                                 int quant_kind, void* stream);
 
+/*
+ * Allocation-free variant of t8g_rms_mod_quant_tensorwise.  No counterpart in the reference.
+ *
+ * Some callers cannot allocate device memory at the point where they quantise: plugins
+ * hosted by a process whose allocator owns every byte of the GPU, C callers with no CUDA
+ * allocator of their own, and code paths where cudaMalloc's implicit device-wide
+ * synchronisation is not acceptable.  The tensorwise form needs two scratch buffers (the
+ * float32 amax word and the bf16 intermediate h that the second pass quantises), which
+ * t8g_rms_mod_quant_tensorwise takes from its caller.  This entry point takes neither: both
+ * live in one file-scope device array of T8G_NOALLOC_SCRATCH_BYTES that every GPU which
+ * loads the library holds until the process exits.  The caller passes only inputs and
+ * outputs (q, optional res, scale_out).
+ *
+ * Limit: S * D * 2 + 256 <= T8G_NOALLOC_SCRATCH_BYTES (S * D <= 8388480 elements, e.g.
+ * 2730 rows of 3072); larger problems are rejected with T8G_ERR_UNSUPPORTED.  The first
+ * call on a device looks up the array's device address (once per device, with that device
+ * current), so make that first call before any stream capture.  The call zeroes the amax
+ * word itself.  All calls share the one array and it keeps the last call's contents, so
+ * calls that overlap on the GPU (other streams, other host threads on the same device)
+ * race; serialise them.  Arguments and results otherwise as t8g_rms_mod_quant_tensorwise.
+ */
+#define T8G_NOALLOC_SCRATCH_BYTES (16u * 1024u * 1024u)
+int t8g_rms_mod_quant_tensorwise_noalloc(const void* x, int64_t ld_x, const void* w, const void* shift,
+                                         const void* scale, int64_t ld_mod, const int32_t* mod_index,
+                                         int64_t rows_per_mod, int scale_is_multiplier, float eps, void* q,
+                                         int64_t ld_q, void* res, int64_t ld_res, float* scale_out, int64_t S,
+                                         int64_t D, int quant_kind, void* stream);
+
 /* Bounded-wait self-test: one kernel waits `limit_ns` on an mbarrier that nothing
  * completes, gives up, records status 0x1FF and writes 1 to the device int *gave_up.
  * Used by the tests to show that a wait which runs out ends the kernel with a status

@@ -40,6 +40,8 @@ SIGNATURES = {
                                             _vp, _i64, _vp, _i64, _vp, _i64, _vp, _vp, _i64, _i64, _i32, _vp]),
     "t8g_swiglu_quant": (_i32, [_vp, _vp, _i64, _vp, _i64, _vp, _vp, _i64, _i64, _i64, _i32, _vp]),
     "t8g_swiglu_quant_tensorwise": (_i32, [_vp, _vp, _i64, _vp, _i64, _vp, _i64, _vp, _vp, _i64, _i64, _i32, _vp]),
+    "t8g_rms_mod_quant_tensorwise_noalloc": (_i32, [_vp, _i64, _vp, _vp, _vp, _i64, _vp, _i64, _i32, _f32,
+                                                    _vp, _i64, _vp, _i64, _vp, _i64, _i64, _i32, _vp]),
     "t8g_wait_selftest": (_i32, [_u64, _vp, _vp]),
 }
 

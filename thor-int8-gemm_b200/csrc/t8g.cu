@@ -387,6 +387,31 @@ int swiglu_common(bool tensorwise, const void* gate, const void* up, int64_t ld_
   return launch_checked("swiglu_quant launch");
 }
 
+// ----------------------------------------------------------------- allocation-free scratch
+// Backing store of t8g_rms_mod_quant_tensorwise_noalloc: the amax word at offset 0, the bf16
+// intermediate h from offset kNoAllocHOffset.  Loaded with the module on every device that
+// uses the library; host code reaches it only through the address cudaGetSymbolAddress
+// returns for the current device (the symbol itself is a host-side stand-in).
+static __device__ __align__(256) unsigned char g_noalloc_scratch[T8G_NOALLOC_SCRATCH_BYTES];
+constexpr uint64_t kNoAllocHOffset = 256;
+
+void* g_noalloc_addr[kMaxDevices] = {};
+std::mutex g_noalloc_mu;
+
+// Device address of g_noalloc_scratch on device `dev` (which must be current); looked up
+// on the first use per device and cached.
+int noalloc_scratch(int dev, unsigned char** out) {
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_addr[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(no-alloc scratch)");
+    g_noalloc_addr[dev] = p;
+  }
+  *out = static_cast<unsigned char*>(g_noalloc_addr[dev]);
+  return T8G_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -482,6 +507,33 @@ int t8g_swiglu_quant_tensorwise(const void* gate, const void* up, int64_t ld_in,
                                 int quant_kind, void* stream) {
   return swiglu_common(true, gate, up, ld_in, q, ld_q, nullptr, act, ld_act, amax, scale_out, M, F, quant_kind,
                        stream);
+}
+
+int t8g_rms_mod_quant_tensorwise_noalloc(const void* x, int64_t ld_x, const void* w, const void* shift,
+                                         const void* scale, int64_t ld_mod, const int32_t* mod_index,
+                                         int64_t rows_per_mod, int scale_is_multiplier, float eps, void* q,
+                                         int64_t ld_q, void* res, int64_t ld_res, float* scale_out, int64_t S,
+                                         int64_t D, int quant_kind, void* stream) {
+  g_last_error[0] = '\0';
+  if (S < 0 || D < 0) return fail(T8G_ERR_INVALID_ARGUMENT, "no-alloc tensorwise: negative size");
+  const uint64_t cap = (T8G_NOALLOC_SCRATCH_BYTES - kNoAllocHOffset) / 2;
+  if (S != 0 && D != 0 && static_cast<uint64_t>(S) > cap / static_cast<uint64_t>(D))
+    return fail(T8G_ERR_UNSUPPORTED,
+                "no-alloc tensorwise: S*D = %lld elements exceeds the built-in scratch (%llu elements, "
+                "%u bytes); use t8g_rms_mod_quant_tensorwise with caller-provided buffers",
+                (long long)(S * D), (unsigned long long)cap, (unsigned)T8G_NOALLOC_SCRATCH_BYTES);
+  unsigned char* base = nullptr;
+  if (S != 0 && D != 0) {
+    int dev;
+    DeviceInfo info;
+    int rc = current_device(&dev, &info);
+    if (rc) return rc;
+    if ((rc = noalloc_scratch(dev, &base))) return rc;
+  }
+  float* amax = reinterpret_cast<float*>(base);
+  void* h = base ? base + kNoAllocHOffset : nullptr;
+  return rms_common(true, x, ld_x, w, shift, scale, ld_mod, mod_index, rows_per_mod, scale_is_multiplier, eps, q,
+                    ld_q, nullptr, h, D, res, ld_res, amax, scale_out, S, D, quant_kind, stream);
 }
 
 int t8g_wait_selftest(uint64_t limit_ns, int* gave_up, void* stream) {
