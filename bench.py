@@ -59,7 +59,49 @@ def parse_args():
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true")
+    ap.add_argument("--profile", choices=("gemm_i8", "gemm_fp8", "rms_fp8", "rms_int8", "swiglu_int8"),
+                    help="run one kernel a few times on a mid-size case (for ncu captures) and exit")
+    ap.add_argument("--M", type=int, default=32768)
+    ap.add_argument("--N", type=int, default=9216)
     return ap.parse_args()
+
+
+def run_profile_case(args):
+    """One kernel, `warmup + steps` launches, on a case whose inputs exceed L2 but stay
+    within a few GB: GEMM M x N x 3072; norm/quant [2*56320, 3072]; SwiGLU [32768, 2*12288]."""
+    import torch
+    from __graft_entry__ import load_package
+    load_package()
+    from thor_int8_gemm_b200 import ops
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(5)
+    n = args.warmup + args.steps
+    if args.profile.startswith("gemm"):
+        kind = "int8" if args.profile == "gemm_i8" else "fp8_e4m3"
+        x, xs = ops.quant_rows(torch.randn(args.M, K_DIM, generator=gen, device=dev).to(torch.bfloat16), kind)
+        w, ws = ops.quant_rows((torch.randn(args.N, K_DIM, generator=gen, device=dev) * 0.02).to(torch.bfloat16), kind)
+        bias = (torch.randn(args.N, generator=gen, device=dev) * 0.01).to(torch.bfloat16)
+        out = torch.empty(args.M, args.N, dtype=torch.bfloat16, device=dev)
+        for _ in range(n):
+            ops.gemm_dequant(x, w, xs, ws, bias, out=out)
+    elif args.profile.startswith("rms"):
+        kind = "int8" if args.profile == "rms_int8" else "fp8_e4m3"
+        x = torch.randn(2 * 56320, 3072, generator=gen, device=dev).to(torch.bfloat16)
+        sh = (torch.randn(2, 3072, generator=gen, device=dev) * 0.1).to(torch.bfloat16)
+        sc = (torch.randn(2, 3072, generator=gen, device=dev) * 0.1).to(torch.bfloat16)
+        for _ in range(n):
+            ops.rms_mod_quant(x, sh, sc, rows_per_mod=56320, eps=1e-6, kind=kind)
+    else:
+        y = torch.randn(32768, 2 * 12288, generator=gen, device=dev).to(torch.bfloat16)
+        for _ in range(n):
+            ops.swiglu_quant_fc1(y, kind="int8")
+    torch.cuda.synchronize()
+    status = ops.device_status()
+    print(json.dumps({"profile": args.profile, "launches": n, "device_status": status}))
+    if status:
+        raise SystemExit(1)
 
 
 def dist_env():
@@ -488,7 +530,9 @@ def run_ours(args):
 
 def main():
     args = parse_args()
-    if args.impl == "reference":
+    if args.profile:
+        run_profile_case(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

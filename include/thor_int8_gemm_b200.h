@@ -130,7 +130,7 @@ int t8g_rms_mod_quant_tensorwise(const void* x, int64_t ld_x, const void* w, con
  *   q, q_scale = per-token quantisation of act; act optionally stored.
  * gate and up are [M, F] bf16 with the common row stride ld_in, so the two halves of a
  * [M, 2F] fc1 output are read in place (gate = y, up = y + F, ld_in = 2F).
- * Requirements as t8g_quant_rows with D = F.
+ * Requirements as t8g_quant_rows with D = F, except F <= 24576.
  */
 int t8g_swiglu_quant(const void* gate, const void* up, int64_t ld_in, void* q, int64_t ld_q, float* q_scale,
                      void* act, int64_t ld_act, int64_t M, int64_t F, int quant_kind, void* stream);

@@ -55,9 +55,11 @@ QUANT_FP8 = "fp8_e4m3"
 
 # Canonical launch shape of the row kernels: one row is handled by T threads,
 # T the smallest power of two in [32, ROW_MAX_THREADS] such that every thread
-# holds at most ROW_MAX_VEC 16-byte vectors (8 bf16 values) of the row.
-ROW_MAX_VEC = 12
+# holds at most ROW_FAST_VEC 16-byte vectors (8 bf16 values) of the row, else
+# ROW_MAX_THREADS (rows up to ROW_MAX_D values).
+ROW_FAST_VEC = 4
 ROW_MAX_THREADS = 512
+ROW_MAX_D = 49152
 
 
 # --------------------------------------------------------------------------
@@ -277,12 +279,12 @@ def fp8_gemm_tolerance(a_codes, w_codes, xs, ws, K: int) -> np.ndarray:
 # --------------------------------------------------------------------------
 def row_threads(D: int) -> int:
     """Threads that cooperate on one row in the row kernels (canonical shape)."""
+    if D > ROW_MAX_D:
+        raise ValueError(f"row length {D} exceeds {ROW_MAX_D}")
     nvec = (D + 7) // 8
     t = 32
-    while t < ROW_MAX_THREADS and (nvec + t - 1) // t > ROW_MAX_VEC:
+    while t < ROW_MAX_THREADS and (nvec + t - 1) // t > ROW_FAST_VEC:
         t *= 2
-    if (nvec + t - 1) // t > ROW_MAX_VEC:
-        raise ValueError(f"row length {D} exceeds {ROW_MAX_THREADS * 8 * ROW_MAX_VEC}")
     return t
 
 
@@ -291,14 +293,17 @@ def rms_sum_squares(x: np.ndarray) -> np.ndarray:
     the canonical order of the CUDA row kernel:
 
     * the row is split in 16-byte vectors of 8 values, vector c = t + T*i goes
-      to thread t (T = row_threads(D)); each thread adds its squares in order
-      (i outer, the 8 values inner) into a float32 accumulator;
+      to thread t (T = row_threads(D));
+    * each thread keeps two float32 accumulators, one for the even and one for
+      the odd element of every bf16 pair, and adds the squares of its vectors
+      in order (i ascending, pairs in order) -- a packed FMA in the kernel;
+    * the thread's value is even + odd;
     * each 32-thread warp combines its lanes by a butterfly: for offset in
       16, 8, 4, 2, 1: v = v + v[lane ^ offset];
     * warp results are added left to right: ((w0 + w1) + w2) + ...
 
-    Squares of bf16 values are exact in float32, so an FMA in the kernel and
-    the separate multiply-add here round identically.
+    Squares of bf16 values are exact in float32, so the kernel's FMA and the
+    separate multiply-add here round identically.
     """
     x = np.asarray(x, dtype=np.float32)
     S, D = x.shape
@@ -308,11 +313,16 @@ def rms_sum_squares(x: np.ndarray) -> np.ndarray:
     padded = np.zeros((S, V * T * 8), dtype=np.float32)
     padded[:, :D] = x
     xv = padded.reshape(S, V, T, 8)
-    acc = np.zeros((S, T), dtype=np.float32)
+    acc_e = np.zeros((S, T), dtype=np.float32)
+    acc_o = np.zeros((S, T), dtype=np.float32)
     for i in range(V):
         blk = xv[:, i]
-        for j in range(8):
-            acc = (acc + blk[:, :, j] * blk[:, :, j]).astype(np.float32)
+        for p in range(4):
+            e = blk[:, :, 2 * p]
+            o = blk[:, :, 2 * p + 1]
+            acc_e = (acc_e + e * e).astype(np.float32)
+            acc_o = (acc_o + o * o).astype(np.float32)
+    acc = (acc_e + acc_o).astype(np.float32)
     W = T // 32
     lanes = acc.reshape(S, W, 32)
     idx = np.arange(32)

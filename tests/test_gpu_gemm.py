@@ -23,6 +23,17 @@ def ops():
     assert _ops.device_status() == 0, "a bounded wait ran out during the GEMM tests"
 
 
+@pytest.fixture(params=["2sm", "1sm"])
+def path(request, monkeypatch):
+    """Run a test on the 2-SM kernel (CTA pairs, the default for M > 128) and on the
+    1-SM kernel (forced with T8G_GEMM_SM=1)."""
+    if request.param == "1sm":
+        monkeypatch.setenv("T8G_GEMM_SM", "1")
+    else:
+        monkeypatch.delenv("T8G_GEMM_SM", raising=False)
+    return request.param
+
+
 def out_bits(t: torch.Tensor) -> np.ndarray:
     t = t.cpu()
     if t.dtype == torch.float32:
@@ -43,7 +54,7 @@ GOLD = np.load(os.path.join(HERE, "golden", "gemm_golden.npz"))
 
 
 @pytest.mark.parametrize("i", range(int(GOLD["n_cases"])))
-def test_gemm_i8_matches_reference_golden(ops, i):
+def test_gemm_i8_matches_reference_golden(ops, path, i):
     p = f"g{i}_"
     M, N, K, hb, _ = GOLD[p + "meta"]
     dt = str(GOLD[p + "dtype"])
@@ -65,7 +76,7 @@ CASES = [
 
 
 @pytest.mark.parametrize("M,N,K,hb,dt,scalar", CASES)
-def test_gemm_i8_matches_oracle(ops, M, N, K, hb, dt, scalar):
+def test_gemm_i8_matches_oracle(ops, path, M, N, K, hb, dt, scalar):
     rng = np.random.default_rng(M * 7 + N * 3 + K)
     x8 = rng.integers(-127, 128, (M, K)).astype(np.int8)
     w8 = rng.integers(-127, 128, (N, K)).astype(np.int8)
@@ -79,7 +90,7 @@ def test_gemm_i8_matches_oracle(ops, M, N, K, hb, dt, scalar):
     np.testing.assert_array_equal(got, ref)
 
 
-def test_gemm_i8_extreme_values_exact(ops):
+def test_gemm_i8_extreme_values_exact(ops, path):
     """-128/127 operands at the largest K the audit covered (int32 never overflows)."""
     M, N, K = 130, 200, 65536
     x8 = np.full((M, K), -128, np.int8)
@@ -92,7 +103,7 @@ def test_gemm_i8_extreme_values_exact(ops):
                                   O.gemm_i8_dequant(x8, w8, xs, ws, None, "f32"))
 
 
-def test_gemm_i8_strided_rows(ops):
+def test_gemm_i8_strided_rows(ops, path):
     """Row strides larger than the row (views into a wider buffer)."""
     dev = "cuda"
     M, N, K = 257, 384, 320
@@ -110,7 +121,7 @@ def test_gemm_i8_strided_rows(ops):
     assert not torch.any(out_buf[:, N:].float() != 0), "wrote outside the output view"
 
 
-def test_gemm_i8_full_size_row_sampled(ops):
+def test_gemm_i8_full_size_row_sampled(ops, path):
     """M=32768 x N=9216 x K=3072 (a config-1 QKV shape): every output row of a
     sample of 48 rows, bit-exact against the oracle."""
     dev = "cuda"
@@ -130,7 +141,7 @@ def test_gemm_i8_full_size_row_sampled(ops):
 
 
 @pytest.mark.parametrize("M,N,K,dt", [(256, 512, 512, "bf16"), (1000, 272, 3072, "f32"), (130, 136, 96, "f16")])
-def test_gemm_fp8_within_accumulation_tolerance(ops, M, N, K, dt):
+def test_gemm_fp8_within_accumulation_tolerance(ops, path, M, N, K, dt):
     dev = "cuda"
     rng = np.random.default_rng(M + N + K)
     a = O.round_bf16(rng.standard_normal((M, K)).astype(np.float32))

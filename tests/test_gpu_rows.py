@@ -149,7 +149,7 @@ def test_tensorwise_segments_vs_reference_golden(ops):
 
 
 @pytest.mark.parametrize("kind", ["int8", "fp8_e4m3"])
-@pytest.mark.parametrize("M,F", [(8, 512), (33, 1536), (64, 12288), (3, 49152)])
+@pytest.mark.parametrize("M,F", [(8, 512), (33, 1536), (64, 12288), (5, 16384), (3, 24576)])
 def test_swiglu_quant_per_token(ops, kind, M, F):
     rng = np.random.default_rng(M * F)
     y = O.round_bf16(rng.standard_normal((M, 2 * F)).astype(np.float32) * 2)
@@ -204,6 +204,9 @@ def test_row_kernels_reject_bad_shapes(ops):
     x = torch.zeros(2, 49160, dtype=torch.bfloat16, device="cuda")
     with pytest.raises(T8GError, match="exceeds"):
         ops.quant_rows(x)
+    y = torch.zeros(2, 2 * 24584, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(T8GError, match="exceeds"):
+        ops.swiglu_quant_fc1(y)
 
 
 def test_bounded_wait_gives_up_and_context_survives(ops):
@@ -217,3 +220,36 @@ def test_bounded_wait_gives_up_and_context_survives(ops):
     q, s = ops.quant_rows(x)
     torch.cuda.synchronize()
     assert q.shape == (4, 64)
+
+
+@pytest.mark.parametrize("kind", ["int8", "fp8_e4m3"])
+def test_quantiser_ties_and_format_midpoints(ops, kind):
+    """Rows whose scale is exactly 1.0 and whose values sit on the rounding
+    boundaries of the 8-bit format (half-integers for int8, midpoints between
+    neighbouring e4m3 codes, including the subnormal ones), plus values one bf16
+    ulp either side: the quantiser must round them exactly like the oracle's IEEE
+    divide (ties to even)."""
+    if kind == "int8":
+        amax = 127.0
+        centres = np.arange(-127, 127, dtype=np.float64) + 0.5
+    else:
+        amax = 448.0
+        fin = O._E4M3_FINITE
+        mids = (fin[1:] + fin[:-1]) / 2
+        centres = np.concatenate([mids, -mids])
+    vals = O.round_bf16(centres.astype(np.float32))
+    up = O.bf16_to_f32(O.f32_to_bf16(vals) + 1)          # next bf16 away from zero
+    dn = O.bf16_to_f32(O.f32_to_bf16(vals) - 1)
+    row = np.concatenate([vals, up, dn]).astype(np.float32)
+    row = row[np.abs(row) <= amax]
+    D = ((row.size + 1 + 7) // 8) * 8
+    x = np.zeros((3, D), np.float32)
+    x[:, : row.size] = row
+    x[:, row.size] = amax                                  # pins the row scale to exactly 1.0
+    x[1] = -x[1]
+    x[2] = np.roll(x[2], 5)
+    q, s = ops.quant_rows(bf16_dev(to_bf16_bits(x)), kind)
+    q_ref, s_ref = O.quant_rows(x, KINDS[kind])
+    assert np.all(s_ref == 1.0)
+    np.testing.assert_array_equal(s.cpu().numpy(), s_ref)
+    np.testing.assert_array_equal(qbits(q, kind), q_ref)

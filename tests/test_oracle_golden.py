@@ -136,12 +136,14 @@ def test_rms_sum_squares_tree_matches_sequential_sum_closely():
 
 
 def test_row_threads_rule():
-    assert O.row_threads(3072) == 32
-    assert O.row_threads(12288) == 128
+    assert O.row_threads(3072) == 128
+    assert O.row_threads(1024) == 32
+    assert O.row_threads(5376) == 256
+    assert O.row_threads(12288) == 512
     assert O.row_threads(8) == 32
-    assert O.row_threads(512 * 8 * 12) == 512
+    assert O.row_threads(49152) == 512
     with pytest.raises(ValueError):
-        O.row_threads(512 * 8 * 12 + 8)
+        O.row_threads(49152 + 8)
 
 
 def test_per_token_quant_properties():

@@ -11,12 +11,13 @@ Submodules (imported lazily, so the import-proxy agent stays light at start-up):
   fused       mirror of the reference module ck_fused_mod_norm_quant
   patch_int8  the comfy-kitchen `_C` import proxy and its .pth installer
   build       nvcc build of the shared library
+  shard       token sharding across ranks (one process per GPU)
 """
 import importlib
 
 __version__ = "0.1.0"
 PACKAGE_NAME = "thor_int8_gemm_b200"
-_LAZY = ("ops", "fused", "patch_int8", "build", "_lib")
+_LAZY = ("ops", "fused", "patch_int8", "build", "_lib", "shard")
 
 
 def __getattr__(name):

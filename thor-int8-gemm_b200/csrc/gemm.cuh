@@ -10,6 +10,7 @@
 //
 // CTA layout (192 threads, one CTA per SM, persistent over output tiles):
 //   warp 0      TMA producer: A and W tiles -> 4-stage shared-memory ring
+//               (L2 priority: A normal, W evict-last, output stores evict-first)
 //   warp 1      MMA issuer:   tcgen05.mma 128x256x32 into one of two TMEM
 //               accumulators (2 x 256 columns), commit frees smem stages
 //   warps 2..5  epilogue:     TMEM -> registers (tcgen05.ld), dequant, convert,
@@ -152,6 +153,67 @@ __device__ __forceinline__ void load_channel_params(const Args& a, int n0, float
   }
 }
 
+// Epilogue of one 32-row slice of an output tile: TMEM columns [0, BN) of the lanes
+// at `t_row` -> fp32 dequant in the reference order -> output type -> swizzled
+// staging buffer (two per warp, alternating) -> TMA store at (n_tile0 + 32c, row0).
+template <int IN, int OUT>
+__device__ __forceinline__ void epilogue_tile(const Args& args, const CUtensorMap* tm_out,
+                                              uint8_t (*bufs)[EPI_BUF_BYTES], int& ebuf, uint32_t t_row, int row0,
+                                              int n_tile0, int lane, uint64_t pol_out) {
+  const int row = row0 + lane;
+  const float xs_r = row < args.M ? __ldg(args.xs + row) : 0.f;
+  const int nchunks = min(BN / EPI_COLS, (args.N - n_tile0 + EPI_COLS - 1) / EPI_COLS);
+  for (int c = 0; c < nchunks; ++c) {
+    uint32_t r[32];
+    tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(c * EPI_COLS), r);
+    tmem_ld_wait();
+    const int n0 = n_tile0 + c * EPI_COLS;
+    float wsv[32], bv[32];
+    load_channel_params<OUT>(args, n0, wsv, bv);
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      float f = (IN == kInI8) ? __int2float_rn(static_cast<int>(r[j])) : __uint_as_float(r[j]);
+      f = __fmul_rn(f, xs_r);
+      f = __fmul_rn(f, wsv[j]);
+      if (args.bias != nullptr) f = __fadd_rn(f, bv[j]);
+      v[j] = f;
+    }
+    // the staging buffer used two chunks ago must have been read by its TMA store
+    if (lane == 0) bulk_wait_group_read<1>();
+    __syncwarp();
+    uint8_t* buf = bufs[ebuf];
+    if constexpr (OutTraits<OUT>::kBytes == 2) {
+      // 32 rows x 64 B, 64-byte swizzle: 16-byte chunk q of row r lives at chunk q ^ ((r >> 1) & 3)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint4 w;
+        w.x = OutTraits<OUT>::pack2(v[8 * q + 0], v[8 * q + 1]);
+        w.y = OutTraits<OUT>::pack2(v[8 * q + 2], v[8 * q + 3]);
+        w.z = OutTraits<OUT>::pack2(v[8 * q + 4], v[8 * q + 5]);
+        w.w = OutTraits<OUT>::pack2(v[8 * q + 6], v[8 * q + 7]);
+        const int pq = q ^ ((lane >> 1) & 3);
+        *reinterpret_cast<uint4*>(buf + lane * 64 + pq * 16) = w;
+      }
+    } else {
+      // 32 rows x 128 B, 128-byte swizzle: chunk q of row r lives at chunk q ^ (r & 7)
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float4 w = make_float4(v[4 * q + 0], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+        const int pq = q ^ (lane & 7);
+        *reinterpret_cast<float4*>(buf + lane * 128 + pq * 16) = w;
+      }
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_2d(tm_out, buf, n0, row0, pol_out);
+      bulk_commit_group();
+    }
+    ebuf ^= 1;
+  }
+}
+
 template <int IN, int OUT>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_dequant_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
@@ -196,7 +258,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
-      const uint64_t pol_a = policy_evict_first();
+      // A row panels are re-read by every CTA of the panel (tiles run n-fastest): normal
+      // priority; W is re-read by every panel: keep it.
+      const uint64_t pol_a = policy_evict_normal();
       const uint64_t pol_b = policy_evict_last();
       int stage = 0;
       uint32_t phase = 0;
@@ -282,6 +346,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     // ------------------------------------------------------------ epilogue
     const int ew = warp - 2;           // staging slot of this warp
     const int quarter = warp & 3;      // TMEM lanes [32*quarter, 32*quarter+32) are readable by this warp
+    const uint64_t pol_out = policy_evict_first();   // the output is not re-read here
     int local = 0;
     int ebuf = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
@@ -293,60 +358,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tc_fence_after();
       const int row0 = tm * BM + quarter * 32;
       if (row0 < args.M) {
-        const int row = row0 + lane;
-        const float xs_r = row < args.M ? __ldg(args.xs + row) : 0.f;
-        const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
-        const int n_tile0 = tn * BN;
-        const int nchunks = min(BN / EPI_COLS, (args.N - n_tile0 + EPI_COLS - 1) / EPI_COLS);
-        for (int c = 0; c < nchunks; ++c) {
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(c * EPI_COLS), r);
-          tmem_ld_wait();
-          const int n0 = n_tile0 + c * EPI_COLS;
-          float wsv[32], bv[32];
-          load_channel_params<OUT>(args, n0, wsv, bv);
-          float v[32];
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            float f = (IN == kInI8) ? __int2float_rn(static_cast<int>(r[j])) : __uint_as_float(r[j]);
-            f = __fmul_rn(f, xs_r);
-            f = __fmul_rn(f, wsv[j]);
-            if (args.bias != nullptr) f = __fadd_rn(f, bv[j]);
-            v[j] = f;
-          }
-          // the staging buffer used two chunks ago must have been read by its TMA store
-          if (lane == 0) bulk_wait_group_read<1>();
-          __syncwarp();
-          uint8_t* buf = s.epi[ew][ebuf];
-          if constexpr (OutTraits<OUT>::kBytes == 2) {
-            // 32 rows x 64 B, 64-byte swizzle: 16-byte chunk q of row r lives at chunk q ^ ((r >> 1) & 3)
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              uint4 w;
-              w.x = OutTraits<OUT>::pack2(v[8 * q + 0], v[8 * q + 1]);
-              w.y = OutTraits<OUT>::pack2(v[8 * q + 2], v[8 * q + 3]);
-              w.z = OutTraits<OUT>::pack2(v[8 * q + 4], v[8 * q + 5]);
-              w.w = OutTraits<OUT>::pack2(v[8 * q + 6], v[8 * q + 7]);
-              const int pq = q ^ ((lane >> 1) & 3);
-              *reinterpret_cast<uint4*>(buf + lane * 64 + pq * 16) = w;
-            }
-          } else {
-            // 32 rows x 128 B, 128-byte swizzle: chunk q of row r lives at chunk q ^ (r & 7)
-#pragma unroll
-            for (int q = 0; q < 8; ++q) {
-              const float4 w = make_float4(v[4 * q + 0], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-              const int pq = q ^ (lane & 7);
-              *reinterpret_cast<float4*>(buf + lane * 128 + pq * 16) = w;
-            }
-          }
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) {
-            tma_store_2d(&tm_out, buf, n0, row0);
-            bulk_commit_group();
-          }
-          ebuf ^= 1;
-        }
+        epilogue_tile<IN, OUT>(args, &tm_out, s.epi[ew], ebuf, tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                                                                 static_cast<uint32_t>(acc * BN),
+                               row0, tn * BN, lane, pol_out);
       }
       // hand the accumulator back to the MMA warp
       tc_fence_before();
@@ -362,6 +376,226 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// ===========================================================================
+// 2-SM variant: a cluster of two CTAs (one per SM of a TPC) computes a 256x256
+// output tile with tcgen05.mma.cta_group::2 (M = 256, N = 256, K = 32).
+//   CTA r loads its own A rows [tm*256 + 128r, +128) and its own half of W, rows
+//   [tn*256 + 128r, +128), into its own shared memory; the loads of both CTAs
+//   complete on the leader's (r = 0) `full` barrier; every CTA loads only its own
+//   operands.
+//   The leader's single MMA thread issues the pair MMA, which reads the operands
+//   of both CTAs and accumulates rows 128r..128r+127 in CTA r's TMEM; its commits
+//   free the stage in both CTAs and hand each CTA its accumulator.
+//   Each CTA's epilogue warps store their own 128 rows and report the
+//   accumulator free on the leader's `tmem_empty` barrier.
+// Per SM this halves W's share of the shared-memory fill and of the tensor
+// core's operand reads compared with the 1-SM kernel, and 6 stages fit.
+// ===========================================================================
+constexpr int P_BM = 256;                   // tile rows per CTA pair
+constexpr int P_ROWS = 128;                 // rows of A (and of W) per CTA
+constexpr int P_STAGES = 6;
+constexpr int P_A_BYTES = P_ROWS * BK;
+constexpr int P_B_BYTES = P_ROWS * BK;
+constexpr int P_STAGE_BYTES = P_A_BYTES + P_B_BYTES;   // per CTA
+
+struct SmemPair {
+  uint8_t a[P_STAGES][P_A_BYTES];
+  uint8_t b[P_STAGES][P_B_BYTES];
+  uint8_t epi[EPI_WARPS][2][EPI_BUF_BYTES];
+  uint64_t full[P_STAGES];
+  uint64_t empty[P_STAGES];
+  uint64_t tmem_full[2];
+  uint64_t tmem_empty[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+};
+constexpr size_t P_SMEM_BYTES = sizeof(SmemPair) + 1024;
+
+template <int IN, int OUT>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
+    gemm_dequant_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+                             const __grid_constant__ CUtensorMap tm_out, const Args args) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
+  SmemPair& s = *reinterpret_cast<SmemPair*>(smem_raw + pad);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int pair = static_cast<int>(blockIdx.x >> 1);
+  const int npairs = static_cast<int>(gridDim.x >> 1);
+  const int tiles_n = (args.N + BN - 1) / BN;
+  const int tiles_m = (args.M + P_BM - 1) / P_BM;
+  const int num_tiles = tiles_m * tiles_n;
+  const int kblocks = (args.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int i = 0; i < P_STAGES; ++i) {
+      mbar_init(&s.full[i], 1);
+      mbar_init(&s.empty[i], 1);
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s.tmem_full[i], 1);
+      mbar_init(&s.tmem_empty[i], 2 * EPI_WARPS);
+    }
+    mbar_init(&s.drain, 1);
+    fence_mbarrier_init();
+    prefetch_tensormap(&tm_a);
+    prefetch_tensormap(&tm_b);
+    prefetch_tensormap(&tm_out);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(&s.tmem_base, TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();   // both CTAs' barriers initialised before any cross-CTA signal
+  tc_fence_after();
+  const uint32_t tmem_base = s.tmem_base;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer (both CTAs)
+    if (lane == 0) {
+      const uint64_t pol_a = policy_evict_normal();
+      const uint64_t pol_b = policy_evict_last();
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0;
+      bool ok = true;
+      for (int tile = pair; ok && tile < num_tiles; tile += npairs) {
+        const int tm = tile / tiles_n;
+        const int tn = tile - tm * tiles_n;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&s.empty[stage], phase ^ 1u, kStatusTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          if (rank == 0) mbar_arrive_expect_tx(&s.full[stage], 2 * P_STAGE_BYTES);
+          const uint32_t bar = mapa_shared(smem_u32(&s.full[stage]), 0);
+          tma_load_2d_pair(s.a[stage], &tm_a, bar, kb * BK, tm * P_BM + static_cast<int>(rank) * P_ROWS, pol_a);
+          tma_load_2d_pair(s.b[stage], &tm_b, bar, kb * BK, tn * BN + static_cast<int>(rank) * P_ROWS, pol_b);
+          ++issued;
+          if (++stage == P_STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // the leader sees every copy of the pair land on its `full` barriers
+      if (rank == 0) {
+        for (int i = 0; i < P_STAGES && i < issued; ++i) {
+          const int n = issued - 1 - i;
+          if (!mbar_wait(&s.full[n % P_STAGES], static_cast<uint32_t>((n / P_STAGES) & 1), kStatusTimeoutDrain)) break;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (leader only)
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t idesc = (IN == kInI8) ? make_idesc(2, 1, 1, P_BM, BN)   // s32 <- s8 x s8
+                                               : make_idesc(1, 0, 0, P_BM, BN);  // f32 <- e4m3 x e4m3
+      uint32_t empty_bar[P_STAGES][2], tfull_bar[2][2];
+#pragma unroll
+      for (int i = 0; i < P_STAGES; ++i) {
+        empty_bar[i][0] = mapa_shared(smem_u32(&s.empty[i]), 0);
+        empty_bar[i][1] = mapa_shared(smem_u32(&s.empty[i]), 1);
+      }
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        tfull_bar[i][0] = mapa_shared(smem_u32(&s.tmem_full[i]), 0);
+        tfull_bar[i][1] = mapa_shared(smem_u32(&s.tmem_full[i]), 1);
+      }
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true, any = false;
+      for (int tile = pair; ok && tile < num_tiles; tile += npairs, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = static_cast<uint32_t>((local >> 1) & 1);
+        if (!mbar_wait(&s.tmem_empty[acc], acc_phase ^ 1u, kStatusTimeoutMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&s.full[stage], phase, kStatusTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(s.a[stage]);
+          const uint32_t b0 = smem_u32(s.b[stage]);
+#pragma unroll
+          for (int k = 0; k < BK / MMA_K; ++k) {
+            const uint64_t ad = smem_desc_k_sw128(a0 + k * MMA_K);
+            const uint64_t bd = smem_desc_k_sw128(b0 + k * MMA_K);
+            const uint32_t accumulate = (kb | k) != 0 ? 1u : 0u;
+            if constexpr (IN == kInI8)
+              mma_i8_pair(d_tmem, ad, bd, idesc, accumulate);
+            else
+              mma_f8_pair(d_tmem, ad, bd, idesc, accumulate);
+          }
+          tc_commit_pair(empty_bar[stage][0]);
+          tc_commit_pair(empty_bar[stage][1]);
+          any = true;
+          if (++stage == P_STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        tc_commit_pair(tfull_bar[acc][0]);
+        tc_commit_pair(tfull_bar[acc][1]);
+      }
+      if (any) {
+        tc_commit_pair(mapa_shared(smem_u32(&s.drain), 0));
+        mbar_wait(&s.drain, 0, kStatusTimeoutDrain);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    const int ew = warp - 2;
+    const int quarter = warp & 3;
+    const uint64_t pol_out = policy_evict_first();
+    uint32_t tempty_bar[2];
+    tempty_bar[0] = mapa_shared(smem_u32(&s.tmem_empty[0]), 0);
+    tempty_bar[1] = mapa_shared(smem_u32(&s.tmem_empty[1]), 0);
+    int local = 0;
+    int ebuf = 0;
+    for (int tile = pair; tile < num_tiles; tile += npairs, ++local) {
+      const int tm = tile / tiles_n;
+      const int tn = tile - tm * tiles_n;
+      const int acc = local & 1;
+      const uint32_t acc_phase = static_cast<uint32_t>((local >> 1) & 1);
+      if (!mbar_wait(&s.tmem_full[acc], acc_phase, kStatusTimeoutEpilogue)) break;
+      tc_fence_after();
+      const int row0 = tm * P_BM + static_cast<int>(rank) * P_ROWS + quarter * 32;
+      if (row0 < args.M) {
+        epilogue_tile<IN, OUT>(args, &tm_out, s.epi[ew], ebuf,
+                               tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN),
+                               row0, tn * BN, lane, pol_out);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(tempty_bar[acc]);
+    }
+    if (lane == 0) bulk_wait_group_all();
+    __syncwarp();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();   // the pair's MMAs, copies and cross-CTA signals are all done
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, TMEM_COLS);
   }
 }
 

@@ -2,18 +2,29 @@
 // modulation + quantisation, fused SwiGLU + quantisation, and the reference's
 // tensorwise two-phase forms.
 //
-// One row (token) is processed by T threads, T the smallest power of two in
-// [32, 512] such that each thread holds at most MAX_VEC 16-byte vectors (8
-// bf16 values); vector c of the row goes to thread c % T.  The whole row stays
-// in registers between the reduction passes, so x (or gate/up) is read from
-// HBM exactly once and q + one scale per row are written once.
+// Data movement: persistent CTAs, one row group of T threads per CTA.  Rows
+// stream HBM -> shared memory through a ring of `stages` slots filled by 1-D
+// bulk copies (cp.async.bulk, completion on an mbarrier per slot), so many
+// rows are in flight per SM without holding registers for them.  Each row is
+// read from HBM once and q + one scale (plus optional bf16 outputs) written
+// once.  Thread t of the CTA owns the 16-byte vectors c = t, t + T, t + 2T, ...
+// of a row.
 //
-// Canonical arithmetic (restated by the CPU oracle, bit for bit):
-//   sum of squares: per-thread FMA accumulation in vector order, warp
-//   butterfly (xor 16, 8, 4, 2, 1), then warp partials added left to right;
+// T is the smallest power of two in [32, 512] that leaves at most kFastVec
+// vectors per thread (512 for longer rows; rows are limited by the ring's slot
+// size, 96 KB).  Canonical arithmetic, restated
+// bit for bit by the CPU oracle:
+//   sum of squares: per thread, two FMA accumulators (even / odd element of each
+//   bf16 pair) in vector order, combined as even + odd (the squares of bf16 values
+//   are exact in fp32); warp butterfly (xor 16, 8, 4, 2, 1); warp partials added
+//   left to right;
 //   inv = 1 / sqrt(ss / D + eps) with IEEE divide and square root;
 //   h = (((x * inv) * w) * s) + b, every product and sum rounded separately;
-//   per-token scale = max(amax / qmax, 1e-12); q = cvt(clamp(v / scale)).
+//   per-token scale = max(amax / qmax, 1e-12) (IEEE divide);
+//   q = cvt(RN(v / scale)) (see quant8: a reciprocal multiply with an exact
+//   fallback near rounding boundaries), round-half-even (int8, which never
+//   needs the +-127 clamp: |v / scale| <= 127 * (1 + 2^-23)) or the saturating
+//   RNE e4m3 conversion (fp8).
 #pragma once
 
 #include <cuda_bf16.h>
@@ -23,10 +34,11 @@
 namespace t8g {
 namespace rows {
 
-constexpr int MAX_VEC = 12;
+constexpr int kFastVec = 4;        // vectors per thread that set the row-group size T
 constexpr float kScaleMin = 1e-12f;   // src/ck_fused_mod_norm_quant.py:141
 
 enum QuantKind : int { kQuantInt8 = 0, kQuantFp8 = 1 };
+enum Mode : int { kModeInt8 = 0, kModeFp8 = 1, kModeTensorwise = 2 };
 
 template <int QK>
 struct QMax;
@@ -39,13 +51,10 @@ struct QMax<kQuantFp8> {
   static constexpr float v = 448.0f;
 };
 
+
+// ---------------------------------------------------------------- bf16 helpers
 __device__ __forceinline__ float bf_lo(uint32_t u) { return __uint_as_float(u << 16); }
 __device__ __forceinline__ float bf_hi(uint32_t u) { return __uint_as_float(u & 0xFFFF0000u); }
-__device__ __forceinline__ float bf_at(const uint4& v, int j) {
-  const uint32_t w = (j < 2) ? v.x : (j < 4) ? v.y : (j < 6) ? v.z : v.w;
-  return (j & 1) ? bf_hi(w) : bf_lo(w);
-}
-__device__ __forceinline__ float round_bf16(float f) { return __bfloat162float(__float2bfloat16_rn(f)); }
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
@@ -57,94 +66,165 @@ __device__ __forceinline__ void unpack8(const uint4& v, float (&f)[8]) {
 __device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
   return make_uint4(pack_bf16(f[0], f[1]), pack_bf16(f[2], f[3]), pack_bf16(f[4], f[5]), pack_bf16(f[6], f[7]));
 }
-
-__device__ __forceinline__ uint4 ld_nc_v4(const void* p) {
-  uint4 r;
-  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
-               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
-               : "l"(p));
-  return r;
+// |a| max |b| on packed bf16 pairs (exact).
+__device__ __forceinline__ uint32_t absmax_bf16x2(uint32_t a, uint32_t b) {
+  __nv_bfloat162 x = *reinterpret_cast<__nv_bfloat162*>(&a);
+  __nv_bfloat162 y = *reinterpret_cast<__nv_bfloat162*>(&b);
+  __nv_bfloat162 r = __hmax2(x, __habs2(y));
+  return *reinterpret_cast<uint32_t*>(&r);
 }
-__device__ __forceinline__ uint4 ld_v4(const void* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }
+// bf16(1 + s) for a packed pair: a correctly rounded bf16 add, equal to the
+// reference's fp32 add then bf16 rounding (src/ck_fused_patch.py:120).
+__device__ __forceinline__ uint32_t one_plus_bf16x2(uint32_t s) {
+  const __nv_bfloat162 one = __floats2bfloat162_rn(1.0f, 1.0f);
+  __nv_bfloat162 r = __hadd2(one, *reinterpret_cast<__nv_bfloat162*>(&s));
+  return *reinterpret_cast<uint32_t*>(&r);
+}
 
-// Two fp32 values -> two e4m3 codes (round to nearest even, saturating);
-// `lo` lands in the low byte.
+__device__ __forceinline__ uint4 ld_v4(const void* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }
+__device__ __forceinline__ uint4 lds_v4(const void* p) { return *reinterpret_cast<const uint4*>(p); }
+
+// Two fp32 values -> two e4m3 codes (RNE, saturating); `lo` lands in the low byte.
 __device__ __forceinline__ uint32_t cvt_e4m3x2(float lo, float hi) {
   uint16_t r;
   asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
   return r;
 }
-
-// 8 values -> 8 quantised bytes (IEEE divide by the scale).
-template <int QK>
-__device__ __forceinline__ uint2 quant8(const float (&f)[8], float scale) {
-  uint32_t b[8];
-  if constexpr (QK == kQuantInt8) {
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      float v = rintf(__fdiv_rn(f[j], scale));
-      v = fminf(fmaxf(v, -127.0f), 127.0f);
-      b[j] = static_cast<uint32_t>(static_cast<int>(v)) & 0xFFu;
-    }
-  } else {
-#pragma unroll
-    for (int j = 0; j < 8; j += 2) {
-      const float v0 = fminf(fmaxf(__fdiv_rn(f[j], scale), -448.0f), 448.0f);
-      const float v1 = fminf(fmaxf(__fdiv_rn(f[j + 1], scale), -448.0f), 448.0f);
-      const uint32_t p = cvt_e4m3x2(v0, v1);
-      b[j] = p & 0xFFu;
-      b[j + 1] = p >> 8;
-    }
-  }
-  return make_uint2(b[0] | (b[1] << 8) | (b[2] << 16) | (b[3] << 24), b[4] | (b[5] << 8) | (b[6] << 16) | (b[7] << 24));
+// Packed fp32 arithmetic with explicit round-to-nearest-even.  A packed multiply that
+// feeds a packed add can still be fused into one multiply-add by the assembler (observed:
+// h = t * s + b came out as fma(t, s, b) in a rare cancelling case), so every add whose
+// operand is a product uses the scalar IEEE add (__fadd_rn, never contracted) instead.
+__device__ __forceinline__ float2 mul2_rn(float2 a, float2 b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;"
+      : "=l"(d)
+      : "l"(*reinterpret_cast<uint64_t*>(&a)), "l"(*reinterpret_cast<uint64_t*>(&b)));
+  return *reinterpret_cast<float2*>(&d);
+}
+__device__ __forceinline__ float2 add2_rn(float2 a, float2 b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;"
+      : "=l"(d)
+      : "l"(*reinterpret_cast<uint64_t*>(&a)), "l"(*reinterpret_cast<uint64_t*>(&b)));
+  return *reinterpret_cast<float2*>(&d);
+}
+__device__ __forceinline__ float2 fma2_rn(float2 a, float2 b, float2 c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;"
+      : "=l"(d)
+      : "l"(*reinterpret_cast<uint64_t*>(&a)), "l"(*reinterpret_cast<uint64_t*>(&b)),
+        "l"(*reinterpret_cast<uint64_t*>(&c)));
+  return *reinterpret_cast<float2*>(&d);
 }
 
-template <int QK>
-__device__ __forceinline__ float scale_from_amax(float amax) {
-  return fmaxf(__fdiv_rn(amax, QMax<QK>::v), kScaleMin);
+__device__ __forceinline__ float2 bf2_to_f2(uint32_t u) {
+  return make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xFFFF0000u));
 }
+__device__ __forceinline__ uint32_t f2_to_bf2(float2 v) { return pack_bf16(v.x, v.y); }
 
-// Block geometry: rows of T threads packed into blocks of max(256, T) threads.
-template <int T>
-struct Geo {
-  static constexpr int kBlock = T >= 256 ? T : 256;
-  static constexpr int kRows = kBlock / T;
-  static constexpr int kWarps = T / 32;
+// Round-half-even to an integer through the fp32 adder: for |v| < 2^22 the low byte
+// of bits(v + 1.5 * 2^23) is rint(v) as a two's-complement int8.
+constexpr float kRoundMagic = 12582912.0f;
+
+// Per-row constants of the quantiser.
+struct QuantRow {
+  float scale;    // max(amax / qmax, 1e-12)
+  float2 c_lo;    // RN(RN(1 / scale) * (1 - 2^-21)), both lanes
+  float2 c_hi;    // RN(RN(1 / scale) * (1 + 2^-21)), both lanes
 };
 
-// Canonical row sum (see file comment).  `red` holds kWarps floats of this row.
+template <int QK>
+__device__ __forceinline__ QuantRow quant_row(float amax) {
+  QuantRow r;
+  r.scale = fmaxf(__fdiv_rn(amax, QMax<QK>::v), kScaleMin);
+  const float rcp = __fdiv_rn(1.0f, r.scale);
+  const float lo = __fmul_rn(rcp, 1.0f - 0x1p-21f), hi = __fmul_rn(rcp, 1.0f + 0x1p-21f);
+  r.c_lo = make_float2(lo, lo);
+  r.c_hi = make_float2(hi, hi);
+  return r;
+}
+
+// 8 values (4 pairs) -> 8 quantised bytes, bit-identical to cvt(RN(v / scale)) with an
+// IEEE divide.  Writing x = v / scale, a = RN(v * c_lo) and b = RN(v * c_hi) bracket
+// x within a relative 2^-21 - 2^-23 > 2^-23 of it on either side, so RN(x) lies
+// between a and b.  The 8-bit conversion (int8: round half to even; e4m3: RNE with
+// saturation) is monotone, so when a and b convert to the same code that code is
+// the one RN(x) converts to.  Otherwise (a rounding boundary lies within ~2^-21 of
+// x, probability ~2^-17 per value) the lane recomputes its eight values with the
+// IEEE divide.  int8 never needs the +-127 clamp: |x| <= 127 * (1 + 2^-23).
+template <int QK>
+__device__ __forceinline__ uint2 quant8(const float2 (&v)[4], const QuantRow& qr) {
+  uint32_t ca[4], cb[4];
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    const float2 a = mul2_rn(v[p], qr.c_lo);
+    const float2 b = mul2_rn(v[p], qr.c_hi);
+    if constexpr (QK == kQuantInt8) {
+      const float2 m = make_float2(kRoundMagic, kRoundMagic);
+      const float2 ra = add2_rn(a, m), rb = add2_rn(b, m);
+      ca[p] = __byte_perm(__float_as_uint(ra.x), __float_as_uint(ra.y), 0x0040);
+      cb[p] = __byte_perm(__float_as_uint(rb.x), __float_as_uint(rb.y), 0x0040);
+    } else {
+      ca[p] = cvt_e4m3x2(a.x, a.y);
+      cb[p] = cvt_e4m3x2(b.x, b.y);
+    }
+  }
+  uint32_t w0 = __byte_perm(ca[0], ca[1], 0x5410), w1 = __byte_perm(ca[2], ca[3], 0x5410);
+  const uint32_t u0 = __byte_perm(cb[0], cb[1], 0x5410), u1 = __byte_perm(cb[2], cb[3], 0x5410);
+  if ((w0 != u0) | (w1 != u1)) {
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      const float qx = __fdiv_rn(v[p].x, qr.scale), qy = __fdiv_rn(v[p].y, qr.scale);
+      if constexpr (QK == kQuantInt8)
+        ca[p] = __byte_perm(__float_as_uint(__fadd_rn(qx, kRoundMagic)), __float_as_uint(__fadd_rn(qy, kRoundMagic)),
+                            0x0040);
+      else
+        ca[p] = cvt_e4m3x2(qx, qy);
+    }
+    w0 = __byte_perm(ca[0], ca[1], 0x5410);
+    w1 = __byte_perm(ca[2], ca[3], 0x5410);
+  }
+  return make_uint2(w0, w1);
+}
+
+__device__ __forceinline__ void unpack_pairs(const uint4& u, float2 (&v)[4]) {
+  v[0] = bf2_to_f2(u.x);
+  v[1] = bf2_to_f2(u.y);
+  v[2] = bf2_to_f2(u.z);
+  v[3] = bf2_to_f2(u.w);
+}
+
+
+// ---------------------------------------------------------------- block reductions
+// The CTA is one row group of T threads; `red` holds T/32 floats.
 template <int T>
-__device__ __forceinline__ float row_sum(float v, float* red) {
+__device__ __forceinline__ float block_sum(float v, float* red) {
 #pragma unroll
   for (int off = 16; off >= 1; off >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xFFFFFFFFu, v, off));
   if constexpr (T == 32) {
     return v;
   } else {
-    const int w = (threadIdx.x % T) >> 5;
-    if ((threadIdx.x & 31) == 0) red[w] = v;
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
     __syncthreads();
     float t = red[0];
 #pragma unroll
     for (int i = 1; i < T / 32; ++i) t = __fadd_rn(t, red[i]);
-    __syncthreads();
     return t;
   }
 }
 
 template <int T>
-__device__ __forceinline__ float row_max(float v, float* red) {
+__device__ __forceinline__ float block_max(float v, float* red) {
 #pragma unroll
   for (int off = 16; off >= 1; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xFFFFFFFFu, v, off));
   if constexpr (T == 32) {
     return v;
   } else {
-    const int w = (threadIdx.x % T) >> 5;
-    if ((threadIdx.x & 31) == 0) red[w] = v;
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
     __syncthreads();
     float t = red[0];
 #pragma unroll
     for (int i = 1; i < T / 32; ++i) t = fmaxf(t, red[i]);
-    __syncthreads();
     return t;
   }
 }
@@ -154,9 +234,44 @@ __device__ __forceinline__ void atomic_max_nonneg(float* addr, float v) {
   atomicMax(reinterpret_cast<int*>(addr), __float_as_int(v));
 }
 
-// ---------------------------------------------------------------------------
-// per-token quantisation of a bf16 matrix (comfy-kitchen int8_linear input)
-// ---------------------------------------------------------------------------
+// ---------------------------------------------------------------- row ring
+// Shared-memory layout of every row kernel: mbarriers, reduction scratch, then
+// `stages` slots of `slot_bytes` (1024-byte aligned).
+struct RingGeom {
+  int stages;          // slots in the ring (>= 2)
+  uint32_t slot_bytes; // bytes of one slot (one row, or gate row + up row)
+  uint32_t part_bytes; // bytes of one bulk copy (a row of one operand)
+  int parts;           // bulk copies per slot (1, or 2 for gate + up)
+};
+constexpr int kRingHeader = 1024;   // barriers (<= 16 x 8 B), reductions (2 x 16 floats), flags
+constexpr int kMaxStages = 16;
+
+struct RingState {
+  uint64_t* full;
+  float* red_sum;
+  float* red_max;
+  uint8_t* slots;
+};
+
+__device__ __forceinline__ RingState ring_state(uint8_t* smem) {
+  RingState r;
+  r.full = reinterpret_cast<uint64_t*>(smem);
+  r.red_sum = reinterpret_cast<float*>(smem + 8 * kMaxStages);
+  r.red_max = r.red_sum + 16;
+  r.slots = smem + kRingHeader;
+  return r;
+}
+
+// Issue the bulk copies of row `row` into slot `st` (one thread).
+__device__ __forceinline__ void ring_issue(const RingState& rs, const RingGeom& g, int st, const void* src0,
+                                           const void* src1, uint64_t policy) {
+  uint8_t* dst = rs.slots + static_cast<size_t>(st) * g.slot_bytes;
+  mbar_arrive_expect_tx(&rs.full[st], g.part_bytes * static_cast<uint32_t>(g.parts));
+  bulk_load(dst, src0, g.part_bytes, &rs.full[st], policy);
+  if (g.parts == 2) bulk_load(dst + g.part_bytes, src1, g.part_bytes, &rs.full[st], policy);
+}
+
+// ---------------------------------------------------------------- kernel arguments
 struct QuantRowsArgs {
   const __nv_bfloat16* x;
   int64_t ld_x;
@@ -167,45 +282,6 @@ struct QuantRowsArgs {
   int D;
 };
 
-template <int T, int QK>
-__global__ void __launch_bounds__(Geo<T>::kBlock) quant_rows_kernel(const QuantRowsArgs a) {
-  __shared__ float red[Geo<T>::kRows][Geo<T>::kWarps];
-  const int tid = threadIdx.x % T;
-  const int rloc = threadIdx.x / T;
-  const int64_t row = static_cast<int64_t>(blockIdx.x) * Geo<T>::kRows + rloc;
-  const bool active = row < a.S;
-  const int nvec = a.D >> 3;
-  const __nv_bfloat16* xr = a.x + (active ? row : 0) * a.ld_x;
-  uint4 xv[MAX_VEC];
-  float amax = 0.f;
-#pragma unroll
-  for (int i = 0; i < MAX_VEC; ++i) {
-    const int c = tid + T * i;
-    xv[i] = (active && c < nvec) ? ld_nc_v4(xr + 8 * c) : make_uint4(0, 0, 0, 0);
-    float f[8];
-    unpack8(xv[i], f);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(f[j]));
-  }
-  amax = row_max<T>(amax, red[rloc]);
-  const float scale = scale_from_amax<QK>(amax);
-  if (!active) return;
-  if (tid == 0) a.q_scale[row] = scale;
-  uint8_t* qr = static_cast<uint8_t*>(a.q) + row * a.ld_q;
-#pragma unroll
-  for (int i = 0; i < MAX_VEC; ++i) {
-    const int c = tid + T * i;
-    if (c < nvec) {
-      float f[8];
-      unpack8(xv[i], f);
-      *reinterpret_cast<uint2*>(qr + 8 * c) = quant8<QK>(f, scale);
-    }
-  }
-}
-
-// ---------------------------------------------------------------------------
-// RMSNorm + adaLN modulation (+ per-token quant, or tensorwise phase A)
-// ---------------------------------------------------------------------------
 struct RmsArgs {
   const __nv_bfloat16* x;
   int64_t ld_x;
@@ -220,7 +296,7 @@ struct RmsArgs {
   void* q;                       // per-token mode: [S, D] codes
   int64_t ld_q;
   float* q_scale;                // per-token mode: [S]
-  __nv_bfloat16* h;              // optional [S, D] bf16 h
+  __nv_bfloat16* h;              // optional [S, D] bf16 h (required in tensorwise mode)
   int64_t ld_h;
   __nv_bfloat16* res;            // optional [S, D] bf16 h + x
   int64_t ld_res;
@@ -229,102 +305,6 @@ struct RmsArgs {
   int D;
 };
 
-// MODE 0/1: per-token quant (int8 / fp8); MODE 2: tensorwise phase A.
-template <int T, int MODE>
-__global__ void __launch_bounds__(Geo<T>::kBlock) rms_mod_kernel(const RmsArgs a) {
-  __shared__ float red[Geo<T>::kRows][Geo<T>::kWarps];
-  const int tid = threadIdx.x % T;
-  const int rloc = threadIdx.x / T;
-  const int64_t row = static_cast<int64_t>(blockIdx.x) * Geo<T>::kRows + rloc;
-  const bool active = row < a.S;
-  const int nvec = a.D >> 3;
-  const int64_t r = active ? row : 0;
-  const __nv_bfloat16* xr = a.x + r * a.ld_x;
-
-  uint4 xv[MAX_VEC];
-  float ss = 0.f;
-#pragma unroll
-  for (int i = 0; i < MAX_VEC; ++i) {
-    const int c = tid + T * i;
-    xv[i] = (active && c < nvec) ? ld_nc_v4(xr + 8 * c) : make_uint4(0, 0, 0, 0);
-  }
-#pragma unroll
-  for (int i = 0; i < MAX_VEC; ++i) {
-    float f[8];
-    unpack8(xv[i], f);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) ss = __fmaf_rn(f[j], f[j], ss);
-  }
-  ss = row_sum<T>(ss, red[rloc]);
-  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(a.D)), a.eps)));
-
-  const int64_t m = a.mod_index ? static_cast<int64_t>(a.mod_index[r]) : r / a.rows_per_mod;
-  const __nv_bfloat16* shr = a.shift + m * a.ld_mod;
-  const __nv_bfloat16* scr = a.scale + m * a.ld_mod;
-  float amax = 0.f;
-#pragma unroll
-  for (int i = 0; i < MAX_VEC; ++i) {
-    const int c = tid + T * i;
-    if (active && c < nvec) {
-      float x[8], b[8], s[8], w[8], h[8];
-      unpack8(xv[i], x);
-      unpack8(ld_v4(shr + 8 * c), b);
-      unpack8(ld_v4(scr + 8 * c), s);
-      if (a.w) unpack8(ld_v4(a.w + 8 * c), w);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float sj = a.scale_is_multiplier ? s[j] : round_bf16(__fadd_rn(1.0f, s[j]));
-        float t = __fmul_rn(x[j], inv);
-        if (a.w) t = __fmul_rn(t, w[j]);
-        t = __fmul_rn(t, sj);
-        h[j] = __fadd_rn(t, b[j]);
-      }
-      if (a.res) {
-        float rs[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) rs[j] = __fadd_rn(h[j], x[j]);
-        *reinterpret_cast<uint4*>(a.res + row * a.ld_res + 8 * c) = pack8(rs);
-      }
-      if constexpr (MODE == 2) {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(h[j]));
-      }
-      xv[i] = pack8(h);   // h rounded to bf16 replaces x in registers
-      if constexpr (MODE != 2) {
-        float hb[8];
-        unpack8(xv[i], hb);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(hb[j]));
-      }
-      if (a.h) *reinterpret_cast<uint4*>(a.h + row * a.ld_h + 8 * c) = xv[i];
-    }
-  }
-  if constexpr (MODE == 2) {
-#pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, off));
-    if ((threadIdx.x & 31) == 0 && amax > 0.f) atomic_max_nonneg(a.amax, amax);
-  } else {
-    constexpr int QK = MODE;
-    amax = row_max<T>(amax, red[rloc]);
-    const float scale = scale_from_amax<QK>(amax);
-    if (!active) return;
-    if (tid == 0) a.q_scale[row] = scale;
-    uint8_t* qr = static_cast<uint8_t*>(a.q) + row * a.ld_q;
-#pragma unroll
-    for (int i = 0; i < MAX_VEC; ++i) {
-      const int c = tid + T * i;
-      if (c < nvec) {
-        float f[8];
-        unpack8(xv[i], f);
-        *reinterpret_cast<uint2*>(qr + 8 * c) = quant8<QK>(f, scale);
-      }
-    }
-  }
-}
-
-// ---------------------------------------------------------------------------
-// SwiGLU (+ per-token quant, or tensorwise phase A)
-// ---------------------------------------------------------------------------
 struct SwigluArgs {
   const __nv_bfloat16* gate;   // [M, F] with row stride ld_in
   const __nv_bfloat16* up;     // [M, F] with row stride ld_in
@@ -332,84 +312,241 @@ struct SwigluArgs {
   void* q;
   int64_t ld_q;
   float* q_scale;
-  __nv_bfloat16* act;          // optional [M, F] bf16 act
+  __nv_bfloat16* act;          // optional [M, F] bf16 act (required in tensorwise mode)
   int64_t ld_act;
   float* amax;                 // tensorwise mode
   int64_t M;
   int F;
 };
 
-// act = (g * sigmoid(g)) * u, sigmoid(g) = 1 / (1 + e^-g)
-__device__ __forceinline__ float silu_mul(float g, float u) {
-  const float sig = __frcp_rn(__fadd_rn(1.0f, __expf(-g)));
-  return __fmul_rn(__fmul_rn(g, sig), u);
+// ---------------------------------------------------------------- common loop
+// Runs `body(row, slot_ptr, ring)` for rows blockIdx.x, blockIdx.x + gridDim.x, ...
+// with the ring kept `stages - 1` rows ahead.  `src(row, part)` gives the
+// global address of a row operand.  Returns after draining in-flight copies.
+template <int T, typename Src, typename Body>
+__device__ __forceinline__ void row_loop(uint8_t* smem, const RingGeom& g, int64_t nrows, Src src, Body body) {
+  RingState rs = ring_state(smem);
+  const uint64_t policy = policy_evict_first();
+  const int64_t G = gridDim.x;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < g.stages; ++i) mbar_init(&rs.full[i], 1);
+    fence_mbarrier_init();
+  }
+  __syncthreads();
+  int64_t issued = 0;   // meaningful in thread 0 only
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < g.stages; ++i) {
+      const int64_t r = blockIdx.x + i * G;
+      if (r >= nrows) break;
+      ring_issue(rs, g, i, src(r, 0), src(r, 1), policy);
+      ++issued;
+    }
+  }
+  int64_t k = 0;
+  for (int64_t row = blockIdx.x; row < nrows; row += G, ++k) {
+    const int st = static_cast<int>(k % g.stages);
+    const uint32_t ph = static_cast<uint32_t>((k / g.stages) & 1);
+    const bool ok = mbar_wait(&rs.full[st], ph, kStatusTimeoutProducer);
+    if (__syncthreads_or(!ok)) break;
+    // every thread is past row k-1: refill its slot with row k-1+stages
+    if (threadIdx.x == 0 && k > 0) {
+      const int64_t r = row - G + static_cast<int64_t>(g.stages) * G;
+      if (r < nrows) {
+        ring_issue(rs, g, static_cast<int>((k - 1) % g.stages), src(r, 0), src(r, 1), policy);
+        ++issued;
+      }
+    }
+    body(row, rs.slots + static_cast<size_t>(st) * g.slot_bytes, rs);
+  }
+  // teardown: copies still in flight (only after an abort) must land before exit
+  if (threadIdx.x == 0) {
+    for (int64_t n = k; n < issued; ++n)
+      if (!mbar_wait(&rs.full[n % g.stages], static_cast<uint32_t>((n / g.stages) & 1), kStatusTimeoutDrain)) break;
+  }
+}
+
+// ---------------------------------------------------------------- shared pieces
+// Quantise the row held (as bf16) in `src` (shared memory) and store q.
+template <int T, int QK>
+__device__ __forceinline__ void quant_row_store(const uint8_t* src, int nvec, const QuantRow& qr, uint8_t* qrow) {
+  for (int c = threadIdx.x; c < nvec; c += T) {
+    float2 v[4];
+    unpack_pairs(lds_v4(src + 16 * c), v);
+    *reinterpret_cast<uint2*>(qrow + 8 * c) = quant8<QK>(v, qr);
+  }
+}
+
+__device__ __forceinline__ uint32_t absmax4(uint32_t m2, const uint4& u) {
+  m2 = absmax_bf16x2(m2, u.x);
+  m2 = absmax_bf16x2(m2, u.y);
+  m2 = absmax_bf16x2(m2, u.z);
+  return absmax_bf16x2(m2, u.w);
+}
+
+// Generic-proxy writes to a ring slot must be ordered before the bulk copy that
+// later refills it.
+__device__ __forceinline__ void slot_written() { fence_proxy_async_smem(); }
+
+// ---------------------------------------------------------------- per-token quant
+template <int T, int QK>
+__global__ void __launch_bounds__(T) quant_rows_kernel(const QuantRowsArgs a, const RingGeom g) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const int nvec = a.D >> 3;
+  auto src = [&](int64_t r, int) -> const void* { return a.x + r * a.ld_x; };
+  row_loop<T>(smem, g, a.S, src, [&](int64_t row, const uint8_t* slot, const RingState& rs) {
+    uint32_t m2 = 0;
+    for (int c = threadIdx.x; c < nvec; c += T) m2 = absmax4(m2, lds_v4(slot + 16 * c));
+    const float amax = block_max<T>(fmaxf(bf_lo(m2), bf_hi(m2)), rs.red_max);
+    const QuantRow qr = quant_row<QK>(amax);
+    if (threadIdx.x == 0) a.q_scale[row] = qr.scale;
+    quant_row_store<T, QK>(slot, nvec, qr, static_cast<uint8_t*>(a.q) + row * a.ld_q);
+  });
+}
+
+// ---------------------------------------------------------------- RMSNorm + modulation
+// Sum of squares: each thread keeps two fp32 accumulators, one for the even and one
+// for the odd element of every bf16 pair, adds its vectors' squares in vector order
+// with a packed FMA, then combines them as (even + odd) before the row reduction.
+template <int T, int MODE>
+__global__ void __launch_bounds__(T) rms_mod_kernel(const RmsArgs a, const RingGeom g) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const int nvec = a.D >> 3;
+  const float fD = static_cast<float>(a.D);
+  auto src = [&](int64_t r, int) -> const void* { return a.x + r * a.ld_x; };
+  row_loop<T>(smem, g, a.S, src, [&](int64_t row, uint8_t* slot, const RingState& rs) {
+    // pass 1: sum of squares in the canonical order
+    float2 acc = make_float2(0.f, 0.f);
+    for (int c = threadIdx.x; c < nvec; c += T) {
+      float2 v[4];
+      unpack_pairs(lds_v4(slot + 16 * c), v);
+#pragma unroll
+      for (int p = 0; p < 4; ++p) acc = fma2_rn(v[p], v[p], acc);
+    }
+    const float ss = block_sum<T>(__fadd_rn(acc.x, acc.y), rs.red_sum);
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, fD), a.eps)));
+    const float2 inv2 = make_float2(inv, inv);
+
+    const int64_t m = a.mod_index ? static_cast<int64_t>(__ldg(a.mod_index + row)) : row / a.rows_per_mod;
+    const __nv_bfloat16* shr = a.shift + m * a.ld_mod;
+    const __nv_bfloat16* scr = a.scale + m * a.ld_mod;
+
+    // pass 2: h (written back over x in the slot), optional res / h stores, amax
+    uint32_t m2 = 0;
+    float amax32 = 0.f;
+    for (int c = threadIdx.x; c < nvec; c += T) {
+      const uint4 xu = lds_v4(slot + 16 * c);
+      uint4 su = ld_v4(scr + 8 * c);
+      const uint4 bu = ld_v4(shr + 8 * c);
+      if (!a.scale_is_multiplier)
+        su = make_uint4(one_plus_bf16x2(su.x), one_plus_bf16x2(su.y), one_plus_bf16x2(su.z), one_plus_bf16x2(su.w));
+      float2 x[4], sv[4], bv[4], h[4];
+      unpack_pairs(xu, x);
+      unpack_pairs(su, sv);
+      unpack_pairs(bu, bv);
+      float2 prod[4];
+      if (a.w) {
+        float2 wv[4];
+        unpack_pairs(ld_v4(a.w + 8 * c), wv);
+#pragma unroll
+        for (int p = 0; p < 4; ++p) prod[p] = mul2_rn(mul2_rn(mul2_rn(x[p], inv2), wv[p]), sv[p]);
+      } else {
+#pragma unroll
+        for (int p = 0; p < 4; ++p) prod[p] = mul2_rn(mul2_rn(x[p], inv2), sv[p]);
+      }
+#pragma unroll
+      for (int p = 0; p < 4; ++p) h[p] = make_float2(__fadd_rn(prod[p].x, bv[p].x), __fadd_rn(prod[p].y, bv[p].y));
+      if (a.res) {
+        uint4 ru;
+        ru.x = f2_to_bf2(add2_rn(h[0], x[0]));
+        ru.y = f2_to_bf2(add2_rn(h[1], x[1]));
+        ru.z = f2_to_bf2(add2_rn(h[2], x[2]));
+        ru.w = f2_to_bf2(add2_rn(h[3], x[3]));
+        *reinterpret_cast<uint4*>(a.res + row * a.ld_res + 8 * c) = ru;
+      }
+      if constexpr (MODE == kModeTensorwise) {
+#pragma unroll
+        for (int p = 0; p < 4; ++p) amax32 = fmaxf(amax32, fmaxf(fabsf(h[p].x), fabsf(h[p].y)));
+      }
+      const uint4 hu = make_uint4(f2_to_bf2(h[0]), f2_to_bf2(h[1]), f2_to_bf2(h[2]), f2_to_bf2(h[3]));
+      m2 = absmax4(m2, hu);
+      *reinterpret_cast<uint4*>(slot + 16 * c) = hu;
+      if (a.h) *reinterpret_cast<uint4*>(a.h + row * a.ld_h + 8 * c) = hu;
+    }
+    slot_written();
+    if constexpr (MODE == kModeTensorwise) {
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) amax32 = fmaxf(amax32, __shfl_xor_sync(0xFFFFFFFFu, amax32, off));
+      if ((threadIdx.x & 31) == 0 && amax32 > 0.f) atomic_max_nonneg(a.amax, amax32);
+    } else {
+      constexpr int QK = MODE;
+      const float amax = block_max<T>(fmaxf(bf_lo(m2), bf_hi(m2)), rs.red_max);   // barrier: h complete
+      const QuantRow qr = quant_row<QK>(amax);
+      if (threadIdx.x == 0) a.q_scale[row] = qr.scale;
+      quant_row_store<T, QK>(slot, nvec, qr, static_cast<uint8_t*>(a.q) + row * a.ld_q);
+    }
+  });
+}
+
+// ---------------------------------------------------------------- SwiGLU
+// act = (g * sigmoid(g)) * u with sigmoid(g) = 1 / (1 + e^-g); e^-g and the reciprocal
+// use the fast hardware approximations (act is compared with the oracle within one
+// bf16 ulp).
+// Approximate reciprocal (max 1 ulp), subnormal results kept (no flush to zero).
+__device__ __forceinline__ float rcp_approx(float x) {
+  float r;
+  asm("rcp.approx.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+
+__device__ __forceinline__ float2 silu_mul2(float2 g, float2 u) {
+  const float2 e = make_float2(__expf(-g.x), __expf(-g.y));
+  const float2 d = add2_rn(make_float2(1.0f, 1.0f), e);
+  const float2 r = make_float2(rcp_approx(d.x), rcp_approx(d.y));
+  return mul2_rn(mul2_rn(g, r), u);
 }
 
 template <int T, int MODE>
-__global__ void __launch_bounds__(Geo<T>::kBlock) swiglu_kernel(const SwigluArgs a) {
-  __shared__ float red[Geo<T>::kRows][Geo<T>::kWarps];
-  const int tid = threadIdx.x % T;
-  const int rloc = threadIdx.x / T;
-  const int64_t row = static_cast<int64_t>(blockIdx.x) * Geo<T>::kRows + rloc;
-  const bool active = row < a.M;
+__global__ void __launch_bounds__(T) swiglu_kernel(const SwigluArgs a, const RingGeom g) {
+  extern __shared__ __align__(1024) uint8_t smem[];
   const int nvec = a.F >> 3;
-  const int64_t r = active ? row : 0;
-  const __nv_bfloat16* gr = a.gate + r * a.ld_in;
-  const __nv_bfloat16* ur = a.up + r * a.ld_in;
-
-  uint4 av[MAX_VEC];
-  float amax = 0.f;
+  auto src = [&](int64_t r, int part) -> const void* { return (part ? a.up : a.gate) + r * a.ld_in; };
+  row_loop<T>(smem, g, a.M, src, [&](int64_t row, uint8_t* slot, const RingState& rs) {
+    const uint8_t* up = slot + g.part_bytes;
+    uint32_t m2 = 0;
+    float amax32 = 0.f;
+    for (int c = threadIdx.x; c < nvec; c += T) {
+      float2 gv[4], uv[4], act[4];
+      unpack_pairs(lds_v4(slot + 16 * c), gv);
+      unpack_pairs(lds_v4(up + 16 * c), uv);
 #pragma unroll
-  for (int i = 0; i < MAX_VEC; ++i) {
-    const int c = tid + T * i;
-    if (active && c < nvec) {
-      float g[8], u[8], act[8];
-      unpack8(ld_nc_v4(gr + 8 * c), g);
-      unpack8(ld_nc_v4(ur + 8 * c), u);
+      for (int p = 0; p < 4; ++p) act[p] = silu_mul2(gv[p], uv[p]);
+      if constexpr (MODE == kModeTensorwise) {
 #pragma unroll
-      for (int j = 0; j < 8; ++j) act[j] = silu_mul(g[j], u[j]);
-      if constexpr (MODE == 2) {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(act[j]));
+        for (int p = 0; p < 4; ++p) amax32 = fmaxf(amax32, fmaxf(fabsf(act[p].x), fabsf(act[p].y)));
       }
-      av[i] = pack8(act);
-      if constexpr (MODE != 2) {
-        float ab[8];
-        unpack8(av[i], ab);
+      const uint4 au = make_uint4(f2_to_bf2(act[0]), f2_to_bf2(act[1]), f2_to_bf2(act[2]), f2_to_bf2(act[3]));
+      m2 = absmax4(m2, au);
+      *reinterpret_cast<uint4*>(slot + 16 * c) = au;   // act replaces the gate row
+      if (a.act) *reinterpret_cast<uint4*>(a.act + row * a.ld_act + 8 * c) = au;
+    }
+    slot_written();
+    if constexpr (MODE == kModeTensorwise) {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(ab[j]));
-      }
-      if (a.act) *reinterpret_cast<uint4*>(a.act + row * a.ld_act + 8 * c) = av[i];
+      for (int off = 16; off >= 1; off >>= 1) amax32 = fmaxf(amax32, __shfl_xor_sync(0xFFFFFFFFu, amax32, off));
+      if ((threadIdx.x & 31) == 0 && amax32 > 0.f) atomic_max_nonneg(a.amax, amax32);
     } else {
-      av[i] = make_uint4(0, 0, 0, 0);
+      constexpr int QK = MODE;
+      const float amax = block_max<T>(fmaxf(bf_lo(m2), bf_hi(m2)), rs.red_max);   // barrier: act complete
+      const QuantRow qr = quant_row<QK>(amax);
+      if (threadIdx.x == 0) a.q_scale[row] = qr.scale;
+      quant_row_store<T, QK>(slot, nvec, qr, static_cast<uint8_t*>(a.q) + row * a.ld_q);
     }
-  }
-  if constexpr (MODE == 2) {
-#pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, off));
-    if ((threadIdx.x & 31) == 0 && amax > 0.f) atomic_max_nonneg(a.amax, amax);
-  } else {
-    constexpr int QK = MODE;
-    amax = row_max<T>(amax, red[rloc]);
-    const float scale = scale_from_amax<QK>(amax);
-    if (!active) return;
-    if (tid == 0) a.q_scale[row] = scale;
-    uint8_t* qr = static_cast<uint8_t*>(a.q) + row * a.ld_q;
-#pragma unroll
-    for (int i = 0; i < MAX_VEC; ++i) {
-      const int c = tid + T * i;
-      if (c < nvec) {
-        float f[8];
-        unpack8(av[i], f);
-        *reinterpret_cast<uint2*>(qr + 8 * c) = quant8<QK>(f, scale);
-      }
-    }
-  }
+  });
 }
 
 // ---------------------------------------------------------------------------
-// tensorwise phase B: q = cvt(clamp(h / max(amax / qmax, 1e-12))) from the
-// device amax (src/ck_fused_mod_norm_quant.py:92-111); also writes the scale.
+// tensorwise phase B: q = cvt(RN(h / max(amax / qmax, 1e-12))) from the device amax
+// (src/ck_fused_mod_norm_quant.py:92-111); also writes the scale.
 // ---------------------------------------------------------------------------
 struct QuantGivenArgs {
   const __nv_bfloat16* h;
@@ -424,17 +561,17 @@ struct QuantGivenArgs {
 
 template <int QK>
 __global__ void __launch_bounds__(256) quant_given_amax_kernel(const QuantGivenArgs a) {
-  const float scale = scale_from_amax<QK>(*a.amax);
-  if (blockIdx.x == 0 && threadIdx.x == 0 && a.scale_out) *a.scale_out = scale;
+  const QuantRow qr = quant_row<QK>(*a.amax);
+  if (blockIdx.x == 0 && threadIdx.x == 0 && a.scale_out) *a.scale_out = qr.scale;
   const int nvec = a.D >> 3;
   const int64_t total = a.S * nvec;
   for (int64_t v = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; v < total;
        v += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int64_t row = v / nvec;
     const int c = static_cast<int>(v - row * nvec);
-    float f[8];
-    unpack8(ld_nc_v4(a.h + row * a.ld_h + 8 * c), f);
-    *reinterpret_cast<uint2*>(static_cast<uint8_t*>(a.q) + row * a.ld_q + 8 * c) = quant8<QK>(f, scale);
+    float2 f[4];
+    unpack_pairs(ld_v4(a.h + row * a.ld_h + 8 * c), f);
+    *reinterpret_cast<uint2*>(static_cast<uint8_t*>(a.q) + row * a.ld_q + 8 * c) = quant8<QK>(f, qr);
   }
 }
 

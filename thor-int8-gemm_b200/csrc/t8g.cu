@@ -7,6 +7,7 @@
 #include <stdarg.h>
 #include <stdint.h>
 #include <stdio.h>
+#include <stdlib.h>
 
 #include <mutex>
 
@@ -111,6 +112,28 @@ int encode_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t
 bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
 
 // ----------------------------------------------------------------- GEMM
+// 2-SM launch: clusters of two CTAs, grid = 2 x min(tiles, SMs / 2).
+template <int IN, int OUT>
+int launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
+                     const t8g::gemm::Args& args, int dev, int sms, cudaStream_t stream) {
+  using namespace t8g::gemm;
+  static bool attr_done[kMaxDevices] = {};
+  auto kern = gemm_dequant_pair_kernel<IN, OUT>;
+  int rc = ensure_smem_attr(kern, dev, P_SMEM_BYTES, attr_done);
+  if (rc) return rc;
+  const int64_t tiles = static_cast<int64_t>((args.M + P_BM - 1) / P_BM) * ((args.N + BN - 1) / BN);
+  const int64_t pairs = tiles < sms / 2 ? tiles : sms / 2;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs), 1, 1);
+  cfg.blockDim = dim3(NUM_THREADS, 1, 1);
+  cfg.dynamicSmemBytes = P_SMEM_BYTES;
+  cfg.stream = stream;
+  cfg.attrs = nullptr;   // the kernel declares its cluster shape (2, 1, 1)
+  cfg.numAttrs = 0;
+  T8G_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kern, ta, tb, to, args), "gemm pair launch");
+  return T8G_OK;
+}
+
 template <int IN, int OUT>
 int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to, const t8g::gemm::Args& args,
                 int dev, int sms, cudaStream_t stream) {
@@ -156,11 +179,15 @@ int gemm_entry(int in_kind, const void* x, const void* w, const float* x_scale, 
   int rc = current_device(&dev, &info);
   if (rc) return rc;
 
+  // The 2-SM kernel (CTA pairs, 256-row tiles) runs whenever there is more than one
+  // 128-row block; T8G_GEMM_SM=1 in the environment forces the 1-SM kernel.
+  const char* sm_env = getenv("T8G_GEMM_SM");
+  const bool pair = M > BM && !(sm_env && sm_env[0] == '1');
   const CUtensorMapDataType in_dt = CU_TENSOR_MAP_DATA_TYPE_UINT8;
   CUtensorMap ta, tb, to;
   rc = encode_2d(&ta, in_dt, x, K, M, ld_x, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
-  rc = encode_2d(&tb, in_dt, w, K, N, ld_w, BK, BN, CU_TENSOR_MAP_SWIZZLE_128B);
+  rc = encode_2d(&tb, in_dt, w, K, N, ld_w, BK, pair ? P_ROWS : BN, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   const CUtensorMapDataType out_dt = out_dtype == T8G_OUT_BF16  ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                      : out_dtype == T8G_OUT_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
@@ -179,6 +206,20 @@ int gemm_entry(int in_kind, const void* x, const void* w, const float* x_scale, 
   args.N = static_cast<int>(N);
   args.K = static_cast<int>(K);
   cudaStream_t st = static_cast<cudaStream_t>(stream_);
+  if (pair) {
+    if (in_kind == kInI8) {
+      switch (out_dtype) {
+        case T8G_OUT_BF16: return launch_gemm_pair<kInI8, kOutBF16>(ta, tb, to, args, dev, info.sms, st);
+        case T8G_OUT_F16: return launch_gemm_pair<kInI8, kOutF16>(ta, tb, to, args, dev, info.sms, st);
+        default: return launch_gemm_pair<kInI8, kOutF32>(ta, tb, to, args, dev, info.sms, st);
+      }
+    }
+    switch (out_dtype) {
+      case T8G_OUT_BF16: return launch_gemm_pair<kInE4M3, kOutBF16>(ta, tb, to, args, dev, info.sms, st);
+      case T8G_OUT_F16: return launch_gemm_pair<kInE4M3, kOutF16>(ta, tb, to, args, dev, info.sms, st);
+      default: return launch_gemm_pair<kInE4M3, kOutF32>(ta, tb, to, args, dev, info.sms, st);
+    }
+  }
   if (in_kind == kInI8) {
     switch (out_dtype) {
       case T8G_OUT_BF16: return launch_gemm<kInI8, kOutBF16>(ta, tb, to, args, dev, info.sms, st);
@@ -194,19 +235,36 @@ int gemm_entry(int in_kind, const void* x, const void* w, const float* x_scale, 
 }
 
 // ----------------------------------------------------------------- row kernels
-// Threads per row: the smallest power of two in [32, 512] with at most MAX_VEC
-// 16-byte vectors per thread (the oracle restates this rule).
+// Threads per row: the smallest power of two in [32, 512] that leaves at most
+// kFastVec 16-byte vectors per thread, else 512 (the oracle restates this rule).
 int row_threads(int64_t D) {
   const int64_t nvec = (D + 7) / 8;
   int t = 32;
-  while (t < 512 && (nvec + t - 1) / t > t8g::rows::MAX_VEC) t *= 2;
-  return (nvec + t - 1) / t > t8g::rows::MAX_VEC ? -1 : t;
+  while (t < 512 && (nvec + t - 1) / t > t8g::rows::kFastVec) t *= 2;
+  return t;
 }
 
-int check_row_shape(const char* what, int64_t S, int64_t D, int quant_kind) {
+// Ring geometry of a row kernel: `parts` operand rows of D bf16 per slot.
+t8g::rows::RingGeom ring_geom(int64_t D, int parts) {
+  t8g::rows::RingGeom g;
+  g.parts = parts;
+  g.part_bytes = static_cast<uint32_t>(D * 2);
+  g.slot_bytes = (static_cast<uint32_t>(parts) * g.part_bytes + 127u) & ~127u;
+  g.stages = g.slot_bytes <= 12288 ? 4 : g.slot_bytes <= 32768 ? 3 : 2;
+  return g;
+}
+
+size_t ring_smem(const t8g::rows::RingGeom& g) {
+  return t8g::rows::kRingHeader + static_cast<size_t>(g.stages) * g.slot_bytes;
+}
+
+constexpr size_t kRowSmemLimit = 200 * 1024;
+
+int check_row_shape(const char* what, int64_t S, int64_t D, int quant_kind, int parts) {
   if (S < 0 || D < 0) return fail(T8G_ERR_INVALID_ARGUMENT, "%s: negative size", what);
   if (D % 8) return fail(T8G_ERR_INVALID_ARGUMENT, "%s: row length %lld is not a multiple of 8", what, (long long)D);
-  if (row_threads(D) < 0) return fail(T8G_ERR_UNSUPPORTED, "%s: row length %lld exceeds 49152", what, (long long)D);
+  const int64_t dmax = parts == 1 ? 49152 : 24576;
+  if (D > dmax) return fail(T8G_ERR_UNSUPPORTED, "%s: row length %lld exceeds %lld", what, (long long)D, (long long)dmax);
   if (quant_kind != T8G_QUANT_INT8 && quant_kind != T8G_QUANT_FP8_E4M3)
     return fail(T8G_ERR_INVALID_ARGUMENT, "%s: unknown quant_kind %d", what, quant_kind);
   if (S >= (int64_t(1) << 40)) return fail(T8G_ERR_UNSUPPORTED, "%s: too many rows", what);
@@ -227,23 +285,60 @@ int check_q(const void* q, int64_t ld_q, int64_t D) {
   return T8G_OK;
 }
 
-template <int T>
-unsigned row_grid(int64_t S) {
-  return static_cast<unsigned>((S + t8g::rows::Geo<T>::kRows - 1) / t8g::rows::Geo<T>::kRows);
+// Launch a persistent row kernel: grid = min(rows, SMs x resident CTAs).
+template <typename K, typename A>
+int launch_rows(K kern, int T, const A& args, const t8g::rows::RingGeom& g, int64_t rows, int dev, int sms,
+                cudaStream_t st, const char* what) {
+  const size_t smem = ring_smem(g);
+  if (smem > kRowSmemLimit) return fail(T8G_ERR_UNSUPPORTED, "%s: row too long for the shared-memory ring", what);
+  static std::mutex mu;
+  static const void* attr_done[kMaxDevices][64] = {};
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    bool done = false;
+    int slot = 0;
+    for (; slot < 64 && attr_done[dev][slot]; ++slot)
+      if (attr_done[dev][slot] == reinterpret_cast<const void*>(kern)) { done = true; break; }
+    if (!done) {
+      T8G_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kRowSmemLimit),
+                     "cudaFuncSetAttribute(row kernel)");
+      if (slot < 64) attr_done[dev][slot] = reinterpret_cast<const void*>(kern);
+    }
+  }
+  int per_sm = 0;
+  T8G_CHECK_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, T, smem), "occupancy query");
+  if (per_sm < 1) per_sm = 1;
+  const int64_t cap = static_cast<int64_t>(sms) * per_sm;
+  const unsigned grid = static_cast<unsigned>(rows < cap ? rows : cap);
+  kern<<<grid, T, smem, st>>>(args, g);
+  T8G_CHECK_CUDA(cudaGetLastError(), what);
+  return T8G_OK;
 }
 
-#define T8G_DISPATCH_T(t, CALL)                 \
-  switch (t) {                                  \
-    case 32: { constexpr int T = 32; CALL; break; }   \
-    case 64: { constexpr int T = 64; CALL; break; }   \
-    case 128: { constexpr int T = 128; CALL; break; } \
-    case 256: { constexpr int T = 256; CALL; break; } \
-    default: { constexpr int T = 512; CALL; break; }  \
+#define T8G_DISPATCH_T(t, CALL)                        \
+  switch (t) {                                         \
+    case 32: { constexpr int T = 32; CALL; break; }    \
+    case 64: { constexpr int T = 64; CALL; break; }    \
+    case 128: { constexpr int T = 128; CALL; break; }  \
+    case 256: { constexpr int T = 256; CALL; break; }  \
+    default: { constexpr int T = 512; CALL; break; }   \
   }
 
 int launch_checked(const char* what) {
   T8G_CHECK_CUDA(cudaGetLastError(), what);
   return T8G_OK;
+}
+
+int launch_quant_given(const t8g::rows::QuantGivenArgs& b, int quant_kind, int sms, cudaStream_t st) {
+  using namespace t8g::rows;
+  const int64_t vecs = b.S * (b.D / 8);
+  const int64_t want = (vecs + 255) / 256;
+  const unsigned grid = static_cast<unsigned>(want < int64_t(sms) * 16 ? want : int64_t(sms) * 16);
+  if (quant_kind == T8G_QUANT_FP8_E4M3)
+    quant_given_amax_kernel<kQuantFp8><<<grid, 256, 0, st>>>(b);
+  else
+    quant_given_amax_kernel<kQuantInt8><<<grid, 256, 0, st>>>(b);
+  return launch_checked("quant phase B launch");
 }
 
 int rms_common(bool tensorwise, const void* x, int64_t ld_x, const void* w, const void* shift, const void* scale,
@@ -252,7 +347,7 @@ int rms_common(bool tensorwise, const void* x, int64_t ld_x, const void* w, cons
                float* amax, float* scale_out, int64_t S, int64_t D, int quant_kind, void* stream_) {
   using namespace t8g::rows;
   g_last_error[0] = '\0';
-  int rc = check_row_shape("rms_mod_quant", S, D, quant_kind);
+  int rc = check_row_shape("rms_mod_quant", S, D, quant_kind, 1);
   if (rc) return rc;
   if (S == 0 || D == 0) return T8G_OK;
   if ((rc = check_bf16_matrix("x", x, ld_x, D, true))) return rc;
@@ -263,12 +358,8 @@ int rms_common(bool tensorwise, const void* x, int64_t ld_x, const void* w, cons
   if ((rc = check_bf16_matrix("res", res, ld_res, D, false))) return rc;
   if ((rc = check_q(q, ld_q, D))) return rc;
   if (!mod_index && rows_per_mod < 1) return fail(T8G_ERR_INVALID_ARGUMENT, "rows_per_mod must be >= 1 without mod_index");
-  if (tensorwise) {
-    if (!amax) return fail(T8G_ERR_INVALID_ARGUMENT, "amax scratch word is null");
-    if (quant_kind != T8G_QUANT_FP8_E4M3 && quant_kind != T8G_QUANT_INT8) return fail(T8G_ERR_INVALID_ARGUMENT, "quant_kind");
-  } else if (!q_scale) {
-    return fail(T8G_ERR_INVALID_ARGUMENT, "q_scale is null");
-  }
+  if (tensorwise && !amax) return fail(T8G_ERR_INVALID_ARGUMENT, "amax scratch word is null");
+  if (!tensorwise && !q_scale) return fail(T8G_ERR_INVALID_ARGUMENT, "q_scale is null");
   int dev;
   DeviceInfo info;
   if ((rc = current_device(&dev, &info))) return rc;
@@ -296,10 +387,11 @@ int rms_common(bool tensorwise, const void* x, int64_t ld_x, const void* w, cons
   a.S = S;
   a.D = static_cast<int>(D);
   const int t = row_threads(D);
+  const RingGeom g = ring_geom(D, 1);
   if (tensorwise) {
     T8G_CHECK_CUDA(cudaMemsetAsync(amax, 0, sizeof(float), st), "cudaMemsetAsync(amax)");
-    T8G_DISPATCH_T(t, (rms_mod_kernel<T, 2><<<row_grid<T>(S), Geo<T>::kBlock, 0, st>>>(a)));
-    if ((rc = launch_checked("rms_mod phase A launch"))) return rc;
+    T8G_DISPATCH_T(t, rc = launch_rows(rms_mod_kernel<T, kModeTensorwise>, T, a, g, S, dev, info.sms, st, "rms_mod phase A"));
+    if (rc) return rc;
     QuantGivenArgs b;
     b.h = a.h;
     b.ld_h = ld_h;
@@ -309,21 +401,14 @@ int rms_common(bool tensorwise, const void* x, int64_t ld_x, const void* w, cons
     b.scale_out = scale_out;
     b.S = S;
     b.D = a.D;
-    const int64_t vecs = S * (D / 8);
-    const int64_t want = (vecs + 255) / 256;
-    const unsigned grid = static_cast<unsigned>(want < int64_t(info.sms) * 16 ? want : int64_t(info.sms) * 16);
-    if (quant_kind == T8G_QUANT_FP8_E4M3)
-      quant_given_amax_kernel<kQuantFp8><<<grid, 256, 0, st>>>(b);
-    else
-      quant_given_amax_kernel<kQuantInt8><<<grid, 256, 0, st>>>(b);
-    return launch_checked("quant phase B launch");
+    return launch_quant_given(b, quant_kind, info.sms, st);
   }
   if (quant_kind == T8G_QUANT_FP8_E4M3) {
-    T8G_DISPATCH_T(t, (rms_mod_kernel<T, kQuantFp8><<<row_grid<T>(S), Geo<T>::kBlock, 0, st>>>(a)));
+    T8G_DISPATCH_T(t, rc = launch_rows(rms_mod_kernel<T, kModeFp8>, T, a, g, S, dev, info.sms, st, "rms_mod_quant"));
   } else {
-    T8G_DISPATCH_T(t, (rms_mod_kernel<T, kQuantInt8><<<row_grid<T>(S), Geo<T>::kBlock, 0, st>>>(a)));
+    T8G_DISPATCH_T(t, rc = launch_rows(rms_mod_kernel<T, kModeInt8>, T, a, g, S, dev, info.sms, st, "rms_mod_quant"));
   }
-  return launch_checked("rms_mod_quant launch");
+  return rc;
 }
 
 int swiglu_common(bool tensorwise, const void* gate, const void* up, int64_t ld_in, void* q, int64_t ld_q,
@@ -331,7 +416,7 @@ int swiglu_common(bool tensorwise, const void* gate, const void* up, int64_t ld_
                   int quant_kind, void* stream_) {
   using namespace t8g::rows;
   g_last_error[0] = '\0';
-  int rc = check_row_shape("swiglu_quant", M, F, quant_kind);
+  int rc = check_row_shape("swiglu_quant", M, F, quant_kind, 2);
   if (rc) return rc;
   if (M == 0 || F == 0) return T8G_OK;
   if ((rc = check_bf16_matrix("gate", gate, ld_in, F, true))) return rc;
@@ -357,10 +442,11 @@ int swiglu_common(bool tensorwise, const void* gate, const void* up, int64_t ld_
   a.M = M;
   a.F = static_cast<int>(F);
   const int t = row_threads(F);
+  const RingGeom g = ring_geom(F, 2);
   if (tensorwise) {
     T8G_CHECK_CUDA(cudaMemsetAsync(amax, 0, sizeof(float), st), "cudaMemsetAsync(amax)");
-    T8G_DISPATCH_T(t, (swiglu_kernel<T, 2><<<row_grid<T>(M), Geo<T>::kBlock, 0, st>>>(a)));
-    if ((rc = launch_checked("swiglu phase A launch"))) return rc;
+    T8G_DISPATCH_T(t, rc = launch_rows(swiglu_kernel<T, kModeTensorwise>, T, a, g, M, dev, info.sms, st, "swiglu phase A"));
+    if (rc) return rc;
     QuantGivenArgs b;
     b.h = a.act;
     b.ld_h = ld_act;
@@ -370,21 +456,14 @@ int swiglu_common(bool tensorwise, const void* gate, const void* up, int64_t ld_
     b.scale_out = scale_out;
     b.S = M;
     b.D = a.F;
-    const int64_t vecs = M * (F / 8);
-    const int64_t want = (vecs + 255) / 256;
-    const unsigned grid = static_cast<unsigned>(want < int64_t(info.sms) * 16 ? want : int64_t(info.sms) * 16);
-    if (quant_kind == T8G_QUANT_FP8_E4M3)
-      quant_given_amax_kernel<kQuantFp8><<<grid, 256, 0, st>>>(b);
-    else
-      quant_given_amax_kernel<kQuantInt8><<<grid, 256, 0, st>>>(b);
-    return launch_checked("quant phase B launch");
+    return launch_quant_given(b, quant_kind, info.sms, st);
   }
   if (quant_kind == T8G_QUANT_FP8_E4M3) {
-    T8G_DISPATCH_T(t, (swiglu_kernel<T, kQuantFp8><<<row_grid<T>(M), Geo<T>::kBlock, 0, st>>>(a)));
+    T8G_DISPATCH_T(t, rc = launch_rows(swiglu_kernel<T, kModeFp8>, T, a, g, M, dev, info.sms, st, "swiglu_quant"));
   } else {
-    T8G_DISPATCH_T(t, (swiglu_kernel<T, kQuantInt8><<<row_grid<T>(M), Geo<T>::kBlock, 0, st>>>(a)));
+    T8G_DISPATCH_T(t, rc = launch_rows(swiglu_kernel<T, kModeInt8>, T, a, g, M, dev, info.sms, st, "swiglu_quant"));
   }
-  return launch_checked("swiglu_quant launch");
+  return rc;
 }
 
 // ----------------------------------------------------------------- allocation-free scratch
@@ -452,7 +531,7 @@ int t8g_quant_rows(const void* x, int64_t ld_x, void* q, int64_t ld_q, float* q_
                    int quant_kind, void* stream) {
   using namespace t8g::rows;
   g_last_error[0] = '\0';
-  int rc = check_row_shape("quant_rows", S, D, quant_kind);
+  int rc = check_row_shape("quant_rows", S, D, quant_kind, 1);
   if (rc) return rc;
   if (S == 0 || D == 0) return T8G_OK;
   if ((rc = check_bf16_matrix("x", x, ld_x, D, true))) return rc;
@@ -471,12 +550,13 @@ int t8g_quant_rows(const void* x, int64_t ld_x, void* q, int64_t ld_q, float* q_
   a.S = S;
   a.D = static_cast<int>(D);
   const int t = row_threads(D);
+  const RingGeom g = ring_geom(D, 1);
   if (quant_kind == T8G_QUANT_FP8_E4M3) {
-    T8G_DISPATCH_T(t, (quant_rows_kernel<T, kQuantFp8><<<row_grid<T>(S), Geo<T>::kBlock, 0, st>>>(a)));
+    T8G_DISPATCH_T(t, rc = launch_rows(quant_rows_kernel<T, kQuantFp8>, T, a, g, S, dev, info.sms, st, "quant_rows"));
   } else {
-    T8G_DISPATCH_T(t, (quant_rows_kernel<T, kQuantInt8><<<row_grid<T>(S), Geo<T>::kBlock, 0, st>>>(a)));
+    T8G_DISPATCH_T(t, rc = launch_rows(quant_rows_kernel<T, kQuantInt8>, T, a, g, S, dev, info.sms, st, "quant_rows"));
   }
-  return launch_checked("quant_rows launch");
+  return rc;
 }
 
 int t8g_rms_mod_quant(const void* x, int64_t ld_x, const void* w, const void* shift, const void* scale,
