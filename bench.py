@@ -59,7 +59,7 @@ def parse_args():
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true")
-    ap.add_argument("--profile", choices=("gemm_i8", "gemm_fp8", "rms_fp8", "rms_int8", "swiglu_int8"),
+    ap.add_argument("--profile", choices=("gemm_i8", "gemm_fp8", "rms_fp8", "rms_int8", "swiglu_int8", "quant_int8"),
                     help="run one kernel a few times on a mid-size case (for ncu captures) and exit")
     ap.add_argument("--M", type=int, default=32768)
     ap.add_argument("--N", type=int, default=9216)
@@ -68,7 +68,8 @@ def parse_args():
 
 def run_profile_case(args):
     """One kernel, `warmup + steps` launches, on a case whose inputs exceed L2 but stay
-    within a few GB: GEMM M x N x 3072; norm/quant [2*56320, 3072]; SwiGLU [32768, 2*12288]."""
+    within a few GB: GEMM M x N x 3072; norm/quant and per-token quant [2*56320, 3072];
+    SwiGLU [32768, 2*12288]."""
     import torch
     from __graft_entry__ import load_package
     load_package()
@@ -93,6 +94,10 @@ def run_profile_case(args):
         sc = (torch.randn(2, 3072, generator=gen, device=dev) * 0.1).to(torch.bfloat16)
         for _ in range(n):
             ops.rms_mod_quant(x, sh, sc, rows_per_mod=56320, eps=1e-6, kind=kind)
+    elif args.profile == "quant_int8":
+        x = torch.randn(2 * 56320, 3072, generator=gen, device=dev).to(torch.bfloat16)
+        for _ in range(n):
+            ops.quant_rows(x, "int8")
     else:
         y = torch.randn(32768, 2 * 12288, generator=gen, device=dev).to(torch.bfloat16)
         for _ in range(n):

@@ -54,11 +54,8 @@ QUANT_INT8 = "int8"
 QUANT_FP8 = "fp8_e4m3"
 
 # Canonical launch shape of the row kernels: one row is handled by T threads,
-# T the smallest power of two in [32, ROW_MAX_THREADS] such that every thread
-# holds at most ROW_FAST_VEC 16-byte vectors (8 bf16 values) of the row, else
-# ROW_MAX_THREADS (rows up to ROW_MAX_D values).
-ROW_FAST_VEC = 4
-ROW_MAX_THREADS = 512
+# V = max(3, ceil(nvec / 512)) 16-byte vectors (8 bf16 values) per thread and
+# T = 32 * ceil(nvec / (32 * V)), nvec = D / 8 (rows up to ROW_MAX_D values).
 ROW_MAX_D = 49152
 
 
@@ -282,10 +279,8 @@ def row_threads(D: int) -> int:
     if D > ROW_MAX_D:
         raise ValueError(f"row length {D} exceeds {ROW_MAX_D}")
     nvec = (D + 7) // 8
-    t = 32
-    while t < ROW_MAX_THREADS and (nvec + t - 1) // t > ROW_FAST_VEC:
-        t *= 2
-    return t
+    v = max(3, (nvec + 511) // 512)
+    return max(32, 32 * ((nvec + 32 * v - 1) // (32 * v)))
 
 
 def rms_sum_squares(x: np.ndarray) -> np.ndarray:

@@ -50,7 +50,8 @@ def bf16_ulp_diff(a, b):
 
 
 @pytest.mark.parametrize("kind", ["int8", "fp8_e4m3"])
-@pytest.mark.parametrize("S,D", [(1, 8), (7, 3072), (256, 3072), (33, 5376), (9, 12288), (3, 24576), (2, 49152)])
+@pytest.mark.parametrize("S,D", [(1, 8), (7, 3072), (256, 3072), (33, 5376), (20000, 1024), (9, 8192), (9, 8200),
+                                 (9, 12288), (3, 24576), (2, 49152)])
 def test_quant_rows_bit_exact(ops, kind, S, D):
     rng = np.random.default_rng(S * 31 + D)
     x = O.round_bf16((rng.standard_normal((S, D)) * 3).astype(np.float32))
@@ -62,6 +63,22 @@ def test_quant_rows_bit_exact(ops, kind, S, D):
     q_ref, s_ref = O.quant_rows(x, KINDS[kind])
     np.testing.assert_array_equal(s.cpu().numpy(), s_ref)
     np.testing.assert_array_equal(qbits(q, kind), q_ref)
+
+
+@pytest.mark.parametrize("kind", ["int8", "fp8_e4m3"])
+@pytest.mark.parametrize("D", [3072, 12288])
+def test_quant_rows_strided_rows(ops, kind, D):
+    """Row strides wider than the row on both sides (a column slice of a wider matrix)."""
+    S = 300
+    rng = np.random.default_rng(D)
+    wide = O.round_bf16((rng.standard_normal((S, D + 24)) * 2).astype(np.float32))
+    xd = bf16_dev(to_bf16_bits(wide))[:, 8: 8 + D]
+    qbuf = torch.zeros(S, D + 40, dtype=torch.int8 if kind == "int8" else torch.float8_e4m3fn, device="cuda")
+    q, s = ops.quant_rows(xd, kind, q=qbuf[:, 16: 16 + D])
+    q_ref, s_ref = O.quant_rows(wide[:, 8: 8 + D], KINDS[kind])
+    np.testing.assert_array_equal(s.cpu().numpy(), s_ref)
+    np.testing.assert_array_equal(qbits(q, kind), q_ref)
+    np.testing.assert_array_equal(qbits(qbuf[:, :16], kind), 0)     # nothing written outside the slice
 
 
 @pytest.mark.parametrize("kind", ["int8", "fp8_e4m3"])
@@ -164,6 +181,28 @@ def test_swiglu_quant_per_token(ops, kind, M, F):
     q_given, qs_given = O.quant_rows(O.bf16_to_f32(bits16(act)), KINDS[kind])
     np.testing.assert_array_equal(qs.cpu().numpy(), qs_given)
     np.testing.assert_array_equal(qbits(q, kind), q_given)
+
+
+def test_swiglu_every_finite_bf16_gate(ops):
+    """act for every finite bf16 gate value (subnormals, the window g < -87.3 where
+    1 / (1 + e^-g) is subnormal, g < -88.7 where e^-g overflows, and the largest
+    magnitudes) times four up values, within one bf16 ulp of the oracle; q exact given act."""
+    bits = np.arange(65536, dtype=np.uint32).astype(np.uint16)
+    finite = bits[(bits & 0x7F80) != 0x7F80]
+    F = 2048
+    g = np.zeros(-(-finite.size // F) * F, np.uint16)
+    g[: finite.size] = finite
+    g = g.reshape(-1, F)
+    ups = np.array([0.5, -1.0, 1e-3, -0.75], np.float32)
+    gate = np.concatenate([g] * len(ups))
+    up = np.repeat(ups, g.shape[0])[:, None] * np.ones((1, F), np.float32)
+    y = np.concatenate([gate, O.f32_to_bf16(up)], axis=1)
+    q, qs, act = ops.swiglu_quant_fc1(bf16_dev(y), kind="int8", return_act=True)
+    _, _, act_ref = O.swiglu_quant_per_token(O.bf16_to_f32(gate), O.round_bf16(up), O.QUANT_INT8)
+    assert bf16_ulp_diff(bits16(act), act_ref).max() <= 1
+    q_given, qs_given = O.quant_rows(O.bf16_to_f32(bits16(act)), O.QUANT_INT8)
+    np.testing.assert_array_equal(qs.cpu().numpy(), qs_given)
+    np.testing.assert_array_equal(qbits(q, "int8"), q_given)
 
 
 def test_swiglu_quant_config2_shape(ops):

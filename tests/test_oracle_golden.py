@@ -137,9 +137,10 @@ def test_rms_sum_squares_tree_matches_sequential_sum_closely():
 
 def test_row_threads_rule():
     assert O.row_threads(3072) == 128
-    assert O.row_threads(1024) == 32
-    assert O.row_threads(5376) == 256
+    assert O.row_threads(1024) == 64
+    assert O.row_threads(5376) == 224
     assert O.row_threads(12288) == 512
+    assert O.row_threads(16384) == 512
     assert O.row_threads(8) == 32
     assert O.row_threads(49152) == 512
     with pytest.raises(ValueError):

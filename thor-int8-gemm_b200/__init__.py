@@ -12,12 +12,13 @@ Submodules (imported lazily, so the import-proxy agent stays light at start-up):
   patch_int8  the comfy-kitchen `_C` import proxy and its .pth installer
   build       nvcc build of the shared library
   shard       token sharding across ranks (one process per GPU)
+  dit         a DiT block whose linears and norm/quant ops run on these kernels
 """
 import importlib
 
 __version__ = "0.1.0"
 PACKAGE_NAME = "thor_int8_gemm_b200"
-_LAZY = ("ops", "fused", "patch_int8", "build", "_lib", "shard")
+_LAZY = ("ops", "fused", "patch_int8", "build", "_lib", "shard", "dit")
 
 
 def __getattr__(name):

@@ -379,6 +379,94 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   }
 }
 
+// Per-tile channel parameters staged in shared memory by the epilogue warps:
+// ws[n_tile0 + j] and f32(bias[n_tile0 + j]) for j < BN (0 past N).
+struct TileParams {
+  float ws[BN];
+  float bias[BN];
+};
+
+template <int OUT>
+__device__ __forceinline__ void stage_tile_params(const Args& args, int n_tile0, int e, int ne, TileParams& tp) {
+  for (int j = e; j < BN; j += ne) {
+    const int n = n_tile0 + j;
+    const bool in = n < args.N;
+    tp.ws[j] = in ? __ldg(args.ws + (args.ws_stride ? n : 0)) : 0.f;
+    tp.bias[j] = (in && args.bias) ? OutTraits<OUT>::to_f32(args.bias, n) : 0.f;
+  }
+}
+
+// Epilogue of one 32-row slice with the tile's parameters in shared memory and the
+// TMEM loads software-pipelined (the load of chunk c+1 overlaps the math of chunk c).
+template <int IN, int OUT, int EPB>
+__device__ __forceinline__ void epilogue_tile_staged(const Args& args, const CUtensorMap* tm_out,
+                                                     uint8_t (*bufs)[EPB], int& ebuf, uint32_t t_row,
+                                                     int row0, int n_tile0, int lane, uint64_t pol_out, float xs_r,
+                                                     const TileParams& tp) {
+  const int nchunks = min(BN / EPI_COLS, (args.N - n_tile0 + EPI_COLS - 1) / EPI_COLS);
+  const bool has_bias = args.bias != nullptr;
+  uint32_t r[32];
+  tmem_ld_32x32b_x32(t_row, r);
+  for (int c = 0; c < nchunks; ++c) {
+    tmem_ld_wait_regs(r);
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = (IN == kInI8) ? __int2float_rn(static_cast<int>(r[j])) : __uint_as_float(r[j]);
+    if (c + 1 < nchunks) tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>((c + 1) * EPI_COLS), r);
+    const float4* wq = reinterpret_cast<const float4*>(tp.ws + c * EPI_COLS);
+    const float4* bq = reinterpret_cast<const float4*>(tp.bias + c * EPI_COLS);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const float4 w4 = wq[q];
+      const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
+      float bb[4] = {0.f, 0.f, 0.f, 0.f};
+      if (has_bias) {
+        const float4 b4 = bq[q];
+        bb[0] = b4.x; bb[1] = b4.y; bb[2] = b4.z; bb[3] = b4.w;
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float f = __fmul_rn(v[4 * q + e], xs_r);
+        f = __fmul_rn(f, wv[e]);
+        if (has_bias) f = __fadd_rn(f, bb[e]);
+        v[4 * q + e] = f;
+      }
+    }
+    const int n0 = n_tile0 + c * EPI_COLS;
+    // the staging buffer used two chunks ago must have been read by its TMA store
+    if (lane == 0) bulk_wait_group_read<1>();
+    __syncwarp();
+    uint8_t* buf = bufs[ebuf];
+    if constexpr (OutTraits<OUT>::kBytes == 2) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint4 w;
+        w.x = OutTraits<OUT>::pack2(v[8 * q + 0], v[8 * q + 1]);
+        w.y = OutTraits<OUT>::pack2(v[8 * q + 2], v[8 * q + 3]);
+        w.z = OutTraits<OUT>::pack2(v[8 * q + 4], v[8 * q + 5]);
+        w.w = OutTraits<OUT>::pack2(v[8 * q + 6], v[8 * q + 7]);
+        const int pq = q ^ ((lane >> 1) & 3);
+        *reinterpret_cast<uint4*>(buf + lane * 64 + pq * 16) = w;
+      }
+    } else {
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float4 w = make_float4(v[4 * q + 0], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+        const int pq = q ^ (lane & 7);
+        *reinterpret_cast<float4*>(buf + lane * 128 + pq * 16) = w;
+      }
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_2d(tm_out, buf, n0, row0, pol_out);
+      bulk_commit_group();
+    }
+    ebuf ^= 1;
+  }
+  if (nchunks == 0) tmem_ld_wait_regs(r);
+}
+
 // ===========================================================================
 // 2-SM variant: a cluster of two CTAs (one per SM of a TPC) computes a 256x256
 // output tile with tcgen05.mma.cta_group::2 (M = 256, N = 256, K = 32).
@@ -392,27 +480,44 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 //   Each CTA's epilogue warps store their own 128 rows and report the
 //   accumulator free on the leader's `tmem_empty` barrier.
 // Per SM this halves W's share of the shared-memory fill and of the tensor
-// core's operand reads compared with the 1-SM kernel, and 6 stages fit.
+// core's operand reads compared with the 1-SM kernel.  The epilogue stages each
+// tile's channel parameters in shared memory before waiting for its accumulator
+// and pipelines its TMEM loads.
 // ===========================================================================
 constexpr int P_BM = 256;                   // tile rows per CTA pair
 constexpr int P_ROWS = 128;                 // rows of A (and of W) per CTA
-constexpr int P_STAGES = 6;
 constexpr int P_A_BYTES = P_ROWS * BK;
 constexpr int P_B_BYTES = P_ROWS * BK;
 constexpr int P_STAGE_BYTES = P_A_BYTES + P_B_BYTES;   // per CTA
 
+// Ring depth and epilogue staging per output type: a staging buffer holds 32 rows x
+// 32 columns of the output type, so 2-byte outputs leave room for a sixth stage
+// (6 x 32 KB ring + 16 KB staging + 4 KB parameters); fp32 outputs keep five.
+template <int OUT>
+struct PairCfg {
+  static constexpr int kEpiBytes = 32 * EPI_COLS * OutTraits<OUT>::kBytes;
+  static constexpr int kStages = 5;
+};
+
+template <int STAGES, int EPB>
 struct SmemPair {
-  uint8_t a[P_STAGES][P_A_BYTES];
-  uint8_t b[P_STAGES][P_B_BYTES];
-  uint8_t epi[EPI_WARPS][2][EPI_BUF_BYTES];
-  uint64_t full[P_STAGES];
-  uint64_t empty[P_STAGES];
+  uint8_t a[STAGES][P_A_BYTES];
+  uint8_t b[STAGES][P_B_BYTES];
+  uint8_t epi[EPI_WARPS][2][EPB];
+  TileParams params[2];   // channel parameters of the tile in each accumulator
+  uint64_t full[STAGES];
+  uint64_t empty[STAGES];
   uint64_t tmem_full[2];
   uint64_t tmem_empty[2];
   uint64_t drain;
   uint32_t tmem_base;
 };
-constexpr size_t P_SMEM_BYTES = sizeof(SmemPair) + 1024;
+template <int OUT>
+using SmemPairOf = SmemPair<PairCfg<OUT>::kStages, PairCfg<OUT>::kEpiBytes>;
+template <int OUT>
+constexpr size_t pair_smem_bytes() { return sizeof(SmemPairOf<OUT>) + 1024; }   // + slack to align to 1024 B
+static_assert(pair_smem_bytes<kOutBF16>() <= 227 * 1024 && pair_smem_bytes<kOutF32>() <= 227 * 1024,
+              "pair kernel shared memory exceeds the per-CTA limit");
 
 template <int IN, int OUT>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
@@ -420,7 +525,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
                              const __grid_constant__ CUtensorMap tm_out, const Args args) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
-  SmemPair& s = *reinterpret_cast<SmemPair*>(smem_raw + pad);
+  using Cfg = PairCfg<OUT>;
+  constexpr int P_STAGES = Cfg::kStages;
+  SmemPairOf<OUT>& s = *reinterpret_cast<SmemPairOf<OUT>*>(smem_raw + pad);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -500,17 +607,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     if (lane == 0 && rank == 0) {
       constexpr uint32_t idesc = (IN == kInI8) ? make_idesc(2, 1, 1, P_BM, BN)   // s32 <- s8 x s8
                                                : make_idesc(1, 0, 0, P_BM, BN);  // f32 <- e4m3 x e4m3
-      uint32_t empty_bar[P_STAGES][2], tfull_bar[2][2];
-#pragma unroll
-      for (int i = 0; i < P_STAGES; ++i) {
-        empty_bar[i][0] = mapa_shared(smem_u32(&s.empty[i]), 0);
-        empty_bar[i][1] = mapa_shared(smem_u32(&s.empty[i]), 1);
-      }
-#pragma unroll
-      for (int i = 0; i < 2; ++i) {
-        tfull_bar[i][0] = mapa_shared(smem_u32(&s.tmem_full[i]), 0);
-        tfull_bar[i][1] = mapa_shared(smem_u32(&s.tmem_full[i]), 1);
-      }
+      // cluster addresses of the barrier arrays in both CTAs (8 bytes per barrier)
+      const uint32_t empty0[2] = {mapa_shared(smem_u32(&s.empty[0]), 0), mapa_shared(smem_u32(&s.empty[0]), 1)};
+      const uint32_t tfull0[2] = {mapa_shared(smem_u32(&s.tmem_full[0]), 0),
+                                  mapa_shared(smem_u32(&s.tmem_full[0]), 1)};
       int stage = 0;
       uint32_t phase = 0;
       int local = 0;
@@ -542,8 +642,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
             else
               mma_f8_pair(d_tmem, ad, bd, idesc, accumulate);
           }
-          tc_commit_pair(empty_bar[stage][0]);
-          tc_commit_pair(empty_bar[stage][1]);
+          tc_commit_pair(empty0[0] + 8u * static_cast<uint32_t>(stage));
+          tc_commit_pair(empty0[1] + 8u * static_cast<uint32_t>(stage));
           any = true;
           if (++stage == P_STAGES) {
             stage = 0;
@@ -551,8 +651,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
           }
         }
         if (!ok) break;
-        tc_commit_pair(tfull_bar[acc][0]);
-        tc_commit_pair(tfull_bar[acc][1]);
+        tc_commit_pair(tfull0[0] + 8u * static_cast<uint32_t>(acc));
+        tc_commit_pair(tfull0[1] + 8u * static_cast<uint32_t>(acc));
       }
       if (any) {
         tc_commit_pair(mapa_shared(smem_u32(&s.drain), 0));
@@ -563,6 +663,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     // ------------------------------------------------------------ epilogue (both CTAs)
     const int ew = warp - 2;
     const int quarter = warp & 3;
+    const int e = threadIdx.x - 64;   // 0..127 over the epilogue warps
     const uint64_t pol_out = policy_evict_first();
     uint32_t tempty_bar[2];
     tempty_bar[0] = mapa_shared(smem_u32(&s.tmem_empty[0]), 0);
@@ -574,13 +675,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       const int tn = tile - tm * tiles_n;
       const int acc = local & 1;
       const uint32_t acc_phase = static_cast<uint32_t>((local >> 1) & 1);
-      if (!mbar_wait(&s.tmem_full[acc], acc_phase, kStatusTimeoutEpilogue)) break;
-      tc_fence_after();
       const int row0 = tm * P_BM + static_cast<int>(rank) * P_ROWS + quarter * 32;
+      // channel parameters and the row scale load while the MMA still runs
+      stage_tile_params<OUT>(args, tn * BN, e, 128, s.params[acc]);
+      const float xs_r = row0 + lane < args.M ? __ldg(args.xs + row0 + lane) : 0.f;
+      const bool ok = mbar_wait(&s.tmem_full[acc], acc_phase, kStatusTimeoutEpilogue);
+      // all four warps staged the parameters; they leave together if any wait ran out
+      if (named_bar_any(1, 128, !ok)) break;
+      tc_fence_after();
       if (row0 < args.M) {
-        epilogue_tile<IN, OUT>(args, &tm_out, s.epi[ew], ebuf,
-                               tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN),
-                               row0, tn * BN, lane, pol_out);
+        epilogue_tile_staged<IN, OUT, Cfg::kEpiBytes>(args, &tm_out, s.epi[ew], ebuf,
+                                      tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                                          static_cast<uint32_t>(acc * BN),
+                                      row0, tn * BN, lane, pol_out, xs_r, s.params[acc]);
       }
       tc_fence_before();
       __syncwarp();

@@ -235,6 +235,40 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)
 
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// Wait for outstanding tcgen05.ld, tying the 32 destination registers to the wait so
+// that no use of them can be scheduled before it.
+__device__ __forceinline__ void tmem_ld_wait_regs(uint32_t (&r)[32]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                 "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]),
+                 "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]),
+                 "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+               :
+               : "memory");
+}
+
+// Named barrier over `count` threads that also returns whether `v` is true in any of them.
+__device__ __forceinline__ bool named_bar_any(uint32_t id, uint32_t count, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n"
+      "  .reg .pred p, q;\n"
+      "  setp.ne.u32 p, %1, 0;\n"
+      "  bar.red.or.pred q, %2, %3, p;\n"
+      "  selp.u32 %0, 1, 0, q;\n"
+      "}\n"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(v)), "r"(id), "r"(count)
+      : "memory");
+  return r != 0;
+}
+
+// Named barrier over `count` threads (a multiple of 32) of the CTA.
+__device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
 // ---------------------------------------------------------------------------
 // CTA pairs (cluster of 2) for the 2-SM tensor-core path
 // ---------------------------------------------------------------------------

@@ -10,9 +10,9 @@
 // once.  Thread t of the CTA owns the 16-byte vectors c = t, t + T, t + 2T, ...
 // of a row.
 //
-// T is the smallest power of two in [32, 512] that leaves at most kFastVec
-// vectors per thread (512 for longer rows; rows are limited by the ring's slot
-// size, 96 KB).  Canonical arithmetic, restated
+// Row-group shape (host rule, restated by the oracle): V = max(3, ceil(nvec/512))
+// vectors per thread, T = 32 * ceil(nvec / (32 V)) threads, nvec = D / 8; rows
+// are limited by the ring's slot size (96 KB).  Canonical arithmetic, restated
 // bit for bit by the CPU oracle:
 //   sum of squares: per thread, two FMA accumulators (even / odd element of each
 //   bf16 pair) in vector order, combined as even + odd (the squares of bf16 values
@@ -34,7 +34,6 @@
 namespace t8g {
 namespace rows {
 
-constexpr int kFastVec = 4;        // vectors per thread that set the row-group size T
 constexpr float kScaleMin = 1e-12f;   // src/ck_fused_mod_norm_quant.py:141
 
 enum QuantKind : int { kQuantInt8 = 0, kQuantFp8 = 1 };
@@ -90,32 +89,15 @@ __device__ __forceinline__ uint32_t cvt_e4m3x2(float lo, float hi) {
   asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
   return r;
 }
-// Packed fp32 arithmetic with explicit round-to-nearest-even.  A packed multiply that
-// feeds a packed add can still be fused into one multiply-add by the assembler (observed:
-// h = t * s + b came out as fma(t, s, b) in a rare cancelling case), so every add whose
-// operand is a product uses the scalar IEEE add (__fadd_rn, never contracted) instead.
-__device__ __forceinline__ float2 mul2_rn(float2 a, float2 b) {
-  uint64_t d;
-  asm("mul.rn.f32x2 %0, %1, %2;"
-      : "=l"(d)
-      : "l"(*reinterpret_cast<uint64_t*>(&a)), "l"(*reinterpret_cast<uint64_t*>(&b)));
-  return *reinterpret_cast<float2*>(&d);
-}
-__device__ __forceinline__ float2 add2_rn(float2 a, float2 b) {
-  uint64_t d;
-  asm("add.rn.f32x2 %0, %1, %2;"
-      : "=l"(d)
-      : "l"(*reinterpret_cast<uint64_t*>(&a)), "l"(*reinterpret_cast<uint64_t*>(&b)));
-  return *reinterpret_cast<float2*>(&d);
-}
-__device__ __forceinline__ float2 fma2_rn(float2 a, float2 b, float2 c) {
-  uint64_t d;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;"
-      : "=l"(d)
-      : "l"(*reinterpret_cast<uint64_t*>(&a)), "l"(*reinterpret_cast<uint64_t*>(&b)),
-        "l"(*reinterpret_cast<uint64_t*>(&c)));
-  return *reinterpret_cast<float2*>(&d);
-}
+// Packed fp32 arithmetic (two lanes per instruction), each lane rounded to nearest even.
+// A packed multiply that feeds a packed add may be fused into one multiply-add
+// (observed: h = t * s + b came out as fma(t, s, b) in a rare cancelling case), so an
+// add whose operand is a product that must round separately uses the scalar IEEE add
+// (__fadd_rn, never contracted).  Where fusion cannot change the result (the
+// quantiser's bracket, see quant8) the packed forms are used as they are.
+__device__ __forceinline__ float2 mul2_rn(float2 a, float2 b) { return __fmul2_rn(a, b); }
+__device__ __forceinline__ float2 add2_rn(float2 a, float2 b) { return __fadd2_rn(a, b); }
+__device__ __forceinline__ float2 fma2_rn(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
 
 __device__ __forceinline__ float2 bf2_to_f2(uint32_t u) {
   return make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xFFFF0000u));
@@ -149,7 +131,8 @@ __device__ __forceinline__ QuantRow quant_row(float amax) {
 // x within a relative 2^-21 - 2^-23 > 2^-23 of it on either side, so RN(x) lies
 // between a and b.  The 8-bit conversion (int8: round half to even; e4m3: RNE with
 // saturation) is monotone, so when a and b convert to the same code that code is
-// the one RN(x) converts to.  Otherwise (a rounding boundary lies within ~2^-21 of
+// the one RN(x) converts to.  (If the int8 path's multiply and magic-number add are
+// fused, the integers are those of the exact products, which bracket x too.)  Otherwise (a rounding boundary lies within ~2^-21 of
 // x, probability ~2^-17 per value) the lane recomputes its eight values with the
 // IEEE divide.  int8 never needs the +-127 clamp: |x| <= 127 * (1 + 2^-23).
 template <int QK>
@@ -196,37 +179,35 @@ __device__ __forceinline__ void unpack_pairs(const uint4& u, float2 (&v)[4]) {
 
 
 // ---------------------------------------------------------------- block reductions
-// The CTA is one row group of T threads; `red` holds T/32 floats.
-template <int T>
+// The CTA is one row group of blockDim.x (a multiple of 32) threads; `red` holds one
+// float per warp.  Canonical order: butterfly within each warp, then the warp
+// partials added (or maxed) left to right.
 __device__ __forceinline__ float block_sum(float v, float* red) {
 #pragma unroll
   for (int off = 16; off >= 1; off >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xFFFFFFFFu, v, off));
-  if constexpr (T == 32) {
-    return v;
-  } else {
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
-    __syncthreads();
-    float t = red[0];
-#pragma unroll
-    for (int i = 1; i < T / 32; ++i) t = __fadd_rn(t, red[i]);
-    return t;
-  }
+  const int nw = blockDim.x >> 5;
+  if (nw == 1) return v;
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float t = red[0];
+  for (int i = 1; i < nw; ++i) t = __fadd_rn(t, red[i]);
+  return t;
 }
 
-template <int T>
+// Max of non-negative values over the CTA (order-free: every lane of every warp
+// folds the warp partials with one more butterfly).
 __device__ __forceinline__ float block_max(float v, float* red) {
 #pragma unroll
   for (int off = 16; off >= 1; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xFFFFFFFFu, v, off));
-  if constexpr (T == 32) {
-    return v;
-  } else {
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
-    __syncthreads();
-    float t = red[0];
+  const int nw = blockDim.x >> 5;
+  if (nw == 1) return v;
+  const int lane = threadIdx.x & 31;
+  if (lane == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float t = lane < nw ? red[lane] : 0.f;
 #pragma unroll
-    for (int i = 1; i < T / 32; ++i) t = fmaxf(t, red[i]);
-    return t;
-  }
+  for (int off = 16; off >= 1; off >>= 1) t = fmaxf(t, __shfl_xor_sync(0xFFFFFFFFu, t, off));
+  return t;
 }
 
 // Non-negative float max via the integer order of its bit pattern.
@@ -243,7 +224,7 @@ struct RingGeom {
   uint32_t part_bytes; // bytes of one bulk copy (a row of one operand)
   int parts;           // bulk copies per slot (1, or 2 for gate + up)
 };
-constexpr int kRingHeader = 1024;   // barriers (<= 16 x 8 B), reductions (2 x 16 floats), flags
+constexpr int kRingHeader = 1024;   // barriers (<= 16 x 8 B), reductions (2 x 32 floats)
 constexpr int kMaxStages = 16;
 
 struct RingState {
@@ -257,7 +238,7 @@ __device__ __forceinline__ RingState ring_state(uint8_t* smem) {
   RingState r;
   r.full = reinterpret_cast<uint64_t*>(smem);
   r.red_sum = reinterpret_cast<float*>(smem + 8 * kMaxStages);
-  r.red_max = r.red_sum + 16;
+  r.red_max = r.red_sum + 32;
   r.slots = smem + kRingHeader;
   return r;
 }
@@ -323,7 +304,7 @@ struct SwigluArgs {
 // Runs `body(row, slot_ptr, ring)` for rows blockIdx.x, blockIdx.x + gridDim.x, ...
 // with the ring kept `stages - 1` rows ahead.  `src(row, part)` gives the
 // global address of a row operand.  Returns after draining in-flight copies.
-template <int T, typename Src, typename Body>
+template <typename Src, typename Body>
 __device__ __forceinline__ void row_loop(uint8_t* smem, const RingGeom& g, int64_t nrows, Src src, Body body) {
   RingState rs = ring_state(smem);
   const uint64_t policy = policy_evict_first();
@@ -342,39 +323,46 @@ __device__ __forceinline__ void row_loop(uint8_t* smem, const RingGeom& g, int64
       ++issued;
     }
   }
+  // slot and phase of row k advance incrementally (no 64-bit division per row)
   int64_t k = 0;
+  int st = 0, prev = g.stages - 1;
+  uint32_t ph = 0;
+  const int64_t ahead = static_cast<int64_t>(g.stages - 1) * G;   // row k-1+stages = row + ahead
   for (int64_t row = blockIdx.x; row < nrows; row += G, ++k) {
-    const int st = static_cast<int>(k % g.stages);
-    const uint32_t ph = static_cast<uint32_t>((k / g.stages) & 1);
     const bool ok = mbar_wait(&rs.full[st], ph, kStatusTimeoutProducer);
     if (__syncthreads_or(!ok)) break;
     // every thread is past row k-1: refill its slot with row k-1+stages
     if (threadIdx.x == 0 && k > 0) {
-      const int64_t r = row - G + static_cast<int64_t>(g.stages) * G;
+      const int64_t r = row + ahead;
       if (r < nrows) {
-        ring_issue(rs, g, static_cast<int>((k - 1) % g.stages), src(r, 0), src(r, 1), policy);
+        ring_issue(rs, g, prev, src(r, 0), src(r, 1), policy);
         ++issued;
       }
     }
     body(row, rs.slots + static_cast<size_t>(st) * g.slot_bytes, rs);
+    prev = st;
+    if (++st == g.stages) {
+      st = 0;
+      ph ^= 1u;
+    }
   }
   // teardown: copies still in flight (only after an abort) must land before exit
   if (threadIdx.x == 0) {
-    for (int64_t n = k; n < issued; ++n)
-      if (!mbar_wait(&rs.full[n % g.stages], static_cast<uint32_t>((n / g.stages) & 1), kStatusTimeoutDrain)) break;
+    for (int64_t n = k; n < issued; ++n) {
+      if (!mbar_wait(&rs.full[st], ph, kStatusTimeoutDrain)) break;
+      if (++st == g.stages) {
+        st = 0;
+        ph ^= 1u;
+      }
+    }
   }
 }
 
 // ---------------------------------------------------------------- shared pieces
-// Quantise the row held (as bf16) in `src` (shared memory) and store q.
-template <int T, int QK>
-__device__ __forceinline__ void quant_row_store(const uint8_t* src, int nvec, const QuantRow& qr, uint8_t* qrow) {
-  for (int c = threadIdx.x; c < nvec; c += T) {
-    float2 v[4];
-    unpack_pairs(lds_v4(src + 16 * c), v);
-    *reinterpret_cast<uint2*>(qrow + 8 * c) = quant8<QK>(v, qr);
-  }
-}
+// A row group is blockDim.x = T threads; thread t owns the 16-byte vectors
+// c = t + T * i of a row.  Kernels are instantiated for V = 3 or 4 vectors per
+// thread (fully unrolled, results kept in registers) and V = 0, the generic form
+// for longer rows (runtime loop, results staged in the ring slot).
 
 __device__ __forceinline__ uint32_t absmax4(uint32_t m2, const uint4& u) {
   m2 = absmax_bf16x2(m2, u.x);
@@ -387,19 +375,148 @@ __device__ __forceinline__ uint32_t absmax4(uint32_t m2, const uint4& u) {
 // later refills it.
 __device__ __forceinline__ void slot_written() { fence_proxy_async_smem(); }
 
+__device__ __forceinline__ float pair_max(uint32_t m2) { return fmaxf(bf_lo(m2), bf_hi(m2)); }
+
+template <int QK>
+__device__ __forceinline__ void store_q(uint8_t* qrow, int c, const uint4& u, const QuantRow& qr) {
+  float2 v[4];
+  unpack_pairs(u, v);
+  *reinterpret_cast<uint2*>(qrow + 8 * c) = quant8<QK>(v, qr);
+}
+
 // ---------------------------------------------------------------- per-token quant
-template <int T, int QK>
-__global__ void __launch_bounds__(T) quant_rows_kernel(const QuantRowsArgs a, const RingGeom g) {
+template <int V, int QK>
+__global__ void __launch_bounds__(512) quant_rows_kernel(const QuantRowsArgs a, const RingGeom g) {
   extern __shared__ __align__(1024) uint8_t smem[];
+  const int T = blockDim.x;
   const int nvec = a.D >> 3;
   auto src = [&](int64_t r, int) -> const void* { return a.x + r * a.ld_x; };
-  row_loop<T>(smem, g, a.S, src, [&](int64_t row, const uint8_t* slot, const RingState& rs) {
+  row_loop(smem, g, a.S, src, [&](int64_t row, const uint8_t* slot, const RingState& rs) {
+    uint8_t* qrow = static_cast<uint8_t*>(a.q) + row * a.ld_q;
     uint32_t m2 = 0;
-    for (int c = threadIdx.x; c < nvec; c += T) m2 = absmax4(m2, lds_v4(slot + 16 * c));
-    const float amax = block_max<T>(fmaxf(bf_lo(m2), bf_hi(m2)), rs.red_max);
-    const QuantRow qr = quant_row<QK>(amax);
-    if (threadIdx.x == 0) a.q_scale[row] = qr.scale;
-    quant_row_store<T, QK>(slot, nvec, qr, static_cast<uint8_t*>(a.q) + row * a.ld_q);
+    if constexpr (V > 0) {
+      uint4 xv[V];
+#pragma unroll
+      for (int i = 0; i < V; ++i) {
+        const int c = threadIdx.x + T * i;
+        xv[i] = c < nvec ? lds_v4(slot + 16 * c) : make_uint4(0, 0, 0, 0);
+        m2 = absmax4(m2, xv[i]);
+      }
+      const QuantRow qr = quant_row<QK>(block_max(pair_max(m2), rs.red_max));
+      if (threadIdx.x == 0) a.q_scale[row] = qr.scale;
+#pragma unroll
+      for (int i = 0; i < V; ++i) {
+        const int c = threadIdx.x + T * i;
+        if (c < nvec) store_q<QK>(qrow, c, xv[i], qr);
+      }
+    } else {
+      for (int c = threadIdx.x; c < nvec; c += T) m2 = absmax4(m2, lds_v4(slot + 16 * c));
+      const QuantRow qr = quant_row<QK>(block_max(pair_max(m2), rs.red_max));
+      if (threadIdx.x == 0) a.q_scale[row] = qr.scale;
+      for (int c = threadIdx.x; c < nvec; c += T) store_q<QK>(qrow, c, lds_v4(slot + 16 * c), qr);
+    }
+  });
+}
+
+// ---------------------------------------------------------------- warp rings
+// Rows of at most kWarpRowMaxBytes, reduced only with order-free maxima, run one row
+// per warp: every warp has its own ring of `stages` slots (bulk copies issued by its
+// lane 0, one mbarrier per slot), folds the row max with shuffles and never waits for
+// the other warps of its CTA, so a row costs no CTA barrier and its per-row work
+// (reduction, scale, reciprocal bracket) is shared by 32 threads rather than a row group.
+constexpr uint32_t kWarpRowMaxBytes = 16 * 1024;
+constexpr int kWarpMaxWarps = 32;
+constexpr int kWarpMaxStages = 8;
+constexpr int kWarpRingHeader = kWarpMaxWarps * kWarpMaxStages * 8;   // mbarriers
+
+struct WarpRingGeom {
+  int stages;           // slots per warp (2..kWarpMaxStages)
+  uint32_t slot_bytes;  // one row rounded up to 128 bytes
+  uint32_t row_bytes;   // bytes of the row's bulk copy
+};
+
+// Runs `body(row, slot)` for the rows of this warp: blockIdx.x * W + warp, then every
+// gridDim.x * W rows (W warps per CTA), each warp `stages - 1` rows ahead.
+template <typename Src, typename Body>
+__device__ __forceinline__ void warp_row_loop(uint8_t* smem, const WarpRingGeom& g, int64_t nrows, Src src,
+                                              Body body) {
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int W = blockDim.x >> 5;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem) + warp * kWarpMaxStages;
+  uint8_t* slots = smem + kWarpRingHeader + static_cast<size_t>(warp) * g.stages * g.slot_bytes;
+  const int64_t GW = static_cast<int64_t>(gridDim.x) * W;
+  const int64_t first = static_cast<int64_t>(blockIdx.x) * W + warp;
+  const uint64_t policy = policy_evict_first();
+  int64_t issued = 0;   // lane 0 only
+  if (lane == 0) {
+    for (int i = 0; i < g.stages; ++i) mbar_init(&full[i], 1);
+    fence_mbarrier_init();
+    for (int i = 0; i < g.stages; ++i) {
+      const int64_t r = first + i * GW;
+      if (r >= nrows) break;
+      mbar_arrive_expect_tx(&full[i], g.row_bytes);
+      bulk_load(slots + static_cast<size_t>(i) * g.slot_bytes, src(r), g.row_bytes, &full[i], policy);
+      ++issued;
+    }
+  }
+  __syncwarp();
+  int st = 0;
+  uint32_t ph = 0;
+  int64_t k = 0;
+  const int64_t ahead = static_cast<int64_t>(g.stages) * GW;
+  for (int64_t row = first; row < nrows; row += GW, ++k) {
+    const bool ok = mbar_wait(&full[st], ph, kStatusTimeoutProducer);
+    if (__any_sync(0xFFFFFFFFu, !ok)) break;
+    uint8_t* slot = slots + static_cast<size_t>(st) * g.slot_bytes;
+    body(row, slot);
+    __syncwarp();
+    if (lane == 0) {
+      const int64_t r = row + ahead;
+      if (r < nrows) {
+        fence_proxy_async_smem();   // the warp's reads of the slot precede the copy that refills it
+        mbar_arrive_expect_tx(&full[st], g.row_bytes);
+        bulk_load(slot, src(r), g.row_bytes, &full[st], policy);
+        ++issued;
+      }
+    }
+    if (++st == g.stages) {
+      st = 0;
+      ph ^= 1u;
+    }
+  }
+  // teardown: copies still in flight (only after an abort) must land before exit
+  if (lane == 0) {
+    for (int64_t n = k; n < issued; ++n) {
+      if (!mbar_wait(&full[st], ph, kStatusTimeoutDrain)) break;
+      if (++st == g.stages) {
+        st = 0;
+        ph ^= 1u;
+      }
+    }
+  }
+  __syncwarp();
+}
+
+// Per-token quantisation, one row per warp (rows of at most kWarpRowMaxBytes).
+template <int QK>
+__global__ void __launch_bounds__(1024) quant_rows_warp_kernel(const QuantRowsArgs a, const WarpRingGeom g) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const int lane = threadIdx.x & 31;
+  const int nvec = a.D >> 3;
+  auto src = [&](int64_t r) -> const void* { return a.x + r * a.ld_x; };
+  warp_row_loop(smem, g, a.S, src, [&](int64_t row, const uint8_t* slot) {
+    uint32_t m2 = 0;
+#pragma unroll 4
+    for (int c = lane; c < nvec; c += 32) m2 = absmax4(m2, lds_v4(slot + 16 * c));
+    float m = pair_max(m2);
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, off));
+    const QuantRow qr = quant_row<QK>(m);
+    if (lane == 0) a.q_scale[row] = qr.scale;
+    uint8_t* qrow = static_cast<uint8_t*>(a.q) + row * a.ld_q;
+#pragma unroll 4
+    for (int c = lane; c < nvec; c += 32) store_q<QK>(qrow, c, lds_v4(slot + 16 * c), qr);
   });
 }
 
@@ -407,139 +524,325 @@ __global__ void __launch_bounds__(T) quant_rows_kernel(const QuantRowsArgs a, co
 // Sum of squares: each thread keeps two fp32 accumulators, one for the even and one
 // for the odd element of every bf16 pair, adds its vectors' squares in vector order
 // with a packed FMA, then combines them as (even + odd) before the row reduction.
-template <int T, int MODE>
-__global__ void __launch_bounds__(T) rms_mod_kernel(const RmsArgs a, const RingGeom g) {
+__device__ __forceinline__ float2 row_sumsq_vec(float2 acc, const uint4& u) {
+  float2 v[4];
+  unpack_pairs(u, v);
+#pragma unroll
+  for (int p = 0; p < 4; ++p) acc = fma2_rn(v[p], v[p], acc);
+  return acc;
+}
+
+// h for one vector: (((x * inv) * w) * s) + b; products packed, the add scalar.
+__device__ __forceinline__ void rms_h8(const uint4& xu, float2 inv2, const float2 (&s)[4], const float2 (&b)[4],
+                                       const __nv_bfloat16* w, int c, float2 (&x)[4], float2 (&h)[4]) {
+  unpack_pairs(xu, x);
+  float2 prod[4];
+  if (w) {
+    float2 wv[4];
+    unpack_pairs(ld_v4(w + 8 * c), wv);
+#pragma unroll
+    for (int p = 0; p < 4; ++p) prod[p] = mul2_rn(mul2_rn(mul2_rn(x[p], inv2), wv[p]), s[p]);
+  } else {
+#pragma unroll
+    for (int p = 0; p < 4; ++p) prod[p] = mul2_rn(mul2_rn(x[p], inv2), s[p]);
+  }
+#pragma unroll
+  for (int p = 0; p < 4; ++p) h[p] = make_float2(__fadd_rn(prod[p].x, b[p].x), __fadd_rn(prod[p].y, b[p].y));
+}
+
+// Modulation of one vector of mod row `m`: s = scale (or bf16(1 + scale)), b = shift.
+__device__ __forceinline__ void load_mod8(const RmsArgs& a, int64_t m, int c, float2 (&s)[4], float2 (&b)[4]) {
+  uint4 su = ld_v4(a.scale + m * a.ld_mod + 8 * c);
+  if (!a.scale_is_multiplier)
+    su = make_uint4(one_plus_bf16x2(su.x), one_plus_bf16x2(su.y), one_plus_bf16x2(su.z), one_plus_bf16x2(su.w));
+  unpack_pairs(su, s);
+  unpack_pairs(ld_v4(a.shift + m * a.ld_mod + 8 * c), b);
+}
+
+// Stores of one vector of h: res = bf16(h + x), h itself; returns bf16(h).
+__device__ __forceinline__ uint4 rms_store8(const RmsArgs& a, int64_t row, int c, const float2 (&x)[4],
+                                            const float2 (&h)[4]) {
+  if (a.res) {
+    uint4 ru;
+    ru.x = f2_to_bf2(add2_rn(h[0], x[0]));
+    ru.y = f2_to_bf2(add2_rn(h[1], x[1]));
+    ru.z = f2_to_bf2(add2_rn(h[2], x[2]));
+    ru.w = f2_to_bf2(add2_rn(h[3], x[3]));
+    *reinterpret_cast<uint4*>(a.res + row * a.ld_res + 8 * c) = ru;
+  }
+  const uint4 hu = make_uint4(f2_to_bf2(h[0]), f2_to_bf2(h[1]), f2_to_bf2(h[2]), f2_to_bf2(h[3]));
+  if (a.h) *reinterpret_cast<uint4*>(a.h + row * a.ld_h + 8 * c) = hu;
+  return hu;
+}
+
+__device__ __forceinline__ float absmax_f2x4(float m, const float2 (&h)[4]) {
+#pragma unroll
+  for (int p = 0; p < 4; ++p) m = fmaxf(m, fmaxf(fabsf(h[p].x), fabsf(h[p].y)));
+  return m;
+}
+
+// The modulation vectors are re-read (from L1/L2) for every row: caching them in
+// registers across the rows of one batch element raised register use enough to cost
+// more occupancy than the loads it saved (measured at D=3072).
+template <int V, int MODE>
+__global__ void __launch_bounds__(512) rms_mod_kernel(const RmsArgs a, const RingGeom g) {
   extern __shared__ __align__(1024) uint8_t smem[];
+  const int T = blockDim.x;
   const int nvec = a.D >> 3;
   const float fD = static_cast<float>(a.D);
+  int64_t cur_m = -1;
+  int64_t seg_end = -1;          // first row past the current batch element (rows_per_mod layout)
   auto src = [&](int64_t r, int) -> const void* { return a.x + r * a.ld_x; };
-  row_loop<T>(smem, g, a.S, src, [&](int64_t row, uint8_t* slot, const RingState& rs) {
+  row_loop(smem, g, a.S, src, [&](int64_t row, uint8_t* slot, const RingState& rs) {
     // pass 1: sum of squares in the canonical order
     float2 acc = make_float2(0.f, 0.f);
-    for (int c = threadIdx.x; c < nvec; c += T) {
-      float2 v[4];
-      unpack_pairs(lds_v4(slot + 16 * c), v);
+    if constexpr (V > 0) {
 #pragma unroll
-      for (int p = 0; p < 4; ++p) acc = fma2_rn(v[p], v[p], acc);
+      for (int i = 0; i < V; ++i) {
+        const int c = threadIdx.x + T * i;
+        if (c < nvec) acc = row_sumsq_vec(acc, lds_v4(slot + 16 * c));
+      }
+    } else {
+      for (int c = threadIdx.x; c < nvec; c += T) acc = row_sumsq_vec(acc, lds_v4(slot + 16 * c));
     }
-    const float ss = block_sum<T>(__fadd_rn(acc.x, acc.y), rs.red_sum);
+    const float ss = block_sum(__fadd_rn(acc.x, acc.y), rs.red_sum);
     const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, fD), a.eps)));
     const float2 inv2 = make_float2(inv, inv);
-
-    const int64_t m = a.mod_index ? static_cast<int64_t>(__ldg(a.mod_index + row)) : row / a.rows_per_mod;
-    const __nv_bfloat16* shr = a.shift + m * a.ld_mod;
-    const __nv_bfloat16* scr = a.scale + m * a.ld_mod;
-
-    // pass 2: h (written back over x in the slot), optional res / h stores, amax
+    // each CTA visits rows in increasing order: divide only when a batch element ends
+    int64_t m;
+    if (a.mod_index) {
+      m = static_cast<int64_t>(__ldg(a.mod_index + row));
+    } else if (row < seg_end) {
+      m = cur_m >= 0 ? cur_m : row / a.rows_per_mod;
+    } else {
+      m = row / a.rows_per_mod;
+      seg_end = (m + 1) * a.rows_per_mod;
+    }
+    uint8_t* qrow = static_cast<uint8_t*>(a.q) + row * a.ld_q;
     uint32_t m2 = 0;
     float amax32 = 0.f;
-    for (int c = threadIdx.x; c < nvec; c += T) {
-      const uint4 xu = lds_v4(slot + 16 * c);
-      uint4 su = ld_v4(scr + 8 * c);
-      const uint4 bu = ld_v4(shr + 8 * c);
-      if (!a.scale_is_multiplier)
-        su = make_uint4(one_plus_bf16x2(su.x), one_plus_bf16x2(su.y), one_plus_bf16x2(su.z), one_plus_bf16x2(su.w));
-      float2 x[4], sv[4], bv[4], h[4];
-      unpack_pairs(xu, x);
-      unpack_pairs(su, sv);
-      unpack_pairs(bu, bv);
-      float2 prod[4];
-      if (a.w) {
-        float2 wv[4];
-        unpack_pairs(ld_v4(a.w + 8 * c), wv);
+
+    cur_m = m;
+    if constexpr (V > 0) {
+      uint4 hv[V];
 #pragma unroll
-        for (int p = 0; p < 4; ++p) prod[p] = mul2_rn(mul2_rn(mul2_rn(x[p], inv2), wv[p]), sv[p]);
-      } else {
-#pragma unroll
-        for (int p = 0; p < 4; ++p) prod[p] = mul2_rn(mul2_rn(x[p], inv2), sv[p]);
+      for (int i = 0; i < V; ++i) {
+        const int c = threadIdx.x + T * i;
+        hv[i] = make_uint4(0, 0, 0, 0);
+        if (c < nvec) {
+          float2 x[4], h[4], sm[4], bm[4];
+          load_mod8(a, m, c, sm, bm);
+          rms_h8(lds_v4(slot + 16 * c), inv2, sm, bm, a.w, c, x, h);
+          if constexpr (MODE == kModeTensorwise) amax32 = absmax_f2x4(amax32, h);
+          hv[i] = rms_store8(a, row, c, x, h);
+          m2 = absmax4(m2, hv[i]);
+        }
       }
+      if constexpr (MODE != kModeTensorwise) {
+        constexpr int QK = MODE;
+        const QuantRow qr = quant_row<QK>(block_max(pair_max(m2), rs.red_max));
+        if (threadIdx.x == 0) a.q_scale[row] = qr.scale;
 #pragma unroll
-      for (int p = 0; p < 4; ++p) h[p] = make_float2(__fadd_rn(prod[p].x, bv[p].x), __fadd_rn(prod[p].y, bv[p].y));
-      if (a.res) {
-        uint4 ru;
-        ru.x = f2_to_bf2(add2_rn(h[0], x[0]));
-        ru.y = f2_to_bf2(add2_rn(h[1], x[1]));
-        ru.z = f2_to_bf2(add2_rn(h[2], x[2]));
-        ru.w = f2_to_bf2(add2_rn(h[3], x[3]));
-        *reinterpret_cast<uint4*>(a.res + row * a.ld_res + 8 * c) = ru;
+        for (int i = 0; i < V; ++i) {
+          const int c = threadIdx.x + T * i;
+          if (c < nvec) store_q<QK>(qrow, c, hv[i], qr);
+        }
       }
-      if constexpr (MODE == kModeTensorwise) {
-#pragma unroll
-        for (int p = 0; p < 4; ++p) amax32 = fmaxf(amax32, fmaxf(fabsf(h[p].x), fabsf(h[p].y)));
+    } else {
+      for (int c = threadIdx.x; c < nvec; c += T) {
+        float2 s[4], b[4], x[4], h[4];
+        load_mod8(a, m, c, s, b);
+        rms_h8(lds_v4(slot + 16 * c), inv2, s, b, a.w, c, x, h);
+        if constexpr (MODE == kModeTensorwise) amax32 = absmax_f2x4(amax32, h);
+        const uint4 hu = rms_store8(a, row, c, x, h);
+        m2 = absmax4(m2, hu);
+        *reinterpret_cast<uint4*>(slot + 16 * c) = hu;   // h replaces x in the slot
       }
-      const uint4 hu = make_uint4(f2_to_bf2(h[0]), f2_to_bf2(h[1]), f2_to_bf2(h[2]), f2_to_bf2(h[3]));
-      m2 = absmax4(m2, hu);
-      *reinterpret_cast<uint4*>(slot + 16 * c) = hu;
-      if (a.h) *reinterpret_cast<uint4*>(a.h + row * a.ld_h + 8 * c) = hu;
+      slot_written();
+      if constexpr (MODE != kModeTensorwise) {
+        constexpr int QK = MODE;
+        const QuantRow qr = quant_row<QK>(block_max(pair_max(m2), rs.red_max));   // barrier: h complete
+        if (threadIdx.x == 0) a.q_scale[row] = qr.scale;
+        for (int c = threadIdx.x; c < nvec; c += T) store_q<QK>(qrow, c, lds_v4(slot + 16 * c), qr);
+      }
     }
-    slot_written();
     if constexpr (MODE == kModeTensorwise) {
 #pragma unroll
       for (int off = 16; off >= 1; off >>= 1) amax32 = fmaxf(amax32, __shfl_xor_sync(0xFFFFFFFFu, amax32, off));
       if ((threadIdx.x & 31) == 0 && amax32 > 0.f) atomic_max_nonneg(a.amax, amax32);
+    }
+  });
+}
+
+// RMSNorm + modulation + quantisation, one row per warp (rows of at most
+// kWarpRowMaxBytes).  The sum of squares is the canonical row-group tree of
+// rms_mod_kernel for a group of T threads: lane l plays thread 32 j + l of every warp
+// j < T / 32, so each of those warps' accumulation, butterfly and the left-to-right
+// sum of their partials are the same operations in the same order.  h (and the
+// optional res) is stored per vector, and bf16(h) replaces x in the slot for the
+// quantisation pass.
+template <int MODE>
+__global__ void __launch_bounds__(1024) rms_mod_warp_kernel(const RmsArgs a, const WarpRingGeom g, const int T) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const int lane = threadIdx.x & 31;
+  const int nvec = a.D >> 3;
+  const int nw = T >> 5;
+  const float fD = static_cast<float>(a.D);
+  int64_t cur_m = -1;
+  int64_t seg_end = -1;   // first row past the current batch element (rows_per_mod layout)
+  auto src = [&](int64_t r) -> const void* { return a.x + r * a.ld_x; };
+  warp_row_loop(smem, g, a.S, src, [&](int64_t row, uint8_t* slot) {
+    // pass 1: sum of squares, virtual warp by virtual warp
+    float ss = 0.f;
+    for (int j = 0; j < nw; ++j) {
+      float2 acc = make_float2(0.f, 0.f);
+      for (int c = 32 * j + lane; c < nvec; c += T) acc = row_sumsq_vec(acc, lds_v4(slot + 16 * c));
+      float v = __fadd_rn(acc.x, acc.y);
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xFFFFFFFFu, v, off));
+      ss = j == 0 ? v : __fadd_rn(ss, v);
+    }
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, fD), a.eps)));
+    const float2 inv2 = make_float2(inv, inv);
+    int64_t m;
+    if (a.mod_index) {
+      m = static_cast<int64_t>(__ldg(a.mod_index + row));
+    } else if (row < seg_end) {
+      m = cur_m;
     } else {
+      m = row / a.rows_per_mod;
+      seg_end = (m + 1) * a.rows_per_mod;
+    }
+    cur_m = m;
+    // pass 2: h, its stores, the row max; bf16(h) back into the slot
+    uint32_t m2 = 0;
+    float amax32 = 0.f;
+#pragma unroll 2
+    for (int c = lane; c < nvec; c += 32) {
+      float2 s[4], b[4], x[4], h[4];
+      load_mod8(a, m, c, s, b);
+      rms_h8(lds_v4(slot + 16 * c), inv2, s, b, a.w, c, x, h);
+      if constexpr (MODE == kModeTensorwise) amax32 = absmax_f2x4(amax32, h);
+      const uint4 hu = rms_store8(a, row, c, x, h);
+      m2 = absmax4(m2, hu);
+      if constexpr (MODE != kModeTensorwise) *reinterpret_cast<uint4*>(slot + 16 * c) = hu;
+    }
+    if constexpr (MODE != kModeTensorwise) {
       constexpr int QK = MODE;
-      const float amax = block_max<T>(fmaxf(bf_lo(m2), bf_hi(m2)), rs.red_max);   // barrier: h complete
-      const QuantRow qr = quant_row<QK>(amax);
-      if (threadIdx.x == 0) a.q_scale[row] = qr.scale;
-      quant_row_store<T, QK>(slot, nvec, qr, static_cast<uint8_t*>(a.q) + row * a.ld_q);
+      float mx = pair_max(m2);
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, off));
+      const QuantRow qr = quant_row<QK>(mx);
+      if (lane == 0) a.q_scale[row] = qr.scale;
+      uint8_t* qrow = static_cast<uint8_t*>(a.q) + row * a.ld_q;
+#pragma unroll 4
+      for (int c = lane; c < nvec; c += 32) store_q<QK>(qrow, c, lds_v4(slot + 16 * c), qr);
+    } else {
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) amax32 = fmaxf(amax32, __shfl_xor_sync(0xFFFFFFFFu, amax32, off));
+      if (lane == 0 && amax32 > 0.f) atomic_max_nonneg(a.amax, amax32);
     }
   });
 }
 
 // ---------------------------------------------------------------- SwiGLU
-// act = (g * sigmoid(g)) * u with sigmoid(g) = 1 / (1 + e^-g); e^-g and the reciprocal
-// use the fast hardware approximations (act is compared with the oracle within one
-// bf16 ulp).
-// Approximate reciprocal (max 1 ulp), subnormal results kept (no flush to zero).
-__device__ __forceinline__ float rcp_approx(float x) {
+// act = (g * sigmoid(g)) * u with sigmoid(g) = 1 / (1 + e^-g), in fp32 with the fast
+// hardware exponential and reciprocal (act is compared with the oracle within one bf16
+// ulp):
+//   e   = 2^(-g * log2(e))              ex2.approx.ftz (the change-of-base identity)
+//   d4  = (1 + e) / 4                   one fma: RN(1 + e) scaled exactly by 1/4
+//   r4  = approx(1 / d4) = 4 / (1 + e)  rcp.approx.ftz
+//   act = ((g / 4) * r4) * u            g / 4 is exact for every bf16 g
+// The quarter scaling keeps the reciprocal normal where 1 / (1 + e) itself would be
+// subnormal (g < -87.3: 2^-126 < 4 / (1 + e)), so flushing subnormal reciprocals cannot
+// change act; (g / 4) * r4 is the same real product as g * (1 / (1 + e)).  For e = inf
+// (g < -88.7) r4 = 0 and act is a signed zero, as in fp32 with an IEEE reciprocal.
+__device__ __forceinline__ float ex2_approx(float x) {
   float r;
-  asm("rcp.approx.f32 %0, %1;" : "=f"(r) : "f"(x));
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+__device__ __forceinline__ float rcp_approx_ftz(float x) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
   return r;
 }
 
+constexpr float kLog2E = 1.44269504088896340736f;
+
 __device__ __forceinline__ float2 silu_mul2(float2 g, float2 u) {
-  const float2 e = make_float2(__expf(-g.x), __expf(-g.y));
-  const float2 d = add2_rn(make_float2(1.0f, 1.0f), e);
-  const float2 r = make_float2(rcp_approx(d.x), rcp_approx(d.y));
-  return mul2_rn(mul2_rn(g, r), u);
+  const float2 g4 = mul2_rn(g, make_float2(0.25f, 0.25f));
+  const float2 t = mul2_rn(g4, make_float2(-4.0f * kLog2E, -4.0f * kLog2E));   // = -g * log2(e), same rounding
+  const float2 e = make_float2(ex2_approx(t.x), ex2_approx(t.y));
+  const float2 d4 = fma2_rn(e, make_float2(0.25f, 0.25f), make_float2(0.25f, 0.25f));
+  const float2 r4 = make_float2(rcp_approx_ftz(d4.x), rcp_approx_ftz(d4.y));
+  return mul2_rn(mul2_rn(g4, r4), u);
 }
 
-template <int T, int MODE>
-__global__ void __launch_bounds__(T) swiglu_kernel(const SwigluArgs a, const RingGeom g) {
+// act for one vector from the gate and up rows in the slot; returns bf16(act).
+__device__ __forceinline__ uint4 swiglu8(const uint8_t* slot, const uint8_t* up, int c, float& amax32, bool tensorwise) {
+  float2 gv[4], uv[4], act[4];
+  unpack_pairs(lds_v4(slot + 16 * c), gv);
+  unpack_pairs(lds_v4(up + 16 * c), uv);
+#pragma unroll
+  for (int p = 0; p < 4; ++p) act[p] = silu_mul2(gv[p], uv[p]);
+  if (tensorwise) amax32 = absmax_f2x4(amax32, act);
+  return make_uint4(f2_to_bf2(act[0]), f2_to_bf2(act[1]), f2_to_bf2(act[2]), f2_to_bf2(act[3]));
+}
+
+template <int V, int MODE>
+__global__ void __launch_bounds__(1024) swiglu_kernel(const SwigluArgs a, const RingGeom g) {
   extern __shared__ __align__(1024) uint8_t smem[];
+  const int T = blockDim.x;
   const int nvec = a.F >> 3;
   auto src = [&](int64_t r, int part) -> const void* { return (part ? a.up : a.gate) + r * a.ld_in; };
-  row_loop<T>(smem, g, a.M, src, [&](int64_t row, uint8_t* slot, const RingState& rs) {
+  row_loop(smem, g, a.M, src, [&](int64_t row, uint8_t* slot, const RingState& rs) {
     const uint8_t* up = slot + g.part_bytes;
+    uint8_t* qrow = static_cast<uint8_t*>(a.q) + row * a.ld_q;
     uint32_t m2 = 0;
     float amax32 = 0.f;
-    for (int c = threadIdx.x; c < nvec; c += T) {
-      float2 gv[4], uv[4], act[4];
-      unpack_pairs(lds_v4(slot + 16 * c), gv);
-      unpack_pairs(lds_v4(up + 16 * c), uv);
+    constexpr bool kTw = MODE == kModeTensorwise;
+    if constexpr (V > 0) {
+      uint4 av[V];
 #pragma unroll
-      for (int p = 0; p < 4; ++p) act[p] = silu_mul2(gv[p], uv[p]);
-      if constexpr (MODE == kModeTensorwise) {
-#pragma unroll
-        for (int p = 0; p < 4; ++p) amax32 = fmaxf(amax32, fmaxf(fabsf(act[p].x), fabsf(act[p].y)));
+      for (int i = 0; i < V; ++i) {
+        const int c = threadIdx.x + T * i;
+        av[i] = make_uint4(0, 0, 0, 0);
+        if (c < nvec) {
+          av[i] = swiglu8(slot, up, c, amax32, kTw);
+          m2 = absmax4(m2, av[i]);
+          if (a.act) *reinterpret_cast<uint4*>(a.act + row * a.ld_act + 8 * c) = av[i];
+        }
       }
-      const uint4 au = make_uint4(f2_to_bf2(act[0]), f2_to_bf2(act[1]), f2_to_bf2(act[2]), f2_to_bf2(act[3]));
-      m2 = absmax4(m2, au);
-      *reinterpret_cast<uint4*>(slot + 16 * c) = au;   // act replaces the gate row
-      if (a.act) *reinterpret_cast<uint4*>(a.act + row * a.ld_act + 8 * c) = au;
+      if constexpr (!kTw) {
+        constexpr int QK = MODE;
+        const QuantRow qr = quant_row<QK>(block_max(pair_max(m2), rs.red_max));
+        if (threadIdx.x == 0) a.q_scale[row] = qr.scale;
+#pragma unroll
+        for (int i = 0; i < V; ++i) {
+          const int c = threadIdx.x + T * i;
+          if (c < nvec) store_q<QK>(qrow, c, av[i], qr);
+        }
+      }
+    } else {
+      for (int c = threadIdx.x; c < nvec; c += T) {
+        const uint4 au = swiglu8(slot, up, c, amax32, kTw);
+        m2 = absmax4(m2, au);
+        *reinterpret_cast<uint4*>(slot + 16 * c) = au;   // act replaces the gate row
+        if (a.act) *reinterpret_cast<uint4*>(a.act + row * a.ld_act + 8 * c) = au;
+      }
+      slot_written();
+      if constexpr (!kTw) {
+        constexpr int QK = MODE;
+        const QuantRow qr = quant_row<QK>(block_max(pair_max(m2), rs.red_max));   // barrier: act complete
+        if (threadIdx.x == 0) a.q_scale[row] = qr.scale;
+        for (int c = threadIdx.x; c < nvec; c += T) store_q<QK>(qrow, c, lds_v4(slot + 16 * c), qr);
+      }
     }
-    slot_written();
-    if constexpr (MODE == kModeTensorwise) {
+    if constexpr (kTw) {
 #pragma unroll
       for (int off = 16; off >= 1; off >>= 1) amax32 = fmaxf(amax32, __shfl_xor_sync(0xFFFFFFFFu, amax32, off));
       if ((threadIdx.x & 31) == 0 && amax32 > 0.f) atomic_max_nonneg(a.amax, amax32);
-    } else {
-      constexpr int QK = MODE;
-      const float amax = block_max<T>(fmaxf(bf_lo(m2), bf_hi(m2)), rs.red_max);   // barrier: act complete
-      const QuantRow qr = quant_row<QK>(amax);
-      if (threadIdx.x == 0) a.q_scale[row] = qr.scale;
-      quant_row_store<T, QK>(slot, nvec, qr, static_cast<uint8_t*>(a.q) + row * a.ld_q);
     }
   });
 }

@@ -119,14 +119,14 @@ int launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtenso
   using namespace t8g::gemm;
   static bool attr_done[kMaxDevices] = {};
   auto kern = gemm_dequant_pair_kernel<IN, OUT>;
-  int rc = ensure_smem_attr(kern, dev, P_SMEM_BYTES, attr_done);
+  int rc = ensure_smem_attr(kern, dev, pair_smem_bytes<OUT>(), attr_done);
   if (rc) return rc;
   const int64_t tiles = static_cast<int64_t>((args.M + P_BM - 1) / P_BM) * ((args.N + BN - 1) / BN);
   const int64_t pairs = tiles < sms / 2 ? tiles : sms / 2;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs), 1, 1);
   cfg.blockDim = dim3(NUM_THREADS, 1, 1);
-  cfg.dynamicSmemBytes = P_SMEM_BYTES;
+  cfg.dynamicSmemBytes = pair_smem_bytes<OUT>();
   cfg.stream = stream;
   cfg.attrs = nullptr;   // the kernel declares its cluster shape (2, 1, 1)
   cfg.numAttrs = 0;
@@ -235,22 +235,52 @@ int gemm_entry(int in_kind, const void* x, const void* w, const float* x_scale, 
 }
 
 // ----------------------------------------------------------------- row kernels
-// Threads per row: the smallest power of two in [32, 512] that leaves at most
-// kFastVec 16-byte vectors per thread, else 512 (the oracle restates this rule).
-int row_threads(int64_t D) {
+// Row-group shape: V = max(3, ceil(nvec / 512)) 16-byte vectors per thread and
+// T = 32 * ceil(nvec / (32 V)) threads (nvec = D / 8); kernels are unrolled for V = 3
+// and 4 and generic beyond (kernel parameter 0).  The oracle restates this rule.
+struct RowShape {
+  int T;
+  int V;   // 3, 4, or 0 for the generic kernel
+};
+
+RowShape row_shape(int64_t D) {
   const int64_t nvec = (D + 7) / 8;
-  int t = 32;
-  while (t < 512 && (nvec + t - 1) / t > t8g::rows::kFastVec) t *= 2;
-  return t;
+  int64_t v = (nvec + 511) / 512;
+  if (v < 3) v = 3;
+  int64_t t = 32 * ((nvec + 32 * v - 1) / (32 * v));
+  if (t < 32) t = 32;
+  RowShape r;
+  r.T = static_cast<int>(t);
+  r.V = v <= 4 ? static_cast<int>(v) : 0;
+  return r;
 }
 
-// Ring geometry of a row kernel: `parts` operand rows of D bf16 per slot.
+// Row-group shape of the SwiGLU kernels, whose only reduction is a max (any order):
+// V = max(kSwigluVecs, ceil(nvec / 1024)) vectors per thread and T = 32 * ceil(nvec /
+// (32 V)) <= 1024 threads; V in {2, 3, 6} runs an unrolled kernel, longer rows the
+// generic one.
+constexpr int kSwigluVecs = 3;
+
+RowShape swiglu_shape(int64_t F) {
+  const int64_t nvec = (F + 7) / 8;
+  int64_t v = (nvec + 1023) / 1024;
+  if (v < kSwigluVecs) v = kSwigluVecs;
+  int64_t t = 32 * ((nvec + 32 * v - 1) / (32 * v));
+  if (t < 32) t = 32;
+  RowShape r;
+  r.T = static_cast<int>(t);
+  r.V = (v == 2 || v == 3 || v == 6) ? static_cast<int>(v) : 0;
+  return r;
+}
+
+// Ring geometry of a row kernel: `parts` operand rows of D bf16 per slot (the depth
+// is set at launch).
 t8g::rows::RingGeom ring_geom(int64_t D, int parts) {
   t8g::rows::RingGeom g;
   g.parts = parts;
   g.part_bytes = static_cast<uint32_t>(D * 2);
   g.slot_bytes = (static_cast<uint32_t>(parts) * g.part_bytes + 127u) & ~127u;
-  g.stages = g.slot_bytes <= 12288 ? 4 : g.slot_bytes <= 32768 ? 3 : 2;
+  g.stages = 2;
   return g;
 }
 
@@ -285,43 +315,94 @@ int check_q(const void* q, int64_t ld_q, int64_t D) {
   return T8G_OK;
 }
 
-// Launch a persistent row kernel: grid = min(rows, SMs x resident CTAs).
-template <typename K, typename A>
-int launch_rows(K kern, int T, const A& args, const t8g::rows::RingGeom& g, int64_t rows, int dev, int sms,
-                cudaStream_t st, const char* what) {
-  const size_t smem = ring_smem(g);
-  if (smem > kRowSmemLimit) return fail(T8G_ERR_UNSUPPORTED, "%s: row too long for the shared-memory ring", what);
+// Launch a persistent row kernel.  The ring depth is chosen from the occupancy the
+// kernel gets: at most 16 CTAs per SM share ~216 KB of shared memory, each taking as
+// many slots as fit (2..16), so 150-200 KB of rows are in flight per SM.  Grid =
+// min(rows, SMs x resident CTAs).
+// Raise a row kernel's dynamic shared-memory limit to kRowAttrBytes, once per kernel
+// and device.
+constexpr size_t kRowAttrBytes = 220 * 1024;
+
+template <typename K>
+int ensure_row_attr(K kern, int dev) {
   static std::mutex mu;
   static const void* attr_done[kMaxDevices][64] = {};
-  {
-    std::lock_guard<std::mutex> lk(mu);
-    bool done = false;
-    int slot = 0;
-    for (; slot < 64 && attr_done[dev][slot]; ++slot)
-      if (attr_done[dev][slot] == reinterpret_cast<const void*>(kern)) { done = true; break; }
-    if (!done) {
-      T8G_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kRowSmemLimit),
-                     "cudaFuncSetAttribute(row kernel)");
-      if (slot < 64) attr_done[dev][slot] = reinterpret_cast<const void*>(kern);
-    }
-  }
-  int per_sm = 0;
-  T8G_CHECK_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, T, smem), "occupancy query");
-  if (per_sm < 1) per_sm = 1;
-  const int64_t cap = static_cast<int64_t>(sms) * per_sm;
+  std::lock_guard<std::mutex> lk(mu);
+  int slot = 0;
+  for (; slot < 64 && attr_done[dev][slot]; ++slot)
+    if (attr_done[dev][slot] == reinterpret_cast<const void*>(kern)) return T8G_OK;
+  T8G_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kRowAttrBytes),
+                 "cudaFuncSetAttribute(row kernel)");
+  if (slot < 64) attr_done[dev][slot] = reinterpret_cast<const void*>(kern);
+  return T8G_OK;
+}
+
+template <typename K, typename A>
+int launch_rows(K kern, int T, const A& args, t8g::rows::RingGeom g, int64_t rows, int dev, int sms, cudaStream_t st,
+                const char* what) {
+  using t8g::rows::kMaxStages;
+  using t8g::rows::kRingHeader;
+  int rc = ensure_row_attr(kern, dev);
+  if (rc) return rc;
+  g.stages = 2;
+  if (ring_smem(g) > kRowSmemLimit) return fail(T8G_ERR_UNSUPPORTED, "%s: row too long for the shared-memory ring", what);
+  int occ = 0;
+  T8G_CHECK_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, T, ring_smem(g)), "occupancy query");
+  const int n = occ < 1 ? 1 : occ > 16 ? 16 : occ;
+  const size_t per_cta = (216 * 1024) / n;
+  int stages = static_cast<int>((per_cta > kRingHeader ? per_cta - kRingHeader : 0) / g.slot_bytes);
+  stages = stages < 2 ? 2 : stages > kMaxStages ? kMaxStages : stages;
+  while (stages > 2 && ring_smem(t8g::rows::RingGeom{stages, g.slot_bytes, g.part_bytes, g.parts}) > kRowSmemLimit)
+    --stages;
+  g.stages = stages;
+  const size_t smem = ring_smem(g);
+  T8G_CHECK_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, T, smem), "occupancy query");
+  if (occ < 1) occ = 1;
+  const int64_t cap = static_cast<int64_t>(sms) * occ;
   const unsigned grid = static_cast<unsigned>(rows < cap ? rows : cap);
   kern<<<grid, T, smem, st>>>(args, g);
   T8G_CHECK_CUDA(cudaGetLastError(), what);
   return T8G_OK;
 }
 
-#define T8G_DISPATCH_T(t, CALL)                        \
-  switch (t) {                                         \
-    case 32: { constexpr int T = 32; CALL; break; }    \
-    case 64: { constexpr int T = 64; CALL; break; }    \
-    case 128: { constexpr int T = 128; CALL; break; }  \
-    case 256: { constexpr int T = 256; CALL; break; }  \
-    default: { constexpr int T = 512; CALL; break; }   \
+// Launch a warp-ring row kernel (one row per warp): kWarpStages slots per warp and as
+// many warps per CTA as ~216 KB of shared memory holds (at most 32), one CTA per SM.
+constexpr int kWarpStages = 2;
+
+template <typename K, typename A, typename... Extra>
+int launch_warp_rows(K kern, const A& args, uint32_t row_bytes, int64_t rows, int dev, int sms, cudaStream_t st,
+                     const char* what, Extra... extra) {
+  using namespace t8g::rows;
+  int rc = ensure_row_attr(kern, dev);
+  if (rc) return rc;
+  WarpRingGeom g;
+  g.row_bytes = row_bytes;
+  g.slot_bytes = (row_bytes + 127u) & ~127u;
+  g.stages = kWarpStages;
+  int64_t warps = static_cast<int64_t>(216 * 1024 - kWarpRingHeader) / (static_cast<int64_t>(g.stages) * g.slot_bytes);
+  if (warps > kWarpMaxWarps) warps = kWarpMaxWarps;
+  if (warps < 1) return fail(T8G_ERR_UNSUPPORTED, "%s: row too long for a warp ring", what);
+  int64_t grid = (rows + warps - 1) / warps;
+  if (grid > sms) grid = sms;
+  const size_t smem = kWarpRingHeader + static_cast<size_t>(warps) * g.stages * g.slot_bytes;
+  kern<<<static_cast<unsigned>(grid), static_cast<unsigned>(32 * warps), smem, st>>>(args, g, extra...);
+  T8G_CHECK_CUDA(cudaGetLastError(), what);
+  return T8G_OK;
+}
+
+#define T8G_DISPATCH_SW(v, CALL)                       \
+  switch (v) {                                         \
+    case 2: { constexpr int V = 2; CALL; break; }      \
+    case 3: { constexpr int V = 3; CALL; break; }      \
+    case 6: { constexpr int V = 6; CALL; break; }      \
+    default: { constexpr int V = 0; CALL; break; }     \
+  }
+
+#define T8G_DISPATCH_V(v, CALL)                        \
+  switch (v) {                                         \
+    case 3: { constexpr int V = 3; CALL; break; }      \
+    case 4: { constexpr int V = 4; CALL; break; }      \
+    default: { constexpr int V = 0; CALL; break; }     \
   }
 
 int launch_checked(const char* what) {
@@ -386,11 +467,17 @@ int rms_common(bool tensorwise, const void* x, int64_t ld_x, const void* w, cons
   a.amax = amax;
   a.S = S;
   a.D = static_cast<int>(D);
-  const int t = row_threads(D);
+  const RowShape rsh = row_shape(D);
   const RingGeom g = ring_geom(D, 1);
+  const uint32_t row_bytes = static_cast<uint32_t>(2 * D);
+  const bool warp_rows = row_bytes <= kWarpRowMaxBytes;
   if (tensorwise) {
     T8G_CHECK_CUDA(cudaMemsetAsync(amax, 0, sizeof(float), st), "cudaMemsetAsync(amax)");
-    T8G_DISPATCH_T(t, rc = launch_rows(rms_mod_kernel<T, kModeTensorwise>, T, a, g, S, dev, info.sms, st, "rms_mod phase A"));
+    if (warp_rows)
+      rc = launch_warp_rows(rms_mod_warp_kernel<kModeTensorwise>, a, row_bytes, S, dev, info.sms, st,
+                            "rms_mod phase A", rsh.T);
+    else
+      T8G_DISPATCH_V(rsh.V, rc = launch_rows(rms_mod_kernel<V, kModeTensorwise>, rsh.T, a, g, S, dev, info.sms, st, "rms_mod phase A"));
     if (rc) return rc;
     QuantGivenArgs b;
     b.h = a.h;
@@ -403,10 +490,15 @@ int rms_common(bool tensorwise, const void* x, int64_t ld_x, const void* w, cons
     b.D = a.D;
     return launch_quant_given(b, quant_kind, info.sms, st);
   }
+  if (warp_rows) {
+    if (quant_kind == T8G_QUANT_FP8_E4M3)
+      return launch_warp_rows(rms_mod_warp_kernel<kModeFp8>, a, row_bytes, S, dev, info.sms, st, "rms_mod_quant", rsh.T);
+    return launch_warp_rows(rms_mod_warp_kernel<kModeInt8>, a, row_bytes, S, dev, info.sms, st, "rms_mod_quant", rsh.T);
+  }
   if (quant_kind == T8G_QUANT_FP8_E4M3) {
-    T8G_DISPATCH_T(t, rc = launch_rows(rms_mod_kernel<T, kModeFp8>, T, a, g, S, dev, info.sms, st, "rms_mod_quant"));
+    T8G_DISPATCH_V(rsh.V, rc = launch_rows(rms_mod_kernel<V, kModeFp8>, rsh.T, a, g, S, dev, info.sms, st, "rms_mod_quant"));
   } else {
-    T8G_DISPATCH_T(t, rc = launch_rows(rms_mod_kernel<T, kModeInt8>, T, a, g, S, dev, info.sms, st, "rms_mod_quant"));
+    T8G_DISPATCH_V(rsh.V, rc = launch_rows(rms_mod_kernel<V, kModeInt8>, rsh.T, a, g, S, dev, info.sms, st, "rms_mod_quant"));
   }
   return rc;
 }
@@ -441,11 +533,11 @@ int swiglu_common(bool tensorwise, const void* gate, const void* up, int64_t ld_
   a.amax = amax;
   a.M = M;
   a.F = static_cast<int>(F);
-  const int t = row_threads(F);
+  const RowShape rsh = swiglu_shape(F);
   const RingGeom g = ring_geom(F, 2);
   if (tensorwise) {
     T8G_CHECK_CUDA(cudaMemsetAsync(amax, 0, sizeof(float), st), "cudaMemsetAsync(amax)");
-    T8G_DISPATCH_T(t, rc = launch_rows(swiglu_kernel<T, kModeTensorwise>, T, a, g, M, dev, info.sms, st, "swiglu phase A"));
+    T8G_DISPATCH_SW(rsh.V, rc = launch_rows(swiglu_kernel<V, kModeTensorwise>, rsh.T, a, g, M, dev, info.sms, st, "swiglu phase A"));
     if (rc) return rc;
     QuantGivenArgs b;
     b.h = a.act;
@@ -459,9 +551,9 @@ int swiglu_common(bool tensorwise, const void* gate, const void* up, int64_t ld_
     return launch_quant_given(b, quant_kind, info.sms, st);
   }
   if (quant_kind == T8G_QUANT_FP8_E4M3) {
-    T8G_DISPATCH_T(t, rc = launch_rows(swiglu_kernel<T, kModeFp8>, T, a, g, M, dev, info.sms, st, "swiglu_quant"));
+    T8G_DISPATCH_SW(rsh.V, rc = launch_rows(swiglu_kernel<V, kModeFp8>, rsh.T, a, g, M, dev, info.sms, st, "swiglu_quant"));
   } else {
-    T8G_DISPATCH_T(t, rc = launch_rows(swiglu_kernel<T, kModeInt8>, T, a, g, M, dev, info.sms, st, "swiglu_quant"));
+    T8G_DISPATCH_SW(rsh.V, rc = launch_rows(swiglu_kernel<V, kModeInt8>, rsh.T, a, g, M, dev, info.sms, st, "swiglu_quant"));
   }
   return rc;
 }
@@ -549,12 +641,18 @@ int t8g_quant_rows(const void* x, int64_t ld_x, void* q, int64_t ld_q, float* q_
   a.q_scale = q_scale;
   a.S = S;
   a.D = static_cast<int>(D);
-  const int t = row_threads(D);
+  const uint32_t row_bytes = static_cast<uint32_t>(2 * D);
+  if (row_bytes <= kWarpRowMaxBytes) {
+    if (quant_kind == T8G_QUANT_FP8_E4M3)
+      return launch_warp_rows(quant_rows_warp_kernel<kQuantFp8>, a, row_bytes, S, dev, info.sms, st, "quant_rows");
+    return launch_warp_rows(quant_rows_warp_kernel<kQuantInt8>, a, row_bytes, S, dev, info.sms, st, "quant_rows");
+  }
+  const RowShape rsh = row_shape(D);
   const RingGeom g = ring_geom(D, 1);
   if (quant_kind == T8G_QUANT_FP8_E4M3) {
-    T8G_DISPATCH_T(t, rc = launch_rows(quant_rows_kernel<T, kQuantFp8>, T, a, g, S, dev, info.sms, st, "quant_rows"));
+    T8G_DISPATCH_V(rsh.V, rc = launch_rows(quant_rows_kernel<V, kQuantFp8>, rsh.T, a, g, S, dev, info.sms, st, "quant_rows"));
   } else {
-    T8G_DISPATCH_T(t, rc = launch_rows(quant_rows_kernel<T, kQuantInt8>, T, a, g, S, dev, info.sms, st, "quant_rows"));
+    T8G_DISPATCH_V(rsh.V, rc = launch_rows(quant_rows_kernel<V, kQuantInt8>, rsh.T, a, g, S, dev, info.sms, st, "quant_rows"));
   }
   return rc;
 }
