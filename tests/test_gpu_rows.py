@@ -104,6 +104,28 @@ def test_rms_mod_quant_per_token_bit_exact(ops, kind, S, D, n_mod, with_w):
     np.testing.assert_array_equal(qbits(q, kind), q_ref)
 
 
+@pytest.mark.parametrize("kind", ["int8", "fp8_e4m3"])
+@pytest.mark.parametrize("S,D,rows_per_mod", [(5000, 3072, 37), (4000, 1024, 1), (3001, 4096, 1000),
+                                              (2500, 1536, 2500), (777, 2048, 100)])
+def test_rms_mod_quant_batch_major_rows(ops, kind, S, D, rows_per_mod):
+    """The DiT form (no weight, no h/res, rows_per_mod tokens per batch element) at the row
+    lengths with register-resident kernels, with batch elements shorter and longer than a
+    CTA's block of rows, against the oracle bit for bit."""
+    rng = np.random.default_rng(S + D)
+    n_mod = -(-S // rows_per_mod)
+    x = rng.standard_normal((S, D)).astype(np.float32)
+    x[1] *= 1e3
+    x = O.round_bf16(x)
+    shift = O.round_bf16((rng.standard_normal((n_mod, D)) * 0.1).astype(np.float32))
+    scale = O.round_bf16((rng.standard_normal((n_mod, D)) * 0.1).astype(np.float32))
+    q, qs = ops.rms_mod_quant(bf16_dev(to_bf16_bits(x)), bf16_dev(to_bf16_bits(shift)), bf16_dev(to_bf16_bits(scale)),
+                              rows_per_mod=rows_per_mod, eps=1e-6, kind=kind)
+    q_ref, qs_ref, _, _ = O.rms_mod_quant_per_token(x, shift, scale, rows_per_mod=rows_per_mod, eps=1e-6,
+                                                    kind=KINDS[kind])
+    np.testing.assert_array_equal(qs.cpu().numpy(), qs_ref)
+    np.testing.assert_array_equal(qbits(q, kind), q_ref)
+
+
 def test_rms_mod_quant_config3_full_size(ops):
     """x [2, 56320, 3072] bf16 ~ N(0,1), shift/scale [2, 3072] ~ N(0, 0.1), eps 1e-6,
     fp8 and int8: all rows bit-exact against the oracle (one pass, no h/res)."""

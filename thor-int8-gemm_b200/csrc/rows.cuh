@@ -135,6 +135,24 @@ __device__ __forceinline__ QuantRow quant_row(float amax) {
 // fused, the integers are those of the exact products, which bracket x too.)  Otherwise (a rounding boundary lies within ~2^-21 of
 // x, probability ~2^-17 per value) the lane recomputes its eight values with the
 // IEEE divide.  int8 never needs the +-127 clamp: |x| <= 127 * (1 + 2^-23).
+// The exact path of quant8: cvt(RN(v / scale)) with the IEEE divide, out of line so that
+// the unrolled row loops carry one call instead of eight inlined divides per vector.
+template <int QK>
+__device__ __noinline__ uint2 quant8_divide(float2 v0, float2 v1, float2 v2, float2 v3, float scale) {
+  const float2 v[4] = {v0, v1, v2, v3};
+  uint32_t ca[4];
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    const float qx = __fdiv_rn(v[p].x, scale), qy = __fdiv_rn(v[p].y, scale);
+    if constexpr (QK == kQuantInt8)
+      ca[p] = __byte_perm(__float_as_uint(__fadd_rn(qx, kRoundMagic)), __float_as_uint(__fadd_rn(qy, kRoundMagic)),
+                          0x0040);
+    else
+      ca[p] = cvt_e4m3x2(qx, qy);
+  }
+  return make_uint2(__byte_perm(ca[0], ca[1], 0x5410), __byte_perm(ca[2], ca[3], 0x5410));
+}
+
 template <int QK>
 __device__ __forceinline__ uint2 quant8(const float2 (&v)[4], const QuantRow& qr) {
   uint32_t ca[4], cb[4];
@@ -152,21 +170,9 @@ __device__ __forceinline__ uint2 quant8(const float2 (&v)[4], const QuantRow& qr
       cb[p] = cvt_e4m3x2(b.x, b.y);
     }
   }
-  uint32_t w0 = __byte_perm(ca[0], ca[1], 0x5410), w1 = __byte_perm(ca[2], ca[3], 0x5410);
+  const uint32_t w0 = __byte_perm(ca[0], ca[1], 0x5410), w1 = __byte_perm(ca[2], ca[3], 0x5410);
   const uint32_t u0 = __byte_perm(cb[0], cb[1], 0x5410), u1 = __byte_perm(cb[2], cb[3], 0x5410);
-  if ((w0 != u0) | (w1 != u1)) {
-#pragma unroll
-    for (int p = 0; p < 4; ++p) {
-      const float qx = __fdiv_rn(v[p].x, qr.scale), qy = __fdiv_rn(v[p].y, qr.scale);
-      if constexpr (QK == kQuantInt8)
-        ca[p] = __byte_perm(__float_as_uint(__fadd_rn(qx, kRoundMagic)), __float_as_uint(__fadd_rn(qy, kRoundMagic)),
-                            0x0040);
-      else
-        ca[p] = cvt_e4m3x2(qx, qy);
-    }
-    w0 = __byte_perm(ca[0], ca[1], 0x5410);
-    w1 = __byte_perm(ca[2], ca[3], 0x5410);
-  }
+  if (__builtin_expect((w0 != u0) | (w1 != u1), 0)) return quant8_divide<QK>(v[0], v[1], v[2], v[3], qr.scale);
   return make_uint2(w0, w1);
 }
 
@@ -433,6 +439,8 @@ struct WarpRingGeom {
   int stages;           // slots per warp (2..kWarpMaxStages)
   uint32_t slot_bytes;  // one row rounded up to 128 bytes
   uint32_t row_bytes;   // bytes of the row's bulk copy
+  int64_t cta_rows;     // > 0: CTA b owns rows [b * cta_rows, (b + 1) * cta_rows), its warps
+                        // interleaved; 0: rows are dealt round robin over all warps of the grid
 };
 
 // Runs `body(row, slot)` for the rows of this warp: blockIdx.x * W + warp, then every
@@ -745,6 +753,358 @@ __global__ void __launch_bounds__(1024) rms_mod_warp_kernel(const RmsArgs a, con
   });
 }
 
+// ---------------------------------------------------------------- register-resident warp rows
+// For rows of exactly 32 * NV vectors (D = 256 NV) a warp copies its row from the slot
+// into registers (NV vectors per lane, lane l holding vectors 32 k + l) and refills the
+// slot at once, so the next `stages` rows are in flight while it computes; all
+// indexing is compile-time.
+template <int NV>
+struct RowRegs {
+  uint4 v[NV];
+};
+
+template <typename Src, typename Load, typename Compute>
+__device__ __forceinline__ void warp_row_loop_reg(uint8_t* smem, const WarpRingGeom& g, int64_t nrows, Src src,
+                                                  Load load, Compute compute) {
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int W = blockDim.x >> 5;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem) + warp * kWarpMaxStages;
+  uint8_t* slots = smem + kWarpRingHeader + static_cast<size_t>(warp) * g.stages * g.slot_bytes;
+  int64_t first, GW, end;
+  if (g.cta_rows > 0) {
+    first = static_cast<int64_t>(blockIdx.x) * g.cta_rows + warp;
+    GW = W;
+    end = min(nrows, static_cast<int64_t>(blockIdx.x + 1) * g.cta_rows);
+  } else {
+    first = static_cast<int64_t>(blockIdx.x) * W + warp;
+    GW = static_cast<int64_t>(gridDim.x) * W;
+    end = nrows;
+  }
+  const uint64_t policy = policy_evict_first();
+  int64_t issued = 0;   // lane 0 only
+  if (lane == 0) {
+    for (int i = 0; i < g.stages; ++i) mbar_init(&full[i], 1);
+    fence_mbarrier_init();
+    for (int i = 0; i < g.stages; ++i) {
+      const int64_t r = first + i * GW;
+      if (r >= end) break;
+      mbar_arrive_expect_tx(&full[i], g.row_bytes);
+      bulk_load(slots + static_cast<size_t>(i) * g.slot_bytes, src(r), g.row_bytes, &full[i], policy);
+      ++issued;
+    }
+  }
+  __syncwarp();
+  int st = 0;
+  uint32_t ph = 0;
+  int64_t k = 0;
+  const int64_t ahead = static_cast<int64_t>(g.stages) * GW;
+  for (int64_t row = first; row < end; row += GW, ++k) {
+    const bool ok = mbar_wait(&full[st], ph, kStatusTimeoutProducer);
+    if (__any_sync(0xFFFFFFFFu, !ok)) break;
+    uint8_t* slot = slots + static_cast<size_t>(st) * g.slot_bytes;
+    auto regs = load(slot);
+    __syncwarp();
+    if (lane == 0) {
+      const int64_t r = row + ahead;
+      if (r < end) {
+        fence_proxy_async_smem();   // the warp's reads of the slot precede the copy that refills it
+        mbar_arrive_expect_tx(&full[st], g.row_bytes);
+        bulk_load(slot, src(r), g.row_bytes, &full[st], policy);
+        ++issued;
+      }
+    }
+    if (++st == g.stages) {
+      st = 0;
+      ph ^= 1u;
+    }
+    compute(row, regs);
+  }
+  if (lane == 0) {
+    for (int64_t n = k; n < issued; ++n) {
+      if (!mbar_wait(&full[st], ph, kStatusTimeoutDrain)) break;
+      if (++st == g.stages) {
+        st = 0;
+        ph ^= 1u;
+      }
+    }
+  }
+  __syncwarp();
+}
+
+template <int NV>
+__device__ __forceinline__ RowRegs<NV> load_row_regs(const uint8_t* slot, int lane) {
+  RowRegs<NV> r;
+#pragma unroll
+  for (int k = 0; k < NV; ++k) r.v[k] = lds_v4(slot + 16 * (32 * k + lane));
+  return r;
+}
+
+// Mixed-precision helpers: bf16 operands taken straight from the packed pair (no
+// unpacking), one rounding each.
+// acc.x += lo(u)^2, acc.y += hi(u)^2 (the squares of bf16 values are exact in fp32, so
+// this is the packed FMA of the canonical sum of squares).
+__device__ __forceinline__ float2 sumsq_bf16x2(float2 acc, uint32_t u) {
+  float x, y;
+  asm("{ .reg .b16 lo, hi; mov.b32 {lo, hi}, %2; fma.rn.f32.bf16 %0, lo, lo, %3; fma.rn.f32.bf16 %1, hi, hi, %4; }"
+      : "=f"(x), "=f"(y)
+      : "r"(u), "f"(acc.x), "f"(acc.y));
+  return make_float2(x, y);
+}
+// (p.x + lo(b), p.y + hi(b)), each an IEEE add (an add with an explicit rounding mode is
+// never contracted with the product that feeds it).
+__device__ __forceinline__ float2 add_f32_bf16x2(float2 p, uint32_t b) {
+  float x, y;
+  asm("{ .reg .b16 lo, hi; mov.b32 {lo, hi}, %2; add.rn.f32.bf16 %0, lo, %3; add.rn.f32.bf16 %1, hi, %4; }"
+      : "=f"(x), "=f"(y)
+      : "r"(b), "f"(p.x), "f"(p.y));
+  return make_float2(x, y);
+}
+
+// The row-group size of the canonical sum for a row of `nvec` vectors (the host rule).
+__host__ __device__ constexpr int row_group_threads(int nvec) {
+  return 32 * ((nvec + 32 * ((nvec + 511) / 512 < 3 ? 3 : (nvec + 511) / 512) - 1) /
+               (32 * ((nvec + 511) / 512 < 3 ? 3 : (nvec + 511) / 512)));
+}
+
+// 1 / sqrt(mean(x^2) + eps) of a register-resident row of 256 NV elements, the sum of
+// squares in the canonical tree of a row group of T = row_group_threads threads: lane
+// l's vector 32 k + l belongs to group warp k mod (T / 32), in ascending k, exactly as
+// thread 32 (k mod (T/32)) + l visits it.
+template <int NV>
+__device__ __forceinline__ float row_inv_reg(const RowRegs<NV>& r, float eps) {
+  constexpr int NVEC = 32 * NV;
+  constexpr int NW = row_group_threads(NVEC) / 32;
+  static_assert(NW >= 1 && NW <= NV, "row group shape");
+  float2 acc[NW];
+#pragma unroll
+  for (int j = 0; j < NW; ++j) acc[j] = make_float2(0.f, 0.f);
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    float2 t = acc[k % NW];
+    t = sumsq_bf16x2(t, r.v[k].x);
+    t = sumsq_bf16x2(t, r.v[k].y);
+    t = sumsq_bf16x2(t, r.v[k].z);
+    t = sumsq_bf16x2(t, r.v[k].w);
+    acc[k % NW] = t;
+  }
+  float part[NW];
+#pragma unroll
+  for (int j = 0; j < NW; ++j) part[j] = __fadd_rn(acc[j].x, acc[j].y);
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) {
+#pragma unroll
+    for (int j = 0; j < NW; ++j) part[j] = __fadd_rn(part[j], __shfl_xor_sync(0xFFFFFFFFu, part[j], off));
+  }
+  float ss = part[0];
+#pragma unroll
+  for (int j = 1; j < NW; ++j) ss = __fadd_rn(ss, part[j]);
+  return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(8 * NVEC)), eps)));
+}
+
+// max(m, |a|, |b|) in one three-input max.
+__device__ __forceinline__ float max3_abs(float m, float a, float b) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(m), "f"(fabsf(a)), "f"(fabsf(b)));
+  return d;
+}
+
+// h for one vector from x, inv, the fp32 multiplier pairs s and the packed bf16 shift:
+// h = RN(RN(RN(x * inv) * s) + b); returns bf16(h) and folds |h| into amax.
+__device__ __forceinline__ uint4 rms_h_simple8(const uint4& xu, float2 inv2, const float2 (&s)[4], const uint4& bu,
+                                               float& amax) {
+  const uint32_t xw[4] = {xu.x, xu.y, xu.z, xu.w};
+  const uint32_t bw[4] = {bu.x, bu.y, bu.z, bu.w};
+  uint32_t hw[4];
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    const float2 h = add_f32_bf16x2(mul2_rn(mul2_rn(bf2_to_f2(xw[p]), inv2), s[p]), bw[p]);
+    amax = max3_abs(amax, h.x, h.y);
+    hw[p] = f2_to_bf2(h);
+  }
+  return make_uint4(hw[0], hw[1], hw[2], hw[3]);
+}
+
+// One vector of the h pass of rms_mod_simple_kernel for a row whose batch element is
+// not the CTA's cached one: modulation read from global memory.  Out of line (rare), with
+// everything passed by value so that the row stays in registers.
+__device__ __noinline__ uint4 rms_h_simple_global8(const __nv_bfloat16* srow, const __nv_bfloat16* brow, int c, uint4 xu,
+                                                   float inv, float* amax) {
+  const uint4 su = ld_v4(srow + 8 * c);
+  float2 sf[4];
+  unpack_pairs(make_uint4(one_plus_bf16x2(su.x), one_plus_bf16x2(su.y), one_plus_bf16x2(su.z), one_plus_bf16x2(su.w)),
+               sf);
+  float m = *amax;
+  const uint4 hu = rms_h_simple8(xu, make_float2(inv, inv), sf, ld_v4(brow + 8 * c), m);
+  *amax = m;
+  return hu;
+}
+
+// RMSNorm + adaLN modulation + per-token quantisation in the DiT form (no norm weight, no h
+// or res outputs, s = bf16(1 + scale), batch-major tokens with rows_per_mod tokens per
+// batch element) for rows of 256 NV elements held in registers.  Each CTA owns a
+// contiguous block of rows and keeps the modulation of the batch element holding the
+// block's middle row in shared memory (s as fp32, the shift as bf16); rows of another
+// batch element (a block straddling a boundary) read theirs from global memory.
+template <int NV, int QK>
+__global__ void __launch_bounds__(512, 1) rms_mod_simple_kernel(const RmsArgs a, const WarpRingGeom g) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  constexpr int NVEC = 32 * NV;
+  constexpr int D = 8 * NVEC;
+  const int lane = threadIdx.x & 31;
+  const int W = blockDim.x >> 5;
+  // cache: s of elements 8c..8c+3 at cache_lo[c], 8c+4..8c+7 at cache_hi[c] (lane-contiguous
+  // 16-byte reads), then the bf16 shift
+  float4* cache_lo = reinterpret_cast<float4*>(smem + kWarpRingHeader + static_cast<size_t>(W) * g.stages * g.slot_bytes);
+  float4* cache_hi = cache_lo + NVEC;
+  uint4* cache_b = reinterpret_cast<uint4*>(cache_hi + NVEC);
+  const int64_t r0 = static_cast<int64_t>(blockIdx.x) * g.cta_rows;
+  const int64_t r1 = min(a.S, r0 + g.cta_rows);
+  const int64_t cm = r0 < r1 ? ((r0 + r1 - 1) >> 1) / a.rows_per_mod : -1;
+  if (cm >= 0) {
+    for (int c = threadIdx.x; c < NVEC; c += blockDim.x) {
+      const uint4 su = ld_v4(a.scale + cm * a.ld_mod + 8 * c);
+      float2 sf[4];
+      unpack_pairs(
+          make_uint4(one_plus_bf16x2(su.x), one_plus_bf16x2(su.y), one_plus_bf16x2(su.z), one_plus_bf16x2(su.w)), sf);
+      cache_lo[c] = make_float4(sf[0].x, sf[0].y, sf[1].x, sf[1].y);
+      cache_hi[c] = make_float4(sf[2].x, sf[2].y, sf[3].x, sf[3].y);
+      cache_b[c] = ld_v4(a.shift + cm * a.ld_mod + 8 * c);
+    }
+  }
+  __syncthreads();
+  int64_t cur_m = -1;
+  int64_t seg_end = -1;
+  auto src = [&](int64_t r) -> const void* { return a.x + r * a.ld_x; };
+  warp_row_loop_reg(
+      smem, g, a.S, src, [&](const uint8_t* slot) { return load_row_regs<NV>(slot, lane); },
+      [&](int64_t row, RowRegs<NV>& r) {
+        const float inv = row_inv_reg<NV>(r, a.eps);
+        int64_t m;
+        if (row < seg_end) {
+          m = cur_m;
+        } else {
+          m = row / a.rows_per_mod;
+          seg_end = (m + 1) * a.rows_per_mod;
+        }
+        cur_m = m;
+        float amax = 0.f;
+        if (m == cm) {
+          const float2 inv2 = make_float2(inv, inv);
+#pragma unroll
+          for (int k = 0; k < NV; ++k) {
+            const int c = 32 * k + lane;
+            const float4 s0 = cache_lo[c];
+            const float4 s1 = cache_hi[c];
+            const float2 sf[4] = {make_float2(s0.x, s0.y), make_float2(s0.z, s0.w), make_float2(s1.x, s1.y),
+                                  make_float2(s1.z, s1.w)};
+            r.v[k] = rms_h_simple8(r.v[k], inv2, sf, cache_b[c], amax);
+          }
+        } else {
+          const __nv_bfloat16* srow = a.scale + m * a.ld_mod;
+          const __nv_bfloat16* brow = a.shift + m * a.ld_mod;
+#pragma unroll
+          for (int k = 0; k < NV; ++k) r.v[k] = rms_h_simple_global8(srow, brow, 32 * k + lane, r.v[k], inv, &amax);
+        }
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, off));
+        // max |bf16(h)| = bf16(max |h|): rounding is monotone and symmetric
+        const QuantRow qr = quant_row<QK>(__bfloat162float(__float2bfloat16_rn(amax)));
+        if (lane == 0) a.q_scale[row] = qr.scale;
+        uint8_t* qrow = static_cast<uint8_t*>(a.q) + row * a.ld_q;
+#pragma unroll
+        for (int k = 0; k < NV; ++k) store_q<QK>(qrow, 32 * k + lane, r.v[k], qr);
+      });
+}
+
+// RMSNorm + modulation + quantisation (every option of the entry point: norm weight,
+// mod_index, scale as multiplier, h / res outputs, tensorwise phase A) for rows of 256 NV
+// elements held in registers.
+template <int NV, int MODE>
+__global__ void __launch_bounds__(512, 1) rms_mod_warp_reg_kernel(const RmsArgs a, const WarpRingGeom g) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const int lane = threadIdx.x & 31;
+  int64_t cur_m = -1;
+  int64_t seg_end = -1;
+  auto src = [&](int64_t r) -> const void* { return a.x + r * a.ld_x; };
+  warp_row_loop_reg(
+      smem, g, a.S, src, [&](const uint8_t* slot) { return load_row_regs<NV>(slot, lane); },
+      [&](int64_t row, RowRegs<NV>& r) {
+        const float inv = row_inv_reg<NV>(r, a.eps);
+        const float2 inv2 = make_float2(inv, inv);
+        int64_t m;
+        if (a.mod_index) {
+          m = static_cast<int64_t>(__ldg(a.mod_index + row));
+        } else if (row < seg_end) {
+          m = cur_m;
+        } else {
+          m = row / a.rows_per_mod;
+          seg_end = (m + 1) * a.rows_per_mod;
+        }
+        cur_m = m;
+        const __nv_bfloat16* srow = a.scale + m * a.ld_mod;
+        const __nv_bfloat16* brow = a.shift + m * a.ld_mod;
+        uint32_t m2 = 0;
+        float amax32 = 0.f;
+#pragma unroll
+        for (int k = 0; k < NV; ++k) {
+          const int c = 32 * k + lane;
+          uint4 su = ld_v4(srow + 8 * c);
+          const uint4 bu = ld_v4(brow + 8 * c);
+          if (!a.scale_is_multiplier)
+            su = make_uint4(one_plus_bf16x2(su.x), one_plus_bf16x2(su.y), one_plus_bf16x2(su.z),
+                            one_plus_bf16x2(su.w));
+          const uint32_t xw[4] = {r.v[k].x, r.v[k].y, r.v[k].z, r.v[k].w};
+          const uint32_t sw[4] = {su.x, su.y, su.z, su.w};
+          const uint32_t bw[4] = {bu.x, bu.y, bu.z, bu.w};
+          uint4 wu = make_uint4(0, 0, 0, 0);
+          if (a.w) wu = ld_v4(a.w + 8 * c);
+          const uint32_t ww[4] = {wu.x, wu.y, wu.z, wu.w};
+          float2 h[4], x[4];
+#pragma unroll
+          for (int p = 0; p < 4; ++p) {
+            x[p] = bf2_to_f2(xw[p]);
+            float2 t = mul2_rn(x[p], inv2);
+            if (a.w) t = mul2_rn(t, bf2_to_f2(ww[p]));
+            t = mul2_rn(t, bf2_to_f2(sw[p]));
+            h[p] = add_f32_bf16x2(t, bw[p]);
+          }
+          if constexpr (MODE == kModeTensorwise) amax32 = absmax_f2x4(amax32, h);
+          const uint4 hu = make_uint4(f2_to_bf2(h[0]), f2_to_bf2(h[1]), f2_to_bf2(h[2]), f2_to_bf2(h[3]));
+          {
+            if (a.res) {
+              uint4 ru;
+              ru.x = f2_to_bf2(add2_rn(h[0], x[0]));
+              ru.y = f2_to_bf2(add2_rn(h[1], x[1]));
+              ru.z = f2_to_bf2(add2_rn(h[2], x[2]));
+              ru.w = f2_to_bf2(add2_rn(h[3], x[3]));
+              *reinterpret_cast<uint4*>(a.res + row * a.ld_res + 8 * c) = ru;
+            }
+            if (a.h) *reinterpret_cast<uint4*>(a.h + row * a.ld_h + 8 * c) = hu;
+          }
+          m2 = absmax4(m2, hu);
+          r.v[k] = hu;
+          // keep the modulation loads of at most four vectors in flight (register budget)
+          if ((k & 3) == 3) asm volatile("" ::: "memory");
+        }
+        if constexpr (MODE != kModeTensorwise) {
+          constexpr int QK = MODE;
+          float mx = pair_max(m2);
+#pragma unroll
+          for (int off = 16; off >= 1; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, off));
+          const QuantRow qr = quant_row<QK>(mx);
+          if (lane == 0) a.q_scale[row] = qr.scale;
+          uint8_t* qrow = static_cast<uint8_t*>(a.q) + row * a.ld_q;
+#pragma unroll
+          for (int k = 0; k < NV; ++k) store_q<QK>(qrow, 32 * k + lane, r.v[k], qr);
+        } else {
+#pragma unroll
+          for (int off = 16; off >= 1; off >>= 1) amax32 = fmaxf(amax32, __shfl_xor_sync(0xFFFFFFFFu, amax32, off));
+          if (lane == 0 && amax32 > 0.f) atomic_max_nonneg(a.amax, amax32);
+        }
+      });
+}
+
 // ---------------------------------------------------------------- SwiGLU
 // act = (g * sigmoid(g)) * u with sigmoid(g) = 1 / (1 + e^-g), in fp32 with the fast
 // hardware exponential and reciprocal (act is compared with the oracle within one bf16
@@ -770,8 +1130,19 @@ __device__ __forceinline__ float rcp_approx_ftz(float x) {
 
 constexpr float kLog2E = 1.44269504088896340736f;
 
-__device__ __forceinline__ float2 silu_mul2(float2 g, float2 u) {
-  const float2 g4 = mul2_rn(g, make_float2(0.25f, 0.25f));
+// (lo(g) / 4, hi(g) / 4) straight from a packed bf16 pair: one mixed-precision fma per
+// value, g * 0.25 + (-0), exact (the sign of a zero product is kept).
+__device__ __forceinline__ float2 quarter_bf16x2(uint32_t g) {
+  float x, y;
+  asm("{ .reg .b16 lo, hi, q; mov.b32 {lo, hi}, %2; mov.b16 q, 0x3E80;"
+      " fma.rn.f32.bf16 %0, lo, q, 0f80000000; fma.rn.f32.bf16 %1, hi, q, 0f80000000; }"
+      : "=f"(x), "=f"(y)
+      : "r"(g));
+  return make_float2(x, y);
+}
+
+// g4 = g / 4 (exact), u: one packed pair of gate / up values.
+__device__ __forceinline__ float2 silu_mul2(float2 g4, float2 u) {
   const float2 t = mul2_rn(g4, make_float2(-4.0f * kLog2E, -4.0f * kLog2E));   // = -g * log2(e), same rounding
   const float2 e = make_float2(ex2_approx(t.x), ex2_approx(t.y));
   const float2 d4 = fma2_rn(e, make_float2(0.25f, 0.25f), make_float2(0.25f, 0.25f));
@@ -781,11 +1152,12 @@ __device__ __forceinline__ float2 silu_mul2(float2 g, float2 u) {
 
 // act for one vector from the gate and up rows in the slot; returns bf16(act).
 __device__ __forceinline__ uint4 swiglu8(const uint8_t* slot, const uint8_t* up, int c, float& amax32, bool tensorwise) {
-  float2 gv[4], uv[4], act[4];
-  unpack_pairs(lds_v4(slot + 16 * c), gv);
+  float2 uv[4], act[4];
+  const uint4 gu = lds_v4(slot + 16 * c);
+  const uint32_t gw[4] = {gu.x, gu.y, gu.z, gu.w};
   unpack_pairs(lds_v4(up + 16 * c), uv);
 #pragma unroll
-  for (int p = 0; p < 4; ++p) act[p] = silu_mul2(gv[p], uv[p]);
+  for (int p = 0; p < 4; ++p) act[p] = silu_mul2(quarter_bf16x2(gw[p]), uv[p]);
   if (tensorwise) amax32 = absmax_f2x4(amax32, act);
   return make_uint4(f2_to_bf2(act[0]), f2_to_bf2(act[1]), f2_to_bf2(act[2]), f2_to_bf2(act[3]));
 }

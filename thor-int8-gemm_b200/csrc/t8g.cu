@@ -369,9 +369,18 @@ int launch_rows(K kern, int T, const A& args, t8g::rows::RingGeom g, int64_t row
 // many warps per CTA as ~216 KB of shared memory holds (at most 32), one CTA per SM.
 constexpr int kWarpStages = 2;
 
+// `tail_bytes` of shared memory follow the rings (a kernel's own table); with
+// `contiguous`, CTA b owns rows [b * cta_rows, (b + 1) * cta_rows) instead of a round-robin
+// share.
+struct WarpLaunch {
+  int max_warps = t8g::rows::kWarpMaxWarps;
+  size_t tail_bytes = 0;
+  bool contiguous = false;
+};
+
 template <typename K, typename A, typename... Extra>
 int launch_warp_rows(K kern, const A& args, uint32_t row_bytes, int64_t rows, int dev, int sms, cudaStream_t st,
-                     const char* what, Extra... extra) {
+                     const WarpLaunch& opt, const char* what, Extra... extra) {
   using namespace t8g::rows;
   int rc = ensure_row_attr(kern, dev);
   if (rc) return rc;
@@ -379,16 +388,37 @@ int launch_warp_rows(K kern, const A& args, uint32_t row_bytes, int64_t rows, in
   g.row_bytes = row_bytes;
   g.slot_bytes = (row_bytes + 127u) & ~127u;
   g.stages = kWarpStages;
-  int64_t warps = static_cast<int64_t>(216 * 1024 - kWarpRingHeader) / (static_cast<int64_t>(g.stages) * g.slot_bytes);
-  if (warps > kWarpMaxWarps) warps = kWarpMaxWarps;
+  const int64_t budget = static_cast<int64_t>(216 * 1024 - kWarpRingHeader) - static_cast<int64_t>(opt.tail_bytes);
+  int64_t warps = budget / (static_cast<int64_t>(g.stages) * g.slot_bytes);
+  if (warps > opt.max_warps) warps = opt.max_warps;
   if (warps < 1) return fail(T8G_ERR_UNSUPPORTED, "%s: row too long for a warp ring", what);
   int64_t grid = (rows + warps - 1) / warps;
   if (grid > sms) grid = sms;
-  const size_t smem = kWarpRingHeader + static_cast<size_t>(warps) * g.stages * g.slot_bytes;
+  g.cta_rows = opt.contiguous ? (rows + grid - 1) / grid : 0;
+  const size_t smem = kWarpRingHeader + static_cast<size_t>(warps) * g.stages * g.slot_bytes + opt.tail_bytes;
   kern<<<static_cast<unsigned>(grid), static_cast<unsigned>(32 * warps), smem, st>>>(args, g, extra...);
   T8G_CHECK_CUDA(cudaGetLastError(), what);
   return T8G_OK;
 }
+
+// Rows of D = 256 NV elements with these NV run the register-resident warp kernels
+// (at most kRegWarps warps per CTA: their launch bound).
+constexpr int kRegWarps = 16;
+
+int reg_nv(int64_t D) {
+  if (D % 256) return 0;
+  const int64_t nv = D / 256;
+  return (nv == 4 || nv == 6 || nv == 8 || nv == 12 || nv == 16) ? static_cast<int>(nv) : 0;
+}
+
+#define T8G_DISPATCH_NV(nv, CALL)                      \
+  switch (nv) {                                        \
+    case 4: { constexpr int NV = 4; CALL; break; }     \
+    case 6: { constexpr int NV = 6; CALL; break; }     \
+    case 8: { constexpr int NV = 8; CALL; break; }     \
+    case 12: { constexpr int NV = 12; CALL; break; }   \
+    default: { constexpr int NV = 16; CALL; break; }   \
+  }
 
 #define T8G_DISPATCH_SW(v, CALL)                       \
   switch (v) {                                         \
@@ -471,11 +501,18 @@ int rms_common(bool tensorwise, const void* x, int64_t ld_x, const void* w, cons
   const RingGeom g = ring_geom(D, 1);
   const uint32_t row_bytes = static_cast<uint32_t>(2 * D);
   const bool warp_rows = row_bytes <= kWarpRowMaxBytes;
+  const int nv = reg_nv(D);
+  const bool simple = !w && !h && !res && !mod_index && !scale_is_multiplier;
+  WarpLaunch reg_launch;
+  reg_launch.max_warps = kRegWarps;
   if (tensorwise) {
     T8G_CHECK_CUDA(cudaMemsetAsync(amax, 0, sizeof(float), st), "cudaMemsetAsync(amax)");
-    if (warp_rows)
+    if (nv) {
+      T8G_DISPATCH_NV(nv, rc = launch_warp_rows(rms_mod_warp_reg_kernel<NV, kModeTensorwise>, a, row_bytes, S,
+                                                dev, info.sms, st, reg_launch, "rms_mod phase A"));
+    } else if (warp_rows)
       rc = launch_warp_rows(rms_mod_warp_kernel<kModeTensorwise>, a, row_bytes, S, dev, info.sms, st,
-                            "rms_mod phase A", rsh.T);
+                            WarpLaunch{}, "rms_mod phase A", rsh.T);
     else
       T8G_DISPATCH_V(rsh.V, rc = launch_rows(rms_mod_kernel<V, kModeTensorwise>, rsh.T, a, g, S, dev, info.sms, st, "rms_mod phase A"));
     if (rc) return rc;
@@ -490,10 +527,32 @@ int rms_common(bool tensorwise, const void* x, int64_t ld_x, const void* w, cons
     b.D = a.D;
     return launch_quant_given(b, quant_kind, info.sms, st);
   }
+  if (nv) {
+    const bool fp8 = quant_kind == T8G_QUANT_FP8_E4M3;
+    if (simple) {
+      WarpLaunch o = reg_launch;
+      o.tail_bytes = static_cast<size_t>(6 * D);   // fp32 multiplier + bf16 shift of one batch element
+      o.contiguous = true;
+      if (fp8) {
+        T8G_DISPATCH_NV(nv, rc = launch_warp_rows(rms_mod_simple_kernel<NV, kQuantFp8>, a, row_bytes, S, dev,
+                                                  info.sms, st, o, "rms_mod_quant"));
+      } else {
+        T8G_DISPATCH_NV(nv, rc = launch_warp_rows(rms_mod_simple_kernel<NV, kQuantInt8>, a, row_bytes, S, dev,
+                                                  info.sms, st, o, "rms_mod_quant"));
+      }
+    } else if (fp8) {
+      T8G_DISPATCH_NV(nv, rc = launch_warp_rows(rms_mod_warp_reg_kernel<NV, kModeFp8>, a, row_bytes, S, dev,
+                                                info.sms, st, reg_launch, "rms_mod_quant"));
+    } else {
+      T8G_DISPATCH_NV(nv, rc = launch_warp_rows(rms_mod_warp_reg_kernel<NV, kModeInt8>, a, row_bytes, S, dev,
+                                                info.sms, st, reg_launch, "rms_mod_quant"));
+    }
+    return rc;
+  }
   if (warp_rows) {
     if (quant_kind == T8G_QUANT_FP8_E4M3)
-      return launch_warp_rows(rms_mod_warp_kernel<kModeFp8>, a, row_bytes, S, dev, info.sms, st, "rms_mod_quant", rsh.T);
-    return launch_warp_rows(rms_mod_warp_kernel<kModeInt8>, a, row_bytes, S, dev, info.sms, st, "rms_mod_quant", rsh.T);
+      return launch_warp_rows(rms_mod_warp_kernel<kModeFp8>, a, row_bytes, S, dev, info.sms, st, WarpLaunch{}, "rms_mod_quant", rsh.T);
+    return launch_warp_rows(rms_mod_warp_kernel<kModeInt8>, a, row_bytes, S, dev, info.sms, st, WarpLaunch{}, "rms_mod_quant", rsh.T);
   }
   if (quant_kind == T8G_QUANT_FP8_E4M3) {
     T8G_DISPATCH_V(rsh.V, rc = launch_rows(rms_mod_kernel<V, kModeFp8>, rsh.T, a, g, S, dev, info.sms, st, "rms_mod_quant"));
@@ -644,8 +703,8 @@ int t8g_quant_rows(const void* x, int64_t ld_x, void* q, int64_t ld_q, float* q_
   const uint32_t row_bytes = static_cast<uint32_t>(2 * D);
   if (row_bytes <= kWarpRowMaxBytes) {
     if (quant_kind == T8G_QUANT_FP8_E4M3)
-      return launch_warp_rows(quant_rows_warp_kernel<kQuantFp8>, a, row_bytes, S, dev, info.sms, st, "quant_rows");
-    return launch_warp_rows(quant_rows_warp_kernel<kQuantInt8>, a, row_bytes, S, dev, info.sms, st, "quant_rows");
+      return launch_warp_rows(quant_rows_warp_kernel<kQuantFp8>, a, row_bytes, S, dev, info.sms, st, WarpLaunch{}, "quant_rows");
+    return launch_warp_rows(quant_rows_warp_kernel<kQuantInt8>, a, row_bytes, S, dev, info.sms, st, WarpLaunch{}, "quant_rows");
   }
   const RowShape rsh = row_shape(D);
   const RingGeom g = ring_geom(D, 1);
