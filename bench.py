@@ -350,6 +350,125 @@ def time_rows(torch, ops, dev, steps, warmup, stream):
     return res
 
 
+def _event_ms(torch, stream, fn, steps, warmup):
+    """Mean device time of fn() over `steps` calls after `warmup`, CUDA events on `stream`."""
+    with torch.cuda.stream(stream):
+        for _ in range(warmup):
+            fn()
+        stream.synchronize()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(steps):
+            fn()
+        b.record(stream)
+        b.synchronize()
+    return a.elapsed_time(b) / steps
+
+
+def time_mlp_chain(torch, ops, dev, steps, warmup, stream, seed):
+    """DiT SwiGLU MLP, hidden 3072 / FFN 12288 on 32768 tokens: int8 up-GEMM (N 24576, bf16
+    out) -> SwiGLU + per-token int8 quant -> int8 down-GEMM (K 12288, N 3072)."""
+    M, H, F = 32768, 3072, 12288
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(seed)
+    xq, xs = make_activation(torch, ops, M, H, gen, dev, torch.zeros(0, dtype=torch.long, device=dev), "int8")
+    wu, wus = make_weight(torch, ops, 2 * F, H, gen, dev, "int8")
+    wd, wds = make_weight(torch, ops, H, F, gen, dev, "int8")
+    bu = (torch.randn(2 * F, generator=gen, device=dev) * 0.01).to(torch.bfloat16)
+    bd = (torch.randn(H, generator=gen, device=dev) * 0.01).to(torch.bfloat16)
+    y = torch.empty(M, 2 * F, dtype=torch.bfloat16, device=dev)
+    out = torch.empty(M, H, dtype=torch.bfloat16, device=dev)
+
+    def up():
+        ops.gemm_dequant(xq, wu, xs, wus, bu, out=y, stream=stream)
+
+    def act():
+        return ops.swiglu_quant_fc1(y, kind="int8", stream=stream)
+
+    q, qs = act()
+
+    def down():
+        ops.gemm_dequant(q, wd, qs, wds, bd, out=out, stream=stream)
+
+    def chain():
+        up()
+        a, s_ = act()
+        ops.gemm_dequant(a, wd, s_, wds, bd, out=out, stream=stream)
+
+    ms = _event_ms(torch, stream, chain, steps, warmup)
+    parts = {k: round(_event_ms(torch, stream, f, steps, 1), 4) for k, f in (("up_gemm", up), ("swiglu_quant", act),
+                                                                              ("down_gemm", down))}
+    ops_chain = 2.0 * M * H * 2 * F + 2.0 * M * F * H
+    return {"ms": round(ms, 4), "tops": round(ops_chain / (ms / 1e3) / 1e12, 1), "parts_ms": parts,
+            "shape": "x [32768, 3072] -> [32768, 24576] -> act [32768, 12288] -> [32768, 3072]"}
+
+
+def time_dit_block(torch, dev, steps, warmup, stream, seed, tokens=112640, batch=2):
+    """Synthetic DiT block (hidden 3072, 24 heads x 128, SwiGLU FFN 12288, adaLN from a
+    [B, 6*3072] N(0, 0.1) conditioning) over `tokens` tokens: the whole block with torch SDPA
+    attention, and the same block with attention replaced by a pass-through of the values
+    (the linear layers and norm/quant ops alone)."""
+    from thor_int8_gemm_b200 import dit
+    torch.manual_seed(seed)
+    blk = dit.DiTBlock(3072, 24, 12288, kind="int8", device=dev, seed=seed)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(seed + 1)
+    x = torch.randn(tokens, 3072, generator=gen, device=dev).to(torch.bfloat16)
+    cond = (torch.randn(batch, 6 * 3072, generator=gen, device=dev) * 0.1).to(torch.bfloat16)
+
+    def values_only(qkv, b):
+        return qkv[:, 2 * 3072:]
+
+    full_ms = _event_ms(torch, stream, lambda: blk(x, cond, batch), steps, warmup)
+    lin_ms = _event_ms(torch, stream, lambda: blk.linears_and_norms(x, cond, batch, attn_fn=values_only), steps, warmup)
+    lin_ops = blk.linear_ops(tokens)
+    return {"tokens": tokens, "batch": batch, "block_ms": round(full_ms, 3),
+            "linears_and_norms_ms": round(lin_ms, 3), "linear_tops": round(lin_ops / (lin_ms / 1e3) / 1e12, 1),
+            "note": "block_ms includes torch SDPA attention (outside the hot path)"}
+
+
+def time_reference_path_gpu(torch, items, steps, stream):
+    """The reference's `_gemm_intmm` algorithm on this GPU (src/ck_int8_patch_intmm.py:63-71):
+    torch._int_mm to an int32 [M, N] intermediate, then the eager fp32 epilogue; restated
+    here with torch ops, for comparison with the fused kernel on the same inputs."""
+    def run_one(it):
+        acc = torch._int_mm(it["x"], it["w"].t())
+        o = acc.float() * it["xs"].view(-1, 1)
+        o = o * it["ws"].view(1, -1)
+        o = o + it["bias"].float().view(1, -1)
+        return o.to(torch.bfloat16)
+
+    ms = 0.0
+    for it in items:
+        ms += _event_ms(torch, stream, lambda: run_one(it), steps, 1)
+        torch.cuda.empty_cache()
+    return {"step_ms": round(ms, 3), "tops": round(ops_of(SHAPES) / (ms / 1e3) / 1e12, 1),
+            "what": "torch._int_mm + fp32 eager epilogue (the reference's cuBLAS path), same sweep"}
+
+
+def cpu_row_samples(O, rows=512):
+    """The oracle's fp32 norm/mod/quant and SwiGLU/quant on a bounded sample, GB/s of the
+    kernels' algorithmic bytes (the CPU reference for the row kernels)."""
+    import numpy as np
+    rng = np.random.default_rng(1)
+    D, F = 3072, 12288
+    x = O.round_bf16(rng.standard_normal((rows, D)).astype(np.float32))
+    sh = O.round_bf16((rng.standard_normal((1, D)) * 0.1).astype(np.float32))
+    sc = O.round_bf16((rng.standard_normal((1, D)) * 0.1).astype(np.float32))
+    t0 = time.perf_counter()
+    O.rms_mod_quant_per_token(x, sh, sc, rows_per_mod=rows, eps=1e-6, kind=O.QUANT_INT8)
+    t_rms = time.perf_counter() - t0
+    g = O.round_bf16(rng.standard_normal((rows // 4, F)).astype(np.float32))
+    u = O.round_bf16(rng.standard_normal((rows // 4, F)).astype(np.float32))
+    t0 = time.perf_counter()
+    O.swiglu_quant_per_token(g, u, O.QUANT_INT8)
+    t_sw = time.perf_counter() - t0
+    return {"rms_mod_quant_int8_gbs": round((3 * rows * D + 4 * rows) / t_rms / 1e9, 3),
+            "swiglu_quant_int8_gbs": round((5 * (rows // 4) * F + 4 * (rows // 4)) / t_sw / 1e9, 3),
+            "cores": 1, "kind": "port", "sample": f"{rows} rows of 3072 (norm), {rows // 4} rows of 12288 (SwiGLU), numpy"}
+
+
 def cpu_gemm_sample(O, torch, min_seconds=10.0, max_seconds=30.0):
     """The reference CPU path on M-slices of the sweep: torch._int_mm + float32
     epilogue (oracle restatement of src/ck_int8_patch_intmm.py:63-71)."""
@@ -395,9 +514,11 @@ def run_reference(args):
             step_s.append(r)
     v = statistics.mean(r["value"] for r in step_s)
     line = {"impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": "TOPS", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ops_of(SHAPES) / (v * 1e12) * 1e3, 1), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "shapes_MNK": SHAPES, "sample": "M-slices of 2048 tokens"},
+            "config": {"workload": WORKLOAD, "shapes_MNK": SHAPES,
+                       "sample": "M-slices of 2048 tokens; ms_per_step = one full sweep step at the sampled rate"},
             "cpu_baseline": {"value": round(v, 4), "unit": "TOPS", "cores": torch.get_num_threads(), "kind": "port",
                              "sample": step_s[-1]["sample"]},
             "e2e": {"value": round(v, 4), "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -469,11 +590,31 @@ def run_ours(args):
         extras["fp8_gemm_sweep_tops"] = round(step_ops * max(3, args.steps // 2) / (f8_ms / 1e3) / 1e12, 1)
         del f8
         torch.cuda.empty_cache()
+        # the row kernels are issue-bound, so their rate follows the SM clock: a 2 s idle lets
+        # the clock recover from the GEMM sweeps' power draw (the same burst state the GEMMs
+        # are timed in)
+        time.sleep(2.0)
         rows = time_rows(torch, ops, dev, max(5, args.steps), args.warmup, stream)
         hbm = peaks["hbm_gbs"]
         for k, v in rows.items():
             v["frac_of_hbm"] = round(v["gbs"] / hbm, 3)
         extras["row_kernels"] = rows
+        from thor_int8_gemm_b200 import shard
+        mlp = time_mlp_chain(torch, ops, dev, max(3, args.steps // 4), args.warmup, stream, seed=7 + rank)
+        mlp["ms"] = round(shard.max_over_ranks(mlp["ms"], device=dev), 4)
+        mlp["tops"] = round(world * (2.0 * 32768 * 3072 * 24576 + 2.0 * 32768 * 12288 * 3072) / (mlp["ms"] / 1e3) / 1e12, 1)
+        extras["mlp_chain_int8"] = mlp
+        torch.cuda.empty_cache()
+        blk = time_dit_block(torch, dev, 2, 1, stream, seed=11 + rank)
+        for k in ("block_ms", "linears_and_norms_ms"):
+            blk[k] = round(shard.max_over_ranks(blk[k], device=dev), 3)
+        blk["linear_tops"] = round(world * 2.0 * 112640 * (3 * 3072 * 3072 + 3072 * 3072 + 2 * 12288 * 3072 + 3072 * 12288)
+                                   / (blk["linears_and_norms_ms"] / 1e3) / 1e12, 1)
+        extras["dit_block_int8"] = blk
+        torch.cuda.empty_cache()
+        if world == 1:
+            extras["reference_path_gpu"] = time_reference_path_gpu(torch, items, 3, stream)
+            torch.cuda.empty_cache()
         if world > 1:
             import torch.distributed as dist
             shard = items[0]["out"]
@@ -498,6 +639,8 @@ def run_ours(args):
         from oracle import oracle as O
         torch.set_num_threads(os.cpu_count() or 1)
         cpu = cpu_gemm_sample(O, torch)
+        if not args.no_extras:
+            extras["cpu_row_baselines"] = cpu_row_samples(O)
 
     traffic = read_traffic()
     if rank == 0:

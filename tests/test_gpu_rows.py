@@ -126,6 +126,42 @@ def test_rms_mod_quant_batch_major_rows(ops, kind, S, D, rows_per_mod):
     np.testing.assert_array_equal(qbits(q, kind), q_ref)
 
 
+def _tie_row(kind, D):
+    """A row of D values on the 8-bit format's rounding boundaries (half-integers for int8,
+    e4m3 midpoints) and one bf16 ulp either side, tiled, with amax = qmax so the scale is 1."""
+    if kind == "int8":
+        amax, centres = 127.0, np.arange(-127, 127, dtype=np.float64) + 0.5
+    else:
+        fin = O._E4M3_FINITE
+        mids = (fin[1:] + fin[:-1]) / 2
+        amax, centres = 448.0, np.concatenate([mids, -mids])
+    vals = O.round_bf16(centres.astype(np.float32))
+    row = np.concatenate([vals, O.bf16_to_f32(O.f32_to_bf16(vals) + 1), O.bf16_to_f32(O.f32_to_bf16(vals) - 1)])
+    row = row[np.abs(row) <= amax].astype(np.float32)
+    out = np.resize(row, D).astype(np.float32)
+    out[D // 2] = amax
+    return out
+
+
+@pytest.mark.parametrize("kind", ["int8", "fp8_e4m3"])
+@pytest.mark.parametrize("D", [1024, 3072, 2560])
+def test_rms_mod_quant_quantiser_ties(ops, kind, D):
+    """scale = -1 makes s = bf16(1 + scale) = 0, so h = shift exactly: rows of tie values
+    reach the norm kernels' quantiser (the deferred exact path of every vector slot of
+    the register-resident kernels; D = 2560 takes the shared-memory warp kernel)."""
+    S = 40
+    rng = np.random.default_rng(D)
+    x = O.round_bf16(rng.standard_normal((S, D)).astype(np.float32))
+    shift = _tie_row(kind, D)[None, :]
+    scale = -np.ones((1, D), np.float32)
+    q, qs = ops.rms_mod_quant(bf16_dev(to_bf16_bits(x)), bf16_dev(to_bf16_bits(shift)), bf16_dev(to_bf16_bits(scale)),
+                              rows_per_mod=S, eps=1e-6, kind=kind)
+    q_ref, qs_ref, _, _ = O.rms_mod_quant_per_token(x, shift, scale, rows_per_mod=S, eps=1e-6, kind=KINDS[kind])
+    assert np.all(qs_ref == 1.0)
+    np.testing.assert_array_equal(qs.cpu().numpy(), qs_ref)
+    np.testing.assert_array_equal(qbits(q, kind), q_ref)
+
+
 def test_rms_mod_quant_config3_full_size(ops):
     """x [2, 56320, 3072] bf16 ~ N(0,1), shift/scale [2, 3072] ~ N(0, 0.1), eps 1e-6,
     fp8 and int8: all rows bit-exact against the oracle (one pass, no h/res)."""

@@ -950,7 +950,6 @@ template <int NV, int QK>
 __global__ void __launch_bounds__(512, 1) rms_mod_simple_kernel(const RmsArgs a, const WarpRingGeom g) {
   extern __shared__ __align__(1024) uint8_t smem[];
   constexpr int NVEC = 32 * NV;
-  constexpr int D = 8 * NVEC;
   const int lane = threadIdx.x & 31;
   const int W = blockDim.x >> 5;
   // cache: s of elements 8c..8c+3 at cache_lo[c], 8c+4..8c+7 at cache_hi[c] (lane-contiguous
