@@ -399,8 +399,27 @@ def time_mlp_chain(torch, ops, dev, steps, warmup, stream, seed):
     ms = _event_ms(torch, stream, chain, steps, warmup)
     parts = {k: round(_event_ms(torch, stream, f, steps, 1), 4) for k, f in (("up_gemm", up), ("swiglu_quant", act),
                                                                               ("down_gemm", down))}
+    # the same chain with the SwiGLU in the up-GEMM's epilogue (fc1 rows interleaved once)
+    il = ops.interleave_gate_up
+    wu_il, wus_il, bu_il = il(wu), il(wus), il(bu)
+    a_buf = torch.empty(M, F, dtype=torch.bfloat16, device=dev)
+
+    def up_fused():
+        ops.gemm_swiglu(xq, wu_il, xs, wus_il, bu_il, out=a_buf, stream=stream)
+
+    def chain_fused():
+        up_fused()
+        a, s_ = ops.quant_rows(a_buf, "int8", stream=stream)
+        ops.gemm_dequant(a, wd, s_, wds, bd, out=out, stream=stream)
+
+    ms_fused = _event_ms(torch, stream, chain_fused, steps, warmup)
+    parts_fused = {"up_gemm_swiglu": round(_event_ms(torch, stream, up_fused, steps, 1), 4),
+                   "quant_act": round(_event_ms(torch, stream, lambda: ops.quant_rows(a_buf, "int8", stream=stream),
+                                                steps, 1), 4)}
     ops_chain = 2.0 * M * H * 2 * F + 2.0 * M * F * H
     return {"ms": round(ms, 4), "tops": round(ops_chain / (ms / 1e3) / 1e12, 1), "parts_ms": parts,
+            "fused_ms": round(ms_fused, 4), "fused_tops": round(ops_chain / (ms_fused / 1e3) / 1e12, 1),
+            "fused_parts_ms": parts_fused,
             "shape": "x [32768, 3072] -> [32768, 24576] -> act [32768, 12288] -> [32768, 3072]"}
 
 
@@ -601,8 +620,10 @@ def run_ours(args):
         extras["row_kernels"] = rows
         from thor_int8_gemm_b200 import shard
         mlp = time_mlp_chain(torch, ops, dev, max(3, args.steps // 4), args.warmup, stream, seed=7 + rank)
-        mlp["ms"] = round(shard.max_over_ranks(mlp["ms"], device=dev), 4)
-        mlp["tops"] = round(world * (2.0 * 32768 * 3072 * 24576 + 2.0 * 32768 * 12288 * 3072) / (mlp["ms"] / 1e3) / 1e12, 1)
+        chain_ops = 2.0 * 32768 * 3072 * 24576 + 2.0 * 32768 * 12288 * 3072
+        for k, t in (("ms", "tops"), ("fused_ms", "fused_tops")):
+            mlp[k] = round(shard.max_over_ranks(mlp[k], device=dev), 4)
+            mlp[t] = round(world * chain_ops / (mlp[k] / 1e3) / 1e12, 1)
         extras["mlp_chain_int8"] = mlp
         torch.cuda.empty_cache()
         blk = time_dit_block(torch, dev, 2, 1, stream, seed=11 + rank)

@@ -81,6 +81,30 @@ int t8g_gemm_fp8_dequant(const void* x, const void* w, const float* x_scale, con
                          void* stream);
 
 /*
+ * fc1 GEMM with the SwiGLU fused into its epilogue:
+ *   y[m, n]   = bf16( ((float(acc[m, n]) * x_scale[m]) * w_scale[n or 0]) + float(bias[n]) )
+ *   act[m, j] = bf16( silu(gate) * up )   with gate / up the bf16 y values of fc1 channels
+ *               j and F + j (the SwiGLU of t8g_swiglu_quant, bit for bit)
+ * The reference computes y with the GEMM, copies its halves and runs the SwiGLU kernel
+ * (src/ck_fused_patch.py:139-149, src/ck_fused_mod_norm_quant.py:59-73); here y never
+ * reaches memory.  w, w_scale and bias are the fc1 parameters with gate and up rows
+ * interleaved in blocks of 128: row 256 t + i holds gate channel 128 t + i and row
+ * 256 t + 128 + i up channel 128 t + i (i < 128).
+ *   x [M, K] int8 (ld_x), w [2F, K] int8 (ld_w), x_scale [M], w_scale numel 1 or 2F,
+ *   bias numel 0 or 2F (bf16), act [M, F] bf16 (ld_act).
+ * Requirements: F a multiple of 128; alignment and strides as t8g_gemm_i8_dequant.
+ * The per-token quantisation of act is t8g_quant_rows.
+ */
+int t8g_gemm_i8_swiglu(const void* x, const void* w, const float* x_scale, const float* w_scale,
+                       int64_t w_scale_numel, const void* bias, int64_t bias_numel, void* act, int64_t M, int64_t F,
+                       int64_t K, int64_t ld_x, int64_t ld_w, int64_t ld_act, void* stream);
+
+/* float8_e4m3fn twin of t8g_gemm_i8_swiglu. */
+int t8g_gemm_fp8_swiglu(const void* x, const void* w, const float* x_scale, const float* w_scale,
+                        int64_t w_scale_numel, const void* bias, int64_t bias_numel, void* act, int64_t M, int64_t F,
+                        int64_t K, int64_t ld_x, int64_t ld_w, int64_t ld_act, void* stream);
+
+/*
  * Per-token quantisation of a bf16 matrix: q_scale[m] = max(amax_k |x[m,k]| / qmax, 1e-12),
  * q[m, k] = cvt(clamp(x[m, k] / q_scale[m])).  This is the activation quantiser that
  * comfy-kitchen's int8_linear runs in front of _C.cutlass_int8_dequant (its code is not

@@ -97,3 +97,21 @@ def test_dit_block_fp8_runs_close_to_int8(mods):
     assert torch.isfinite(yf).all()
     rel = (yf - y8).norm() / y8.norm()
     assert rel < 0.05, float(rel)
+
+
+@pytest.mark.parametrize("kind", ["int8", "fp8_e4m3"])
+def test_dit_block_fused_mlp_matches(mods, kind):
+    """fc1 with the SwiGLU in its epilogue gives the unfused block's output bit for bit (int8)
+    and within one bf16 ulp through the block (fp8: fp32 accumulation order)."""
+    dit, ops = mods
+    B, T, hidden, heads, ffn = 2, 96, 256, 2, 512
+    g = torch.Generator(device="cuda").manual_seed(12)
+    x = torch.randn(B * T, hidden, generator=g, device="cuda").to(torch.bfloat16)
+    cond = (torch.randn(B, 6 * hidden, generator=g, device="cuda") * 0.1).to(torch.bfloat16)
+    plain = dit.DiTBlock(hidden, heads, ffn, kind=kind, device="cuda", seed=21)
+    fused = dit.DiTBlock(hidden, heads, ffn, kind=kind, device="cuda", seed=21, fused_mlp=True)
+    a, b = plain(x, cond, B), fused(x, cond, B)
+    if kind == "int8":
+        assert torch.equal(a, b)
+    else:
+        assert O.bf16_ulp_distance(bits16(a), bits16(b)).max() <= 2

@@ -260,3 +260,19 @@ def test_pth_boot_never_breaks_startup(tmp_path):
     r = subprocess.run([sys.executable, "-c", "import site, sys; site.addsitedir(sys.argv[1]); print('alive')",
                         str(site_dir)], capture_output=True, text=True, timeout=120)
     assert r.stdout.strip() == "alive"
+
+
+def test_interleave_gate_up_layout():
+    """Blocks of 128 gate rows then the matching 128 up rows; 1-D and 2-D parameters."""
+    import torch
+    from thor_int8_gemm_b200 import ops
+    F = 256
+    w = torch.arange(2 * F).view(2 * F, 1).repeat(1, 3)
+    il = ops.interleave_gate_up(w)
+    order = il[:, 0].tolist()
+    expect = list(range(0, 128)) + list(range(F, F + 128)) + list(range(128, 256)) + list(range(F + 128, F + 256))
+    assert order == expect
+    assert ops.interleave_gate_up(torch.arange(2 * F)).tolist() == expect
+    import pytest
+    with pytest.raises(ValueError):
+        ops.interleave_gate_up(torch.zeros(384))

@@ -23,13 +23,17 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
+#include "f32x2.cuh"
 #include "ptx.cuh"
 
 namespace t8g {
 namespace gemm {
 
 enum InKind : int { kInI8 = 0, kInE4M3 = 1 };
-enum OutKind : int { kOutBF16 = 0, kOutF16 = 1, kOutF32 = 2 };
+enum OutKind : int { kOutBF16 = 0, kOutF16 = 1, kOutF32 = 2, kOutSwiglu = 3 };
+// kOutSwiglu: the GEMM's bf16 output columns come in 128-column gate / up blocks (weights
+// interleaved so that every 256-column tile holds 128 gate columns and the matching 128 up
+// columns); the epilogue stores act = silu(gate) * up (bf16, half the columns) instead.
 
 constexpr int BM = 128;          // tile rows (tokens)
 constexpr int BN = 256;          // tile columns (output channels)
@@ -80,6 +84,8 @@ struct OutTraits<kOutBF16> {
     return *reinterpret_cast<uint32_t*>(&v);
   }
 };
+template <>
+struct OutTraits<kOutSwiglu> : OutTraits<kOutBF16> {};
 template <>
 struct OutTraits<kOutF16> {
   static constexpr int kBytes = 2;
@@ -467,6 +473,64 @@ __device__ __forceinline__ void epilogue_tile_staged(const Args& args, const CUt
   if (nchunks == 0) tmem_ld_wait_regs(r);
 }
 
+// SwiGLU epilogue of one 32-row slice: tile columns [0, 128) are gate and [128, 256) the
+// matching up columns.  Each value is dequantised and rounded to bf16 exactly as the plain
+// epilogue stores it, then act = silu(gate) * up with the row kernels' SiLU (f32x2.cuh),
+// rounded to bf16 and stored at act columns [n_tile0 / 2, n_tile0 / 2 + 128).
+template <int IN, int EPB>
+__device__ __forceinline__ void epilogue_tile_swiglu(const Args& args, const CUtensorMap* tm_out,
+                                                     uint8_t (*bufs)[EPB], int& ebuf, uint32_t t_row, int row0,
+                                                     int n_tile0, int lane, uint64_t pol_out, float xs_r,
+                                                     const TileParams& tp) {
+  const bool has_bias = args.bias != nullptr;
+#pragma unroll 1
+  for (int c = 0; c < BN / 2 / EPI_COLS; ++c) {
+    uint32_t rg[32], ru[32];
+    tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(c * EPI_COLS), rg);
+    tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(BN / 2 + c * EPI_COLS), ru);
+    tmem_ld_wait_regs(rg);
+    tmem_ld_wait_regs(ru);
+    uint32_t act[16];
+#pragma unroll
+    for (int p = 0; p < 16; ++p) {
+      float gv[2], uv[2];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int j = 2 * p + e;
+        const int cg = c * EPI_COLS + j, cu = BN / 2 + c * EPI_COLS + j;
+        float g = (IN == kInI8) ? __int2float_rn(static_cast<int>(rg[j])) : __uint_as_float(rg[j]);
+        float u = (IN == kInI8) ? __int2float_rn(static_cast<int>(ru[j])) : __uint_as_float(ru[j]);
+        g = __fmul_rn(__fmul_rn(g, xs_r), tp.ws[cg]);
+        u = __fmul_rn(__fmul_rn(u, xs_r), tp.ws[cu]);
+        if (has_bias) {
+          g = __fadd_rn(g, tp.bias[cg]);
+          u = __fadd_rn(u, tp.bias[cu]);
+        }
+        gv[e] = __bfloat162float(__float2bfloat16_rn(g));
+        uv[e] = __bfloat162float(__float2bfloat16_rn(u));
+      }
+      // g / 4 is exact for a bf16 g
+      act[p] = f2_to_bf2(silu_mul2(make_float2(gv[0] * 0.25f, gv[1] * 0.25f), make_float2(uv[0], uv[1])));
+    }
+    if (lane == 0) bulk_wait_group_read<1>();
+    __syncwarp();
+    uint8_t* buf = bufs[ebuf];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint4 w = make_uint4(act[4 * q + 0], act[4 * q + 1], act[4 * q + 2], act[4 * q + 3]);
+      const int pq = q ^ ((lane >> 1) & 3);
+      *reinterpret_cast<uint4*>(buf + lane * 64 + pq * 16) = w;
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_2d(tm_out, buf, n_tile0 / 2 + c * EPI_COLS, row0, pol_out);
+      bulk_commit_group();
+    }
+    ebuf ^= 1;
+  }
+}
+
 // ===========================================================================
 // 2-SM variant: a cluster of two CTAs (one per SM of a TPC) computes a 256x256
 // output tile with tcgen05.mma.cta_group::2 (M = 256, N = 256, K = 32).
@@ -684,10 +748,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       if (named_bar_any(1, 128, !ok)) break;
       tc_fence_after();
       if (row0 < args.M) {
-        epilogue_tile_staged<IN, OUT, Cfg::kEpiBytes>(args, &tm_out, s.epi[ew], ebuf,
-                                      tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
-                                          static_cast<uint32_t>(acc * BN),
-                                      row0, tn * BN, lane, pol_out, xs_r, s.params[acc]);
+        const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
+        if constexpr (OUT == kOutSwiglu)
+          epilogue_tile_swiglu<IN, Cfg::kEpiBytes>(args, &tm_out, s.epi[ew], ebuf, t_row, row0, tn * BN, lane, pol_out,
+                                                   xs_r, s.params[acc]);
+        else
+          epilogue_tile_staged<IN, OUT, Cfg::kEpiBytes>(args, &tm_out, s.epi[ew], ebuf, t_row, row0, tn * BN, lane,
+                                                        pol_out, xs_r, s.params[acc]);
       }
       tc_fence_before();
       __syncwarp();

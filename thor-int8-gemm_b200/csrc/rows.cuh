@@ -29,6 +29,7 @@
 
 #include <cuda_bf16.h>
 
+#include "f32x2.cuh"
 #include "ptx.cuh"
 
 namespace t8g {
@@ -54,10 +55,6 @@ struct QMax<kQuantFp8> {
 // ---------------------------------------------------------------- bf16 helpers
 __device__ __forceinline__ float bf_lo(uint32_t u) { return __uint_as_float(u << 16); }
 __device__ __forceinline__ float bf_hi(uint32_t u) { return __uint_as_float(u & 0xFFFF0000u); }
-__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
-  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
-  return *reinterpret_cast<uint32_t*>(&v);
-}
 __device__ __forceinline__ void unpack8(const uint4& v, float (&f)[8]) {
   f[0] = bf_lo(v.x); f[1] = bf_hi(v.x); f[2] = bf_lo(v.y); f[3] = bf_hi(v.y);
   f[4] = bf_lo(v.z); f[5] = bf_hi(v.z); f[6] = bf_lo(v.w); f[7] = bf_hi(v.w);
@@ -89,20 +86,6 @@ __device__ __forceinline__ uint32_t cvt_e4m3x2(float lo, float hi) {
   asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
   return r;
 }
-// Packed fp32 arithmetic (two lanes per instruction), each lane rounded to nearest even.
-// A packed multiply that feeds a packed add may be fused into one multiply-add
-// (observed: h = t * s + b came out as fma(t, s, b) in a rare cancelling case), so an
-// add whose operand is a product that must round separately uses the scalar IEEE add
-// (__fadd_rn, never contracted).  Where fusion cannot change the result (the
-// quantiser's bracket, see quant8) the packed forms are used as they are.
-__device__ __forceinline__ float2 mul2_rn(float2 a, float2 b) { return __fmul2_rn(a, b); }
-__device__ __forceinline__ float2 add2_rn(float2 a, float2 b) { return __fadd2_rn(a, b); }
-__device__ __forceinline__ float2 fma2_rn(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
-
-__device__ __forceinline__ float2 bf2_to_f2(uint32_t u) {
-  return make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xFFFF0000u));
-}
-__device__ __forceinline__ uint32_t f2_to_bf2(float2 v) { return pack_bf16(v.x, v.y); }
 
 // Round-half-even to an integer through the fp32 adder: for |v| < 2^22 the low byte
 // of bits(v + 1.5 * 2^23) is rint(v) as a two's-complement int8.
@@ -1105,30 +1088,6 @@ __global__ void __launch_bounds__(512, 1) rms_mod_warp_reg_kernel(const RmsArgs 
 }
 
 // ---------------------------------------------------------------- SwiGLU
-// act = (g * sigmoid(g)) * u with sigmoid(g) = 1 / (1 + e^-g), in fp32 with the fast
-// hardware exponential and reciprocal (act is compared with the oracle within one bf16
-// ulp):
-//   e   = 2^(-g * log2(e))              ex2.approx.ftz (the change-of-base identity)
-//   d4  = (1 + e) / 4                   one fma: RN(1 + e) scaled exactly by 1/4
-//   r4  = approx(1 / d4) = 4 / (1 + e)  rcp.approx.ftz
-//   act = ((g / 4) * r4) * u            g / 4 is exact for every bf16 g
-// The quarter scaling keeps the reciprocal normal where 1 / (1 + e) itself would be
-// subnormal (g < -87.3: 2^-126 < 4 / (1 + e)), so flushing subnormal reciprocals cannot
-// change act; (g / 4) * r4 is the same real product as g * (1 / (1 + e)).  For e = inf
-// (g < -88.7) r4 = 0 and act is a signed zero, as in fp32 with an IEEE reciprocal.
-__device__ __forceinline__ float ex2_approx(float x) {
-  float r;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
-  return r;
-}
-__device__ __forceinline__ float rcp_approx_ftz(float x) {
-  float r;
-  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
-  return r;
-}
-
-constexpr float kLog2E = 1.44269504088896340736f;
-
 // (lo(g) / 4, hi(g) / 4) straight from a packed bf16 pair: one mixed-precision fma per
 // value, g * 0.25 + (-0), exact (the sign of a zero product is kept).
 __device__ __forceinline__ float2 quarter_bf16x2(uint32_t g) {
@@ -1138,15 +1097,6 @@ __device__ __forceinline__ float2 quarter_bf16x2(uint32_t g) {
       : "=f"(x), "=f"(y)
       : "r"(g));
   return make_float2(x, y);
-}
-
-// g4 = g / 4 (exact), u: one packed pair of gate / up values.
-__device__ __forceinline__ float2 silu_mul2(float2 g4, float2 u) {
-  const float2 t = mul2_rn(g4, make_float2(-4.0f * kLog2E, -4.0f * kLog2E));   // = -g * log2(e), same rounding
-  const float2 e = make_float2(ex2_approx(t.x), ex2_approx(t.y));
-  const float2 d4 = fma2_rn(e, make_float2(0.25f, 0.25f), make_float2(0.25f, 0.25f));
-  const float2 r4 = make_float2(rcp_approx_ftz(d4.x), rcp_approx_ftz(d4.y));
-  return mul2_rn(mul2_rn(g4, r4), u);
 }
 
 // act for one vector from the gate and up rows in the slot; returns bf16(act).

@@ -234,6 +234,57 @@ int gemm_entry(int in_kind, const void* x, const void* w, const float* x_scale, 
   }
 }
 
+// GEMM with the SwiGLU epilogue: w holds the fc1 weight with gate and up rows interleaved in
+// 128-row blocks (2F rows), act receives silu(gate) * up as bf16 [M, F].  Always the 2-SM
+// kernel (its 256-column tiles pair 128 gate with 128 up columns).
+int gemm_swiglu_entry(int in_kind, const void* x, const void* w, const float* x_scale, const float* w_scale,
+                      int64_t w_scale_numel, const void* bias, int64_t bias_numel, void* act, int64_t M, int64_t F,
+                      int64_t K, int64_t ld_x, int64_t ld_w, int64_t ld_act, void* stream_) {
+  using namespace t8g::gemm;
+  g_last_error[0] = '\0';
+  if (M < 0 || F < 0 || K < 1) return fail(T8G_ERR_INVALID_ARGUMENT, "bad sizes M=%lld F=%lld K=%lld", (long long)M, (long long)F, (long long)K);
+  if (F % 128) return fail(T8G_ERR_INVALID_ARGUMENT, "F=%lld must be a multiple of 128", (long long)F);
+  const int64_t N = 2 * F;
+  if (M >= (int64_t(1) << 31) || N >= (int64_t(1) << 31) || K >= (int64_t(1) << 31))
+    return fail(T8G_ERR_UNSUPPORTED, "M, 2F and K must each be below 2^31");
+  if (M == 0 || F == 0) return T8G_OK;
+  if (!x || !w || !x_scale || !w_scale || !act) return fail(T8G_ERR_INVALID_ARGUMENT, "null operand pointer");
+  if (w_scale_numel != 1 && w_scale_numel != N)
+    return fail(T8G_ERR_INVALID_ARGUMENT, "w_scale numel %lld is neither 1 nor 2F=%lld", (long long)w_scale_numel, (long long)N);
+  if (bias_numel != 0 && bias_numel != N)
+    return fail(T8G_ERR_INVALID_ARGUMENT, "bias numel %lld is neither 0 nor 2F=%lld", (long long)bias_numel, (long long)N);
+  if (bias_numel == N && !bias) return fail(T8G_ERR_INVALID_ARGUMENT, "bias numel is 2F but bias is null");
+  if (ld_x < K || ld_w < K || ld_act < F) return fail(T8G_ERR_INVALID_ARGUMENT, "row stride smaller than the row");
+  if (ld_x % 16 || ld_w % 16 || (ld_act * 2) % 16)
+    return fail(T8G_ERR_INVALID_ARGUMENT, "row strides must be multiples of 16 bytes");
+  if (!aligned(x, 16) || !aligned(w, 16) || !aligned(act, 16))
+    return fail(T8G_ERR_INVALID_ARGUMENT, "x, w and act must be 16-byte aligned");
+  if (!aligned(x_scale, 4) || !aligned(w_scale, 4)) return fail(T8G_ERR_INVALID_ARGUMENT, "scales must be 4-byte aligned");
+  int dev;
+  DeviceInfo info;
+  int rc = current_device(&dev, &info);
+  if (rc) return rc;
+  CUtensorMap ta, tb, to;
+  rc = encode_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, x, K, M, ld_x, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  rc = encode_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, K, N, ld_w, BK, P_ROWS, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  rc = encode_2d(&to, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, act, F, M, ld_act * 2, EPI_COLS, 32, CU_TENSOR_MAP_SWIZZLE_64B);
+  if (rc) return rc;
+  Args args;
+  args.xs = x_scale;
+  args.ws = w_scale;
+  args.bias = bias_numel ? bias : nullptr;
+  args.ws_stride = w_scale_numel == 1 ? 0 : 1;
+  args.vec_ok = aligned(w_scale, 16) && (bias_numel == 0 || aligned(bias, 16));
+  args.M = static_cast<int>(M);
+  args.N = static_cast<int>(N);
+  args.K = static_cast<int>(K);
+  cudaStream_t st = static_cast<cudaStream_t>(stream_);
+  if (in_kind == kInI8) return launch_gemm_pair<kInI8, kOutSwiglu>(ta, tb, to, args, dev, info.sms, st);
+  return launch_gemm_pair<kInE4M3, kOutSwiglu>(ta, tb, to, args, dev, info.sms, st);
+}
+
 // ----------------------------------------------------------------- row kernels
 // Row-group shape: V = max(3, ceil(nvec / 512)) 16-byte vectors per thread and
 // T = 32 * ceil(nvec / (32 V)) threads (nvec = D / 8); kernels are unrolled for V = 3
@@ -676,6 +727,20 @@ int t8g_gemm_fp8_dequant(const void* x, const void* w, const float* x_scale, con
                          int64_t M, int64_t N, int64_t K, int64_t ld_x, int64_t ld_w, int64_t ld_out, void* stream) {
   return gemm_entry(t8g::gemm::kInE4M3, x, w, x_scale, w_scale, w_scale_numel, bias, bias_numel, out, out_dtype, M,
                     N, K, ld_x, ld_w, ld_out, stream);
+}
+
+int t8g_gemm_i8_swiglu(const void* x, const void* w, const float* x_scale, const float* w_scale,
+                       int64_t w_scale_numel, const void* bias, int64_t bias_numel, void* act, int64_t M, int64_t F,
+                       int64_t K, int64_t ld_x, int64_t ld_w, int64_t ld_act, void* stream) {
+  return gemm_swiglu_entry(t8g::gemm::kInI8, x, w, x_scale, w_scale, w_scale_numel, bias, bias_numel, act, M, F, K,
+                           ld_x, ld_w, ld_act, stream);
+}
+
+int t8g_gemm_fp8_swiglu(const void* x, const void* w, const float* x_scale, const float* w_scale,
+                        int64_t w_scale_numel, const void* bias, int64_t bias_numel, void* act, int64_t M, int64_t F,
+                        int64_t K, int64_t ld_x, int64_t ld_w, int64_t ld_act, void* stream) {
+  return gemm_swiglu_entry(t8g::gemm::kInE4M3, x, w, x_scale, w_scale, w_scale_numel, bias, bias_numel, act, M, F,
+                           K, ld_x, ld_w, ld_act, stream);
 }
 
 int t8g_quant_rows(const void* x, int64_t ld_x, void* q, int64_t ld_q, float* q_scale, int64_t S, int64_t D,

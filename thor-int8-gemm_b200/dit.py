@@ -43,7 +43,7 @@ class DiTBlock:
     """Synthetic DiT block (see module docstring)."""
 
     def __init__(self, hidden: int = 3072, heads: int = 24, ffn: int = 12288, kind: str = "int8",
-                 device=None, seed: int = 0, eps: float = 1e-6):
+                 device=None, seed: int = 0, eps: float = 1e-6, fused_mlp: bool = False):
         if hidden % heads:
             raise ValueError("hidden must be a multiple of heads")
         self.hidden, self.heads, self.ffn, self.kind, self.eps = hidden, heads, ffn, kind, eps
@@ -61,6 +61,11 @@ class DiTBlock:
         self.proj = QuantLinear(w(hidden, hidden), b(hidden), kind)
         self.fc1 = QuantLinear(w(2 * ffn, hidden), b(2 * ffn), kind)
         self.fc2 = QuantLinear(w(hidden, ffn), b(hidden), kind)
+        # fused_mlp: fc1 with the SwiGLU in its epilogue (gate / up rows interleaved once)
+        self.fused_mlp = fused_mlp
+        if fused_mlp:
+            il = ops.interleave_gate_up
+            self.fc1_il = (il(self.fc1.w), il(self.fc1.ws), il(self.fc1.bias))
 
     def modulation(self, cond: torch.Tensor):
         """Split the conditioning [B, 6*hidden] into shift/scale/gate for attention and MLP."""
@@ -93,8 +98,12 @@ class DiTBlock:
         aq, as_ = ops.quant_rows(attn.contiguous(), self.kind)
         x = self.gated(x, gate_msa, self.proj(aq, as_), batch)
         q2, s2 = self.norm_quant(x, shift_mlp, scale_mlp, T)
-        y = self.fc1(q2, s2)
-        q3, s3 = ops.swiglu_quant_fc1(y, kind=self.kind)
+        if self.fused_mlp:
+            w_il, ws_il, b_il = self.fc1_il
+            q3, s3 = ops.quant_rows(ops.gemm_swiglu(q2, w_il, s2, ws_il, b_il), self.kind)
+        else:
+            y = self.fc1(q2, s2)
+            q3, s3 = ops.swiglu_quant_fc1(y, kind=self.kind)
         return self.gated(x, gate_mlp, self.fc2(q3, s3), batch)
 
     def __call__(self, x: torch.Tensor, cond: torch.Tensor, batch: int) -> torch.Tensor:

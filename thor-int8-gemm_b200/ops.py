@@ -85,6 +85,64 @@ def gemm_dequant(x: torch.Tensor, w: torch.Tensor, x_scale: torch.Tensor, w_scal
     return out
 
 
+SWIGLU_BLOCK = 128
+
+
+def interleave_gate_up(t: torch.Tensor, block: int = SWIGLU_BLOCK) -> torch.Tensor:
+    """Reorder an fc1 parameter whose first half (along dim 0) is gate and second half up
+    into the layout of gemm_swiglu: blocks of `block` gate rows followed by the matching
+    `block` up rows.  Works for the weight [2F, K], its per-channel scales [2F] and the
+    bias [2F]; done once when the weights are loaded."""
+    n = t.shape[0]
+    if n % (2 * block):
+        raise ValueError(f"dim 0 ({n}) must be a multiple of {2 * block}")
+    F = n // 2
+    g = t[:F].reshape(F // block, block, *t.shape[1:])
+    u = t[F:].reshape(F // block, block, *t.shape[1:])
+    return torch.stack([g, u], dim=1).reshape(t.shape).contiguous()
+
+
+def gemm_swiglu(x: torch.Tensor, w_il: torch.Tensor, x_scale: torch.Tensor, w_scale_il: torch.Tensor,
+                bias_il: torch.Tensor | None = None, out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    """act = bf16(silu(gate) * up) of the fc1 GEMM, fused: gate / up are the bf16 outputs
+    the plain gemm_dequant would produce for fc1 channels j and F + j.  w_il, w_scale_il
+    (numel 2F, or 1) and bias_il (bf16, 2F) come from interleave_gate_up; x int8 [M, K] or
+    float8_e4m3fn; out [M, F] bf16."""
+    _need_cuda("x", x, (torch.int8, torch.float8_e4m3fn), 2)
+    _need_cuda("w", w_il, x.dtype, 2)
+    M, K = x.shape
+    N = w_il.shape[0]
+    if w_il.shape[1] != K:
+        raise ValueError(f"w has K={w_il.shape[1]}, x has K={K}")
+    if N % (2 * SWIGLU_BLOCK):
+        raise ValueError(f"w must have 2F rows with F a multiple of {SWIGLU_BLOCK}")
+    F = N // 2
+    _need_cuda("x_scale", x_scale, torch.float32)
+    _need_cuda("w_scale", w_scale_il, torch.float32)
+    if x_scale.numel() != M or not x_scale.is_contiguous():
+        raise ValueError("x_scale must be a contiguous float32 tensor with M elements")
+    if w_scale_il.numel() not in (1, N) or not w_scale_il.is_contiguous():
+        raise ValueError("w_scale must be a contiguous float32 tensor with 1 or 2F elements")
+    if out is None:
+        out = torch.empty(M, F, dtype=torch.bfloat16, device=x.device)
+    _need_cuda("out", out, torch.bfloat16, 2)
+    if tuple(out.shape) != (M, F):
+        raise ValueError(f"out has shape {tuple(out.shape)}, expected {(M, F)}")
+    nb = 0 if bias_il is None else bias_il.numel()
+    if nb:
+        _need_cuda("bias", bias_il, torch.bfloat16)
+        if nb != N or not bias_il.is_contiguous():
+            raise ValueError("bias must be contiguous bf16 with 2F elements")
+    lib = _lib.load()
+    fn = lib.t8g_gemm_i8_swiglu if x.dtype == torch.int8 else lib.t8g_gemm_fp8_swiglu
+    with torch.cuda.device(x.device):
+        rc = fn(_ptr(x), _ptr(w_il), _ptr(x_scale), _ptr(w_scale_il), w_scale_il.numel(),
+                _ptr(bias_il) if nb else None, nb, _ptr(out), M, F, K, x.stride(0), w_il.stride(0), out.stride(0),
+                _stream_handle(x.device, stream))
+    _lib.check(rc)
+    return out
+
+
 def quant_rows(x: torch.Tensor, kind: str = "int8", q: torch.Tensor | None = None,
                q_scale: torch.Tensor | None = None, stream=None):
     """Per-token quantisation of a bf16 [S, D] matrix -> (q [S, D], q_scale [S] float32)."""
