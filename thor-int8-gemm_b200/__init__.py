@@ -14,12 +14,13 @@ Submodules (imported lazily, so the import-proxy agent stays light at start-up):
   shard       token sharding across ranks (one process per GPU)
   dit         a DiT block whose linears and norm/quant ops run on these kernels
   torch_ops   the entry points as torch custom ops (namespace t8g) for torch.compile
+  fused_patch the DiT-block agent (comfy's MiniMax-H3 DiTBlock.forward on the fused kernels)
 """
 import importlib
 
 __version__ = "0.1.0"
 PACKAGE_NAME = "thor_int8_gemm_b200"
-_LAZY = ("ops", "fused", "patch_int8", "build", "_lib", "shard", "dit", "torch_ops")
+_LAZY = ("ops", "fused", "patch_int8", "build", "_lib", "shard", "dit", "torch_ops", "fused_patch")
 
 
 def __getattr__(name):

@@ -1,6 +1,8 @@
 """Run by the one-line .pth file that `patch_int8.write_pth` installs: registers this
-directory as the package `thor_int8_gemm_b200` and installs the comfy-kitchen agent.
-Never raises (a performance patch must not break interpreter start-up)."""
+directory as the package `thor_int8_gemm_b200` and installs the two agents -- the
+comfy-kitchen `_C` proxy (patch_int8) and the DiT-block agent (fused_patch), each inert
+unless its own mode enables it.  Never raises (a performance patch must not break
+interpreter start-up)."""
 import importlib.util
 import os
 import sys
@@ -26,3 +28,8 @@ try:
     _patch.install_safely()
 except Exception as _exc:  # never break interpreter start-up
     print(f"[ck-int8-patch] disabled: {_exc!r}", file=sys.stderr)
+try:
+    from thor_int8_gemm_b200 import fused_patch as _fused
+    _fused.install_safely()
+except Exception as _exc:
+    print(f"[ck-fused-patch] disabled: {_exc!r}", file=sys.stderr)
