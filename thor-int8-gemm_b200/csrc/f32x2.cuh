@@ -16,8 +16,8 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
 // A packed multiply that feeds a packed add may be fused into one multiply-add
 // (observed: h = t * s + b came out as fma(t, s, b) in a rare cancelling case), so an
 // add whose operand is a product that must round separately uses the scalar IEEE add
-// (__fadd_rn, never contracted).  Where fusion cannot change the result (the
-// quantiser's bracket, see quant8) the packed forms are used as they are.
+// (__fadd_rn, never contracted) or the mixed-precision add.rn.f32.bf16.  Products that
+// feed only fmas (the quantiser's quotient correction) are unaffected.
 __device__ __forceinline__ float2 mul2_rn(float2 a, float2 b) { return __fmul2_rn(a, b); }
 __device__ __forceinline__ float2 add2_rn(float2 a, float2 b) { return __fadd2_rn(a, b); }
 __device__ __forceinline__ float2 fma2_rn(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }

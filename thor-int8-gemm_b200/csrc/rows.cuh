@@ -21,10 +21,10 @@
 //   inv = 1 / sqrt(ss / D + eps) with IEEE divide and square root;
 //   h = (((x * inv) * w) * s) + b, every product and sum rounded separately;
 //   per-token scale = max(amax / qmax, 1e-12) (IEEE divide);
-//   q = cvt(RN(v / scale)) (see quant8: a reciprocal multiply with an exact
-//   fallback near rounding boundaries), round-half-even (int8, which never
-//   needs the +-127 clamp: |v / scale| <= 127 * (1 + 2^-23)) or the saturating
-//   RNE e4m3 conversion (fp8).
+//   q = cvt(RN(v / scale)) (see quant8: the correctly rounded quotient from a
+//   reciprocal multiply and one fma correction), round-half-even (int8, which never
+//   needs the +-127 clamp: |v / scale| <= 127) or the saturating RNE e4m3
+//   conversion (fp8).
 #pragma once
 
 #include <cuda_bf16.h>
@@ -94,8 +94,9 @@ constexpr float kRoundMagic = 12582912.0f;
 // Per-row constants of the quantiser.
 struct QuantRow {
   float scale;    // max(amax / qmax, 1e-12)
-  float2 c_lo;    // RN(RN(1 / scale) * (1 - 2^-21)), both lanes
-  float2 c_hi;    // RN(RN(1 / scale) * (1 + 2^-21)), both lanes
+  float2 rcp;     // RN(1 / scale) (IEEE divide), both lanes
+  float2 scale2;  // scale, both lanes
+  float2 nrcp;    // -RN(1 / scale), both lanes
 };
 
 template <int QK>
@@ -103,60 +104,41 @@ __device__ __forceinline__ QuantRow quant_row(float amax) {
   QuantRow r;
   r.scale = fmaxf(__fdiv_rn(amax, QMax<QK>::v), kScaleMin);
   const float rcp = __fdiv_rn(1.0f, r.scale);
-  const float lo = __fmul_rn(rcp, 1.0f - 0x1p-21f), hi = __fmul_rn(rcp, 1.0f + 0x1p-21f);
-  r.c_lo = make_float2(lo, lo);
-  r.c_hi = make_float2(hi, hi);
+  r.rcp = make_float2(rcp, rcp);
+  r.scale2 = make_float2(r.scale, r.scale);
+  r.nrcp = make_float2(-rcp, -rcp);
   return r;
 }
 
 // 8 values (4 pairs) -> 8 quantised bytes, bit-identical to cvt(RN(v / scale)) with an
-// IEEE divide.  Writing x = v / scale, a = RN(v * c_lo) and b = RN(v * c_hi) bracket
-// x within a relative 2^-21 - 2^-23 > 2^-23 of it on either side, so RN(x) lies
-// between a and b.  The 8-bit conversion (int8: round half to even; e4m3: RNE with
-// saturation) is monotone, so when a and b convert to the same code that code is
-// the one RN(x) converts to.  (If the int8 path's multiply and magic-number add are
-// fused, the integers are those of the exact products, which bracket x too.)  Otherwise (a rounding boundary lies within ~2^-21 of
-// x, probability ~2^-17 per value) the lane recomputes its eight values with the
-// IEEE divide.  int8 never needs the +-127 clamp: |x| <= 127 * (1 + 2^-23).
-// The exact path of quant8: cvt(RN(v / scale)) with the IEEE divide, out of line so that
-// the unrolled row loops carry one call instead of eight inlined divides per vector.
-template <int QK>
-__device__ __noinline__ uint2 quant8_divide(float2 v0, float2 v1, float2 v2, float2 v3, float scale) {
-  const float2 v[4] = {v0, v1, v2, v3};
-  uint32_t ca[4];
-#pragma unroll
-  for (int p = 0; p < 4; ++p) {
-    const float qx = __fdiv_rn(v[p].x, scale), qy = __fdiv_rn(v[p].y, scale);
-    if constexpr (QK == kQuantInt8)
-      ca[p] = __byte_perm(__float_as_uint(__fadd_rn(qx, kRoundMagic)), __float_as_uint(__fadd_rn(qy, kRoundMagic)),
-                          0x0040);
-    else
-      ca[p] = cvt_e4m3x2(qx, qy);
-  }
-  return make_uint2(__byte_perm(ca[0], ca[1], 0x5410), __byte_perm(ca[2], ca[3], 0x5410));
-}
-
+// IEEE divide, without a divide and without a branch: the quotient is corrected with
+// Markstein's step (P. Markstein, "Computation of elementary functions on the IBM RISC
+// System/6000 processor", IBM J. Res. Dev. 34(1), 1990): with y = RN(1/s) correctly
+// rounded and q = RN(v y) within one ulp of v/s, the remainder r = v - s q is exact in
+// fp32 (one fma) and q' = RN(q + r y) (one fma) is the correctly rounded v/s.  The
+// remainder can be inexact only when it underflows, which needs |v/s| < 2^-12: there
+// q' and RN(v/s) both convert to a zero code (int8: |x| < 0.5; e4m3: |x| < 2^-10).
+// The remainder is formed negated, n = RN(q s - v), and q' = RN(n (-y) + q), so that an
+// exact zero keeps the sign of v (v = -0 gives q' = -0 + -0 = -0, the IEEE quotient; with
+// r = RN(v - s q) it would be +0, and e4m3 has a negative zero code).  The 8-bit
+// conversion is then the IEEE one (int8: round half to even through the fp32 adder,
+// never needing the +-127 clamp since |v/s| <= 127; e4m3: RNE with saturation).
 template <int QK>
 __device__ __forceinline__ uint2 quant8(const float2 (&v)[4], const QuantRow& qr) {
-  uint32_t ca[4], cb[4];
+  uint32_t c[4];
 #pragma unroll
   for (int p = 0; p < 4; ++p) {
-    const float2 a = mul2_rn(v[p], qr.c_lo);
-    const float2 b = mul2_rn(v[p], qr.c_hi);
+    const float2 q = mul2_rn(v[p], qr.rcp);
+    const float2 n = fma2_rn(q, qr.scale2, make_float2(-v[p].x, -v[p].y));
+    const float2 qq = fma2_rn(n, qr.nrcp, q);
     if constexpr (QK == kQuantInt8) {
-      const float2 m = make_float2(kRoundMagic, kRoundMagic);
-      const float2 ra = add2_rn(a, m), rb = add2_rn(b, m);
-      ca[p] = __byte_perm(__float_as_uint(ra.x), __float_as_uint(ra.y), 0x0040);
-      cb[p] = __byte_perm(__float_as_uint(rb.x), __float_as_uint(rb.y), 0x0040);
+      const float2 rq = add2_rn(qq, make_float2(kRoundMagic, kRoundMagic));
+      c[p] = __byte_perm(__float_as_uint(rq.x), __float_as_uint(rq.y), 0x0040);
     } else {
-      ca[p] = cvt_e4m3x2(a.x, a.y);
-      cb[p] = cvt_e4m3x2(b.x, b.y);
+      c[p] = cvt_e4m3x2(qq.x, qq.y);
     }
   }
-  const uint32_t w0 = __byte_perm(ca[0], ca[1], 0x5410), w1 = __byte_perm(ca[2], ca[3], 0x5410);
-  const uint32_t u0 = __byte_perm(cb[0], cb[1], 0x5410), u1 = __byte_perm(cb[2], cb[3], 0x5410);
-  if (__builtin_expect((w0 != u0) | (w1 != u1), 0)) return quant8_divide<QK>(v[0], v[1], v[2], v[3], qr.scale);
-  return make_uint2(w0, w1);
+  return make_uint2(__byte_perm(c[0], c[1], 0x5410), __byte_perm(c[2], c[3], 0x5410));
 }
 
 __device__ __forceinline__ void unpack_pairs(const uint4& u, float2 (&v)[4]) {
@@ -412,7 +394,7 @@ __global__ void __launch_bounds__(512) quant_rows_kernel(const QuantRowsArgs a, 
 // per warp: every warp has its own ring of `stages` slots (bulk copies issued by its
 // lane 0, one mbarrier per slot), folds the row max with shuffles and never waits for
 // the other warps of its CTA, so a row costs no CTA barrier and its per-row work
-// (reduction, scale, reciprocal bracket) is shared by 32 threads rather than a row group.
+// (reduction, scale, reciprocal) is shared by 32 threads rather than a row group.
 constexpr uint32_t kWarpRowMaxBytes = 16 * 1024;
 constexpr int kWarpMaxWarps = 32;
 constexpr int kWarpMaxStages = 8;
