@@ -9,14 +9,18 @@ tokens -- six launches of the tcgen05 GEMM per step.  `value` is whole-job
 TOPS (2*M*N*K summed over the six shapes, all ranks) with inputs resident in
 HBM; `e2e` is the same metric through the public API with host (pinned)
 activations copied in and every output copied back inside the timed region.
-Secondary figures timed in the same run (not part of `value`): the fp8 e4m3
-GEMM sweep, fused RMSNorm + adaLN modulation + per-token quant on
-[2, 56320, 3072] (fp8 and int8), fused SwiGLU + per-token int8 quant on the
-[32768, 24576] fc1 output, and, with N > 1, an NCCL all-gather of one output.
+Secondary figures timed in the same run (not part of `value`, under `extras`):
+the single 256x3072x3072 GEMM, the fp8 e4m3 GEMM sweep, fused RMSNorm + adaLN
+modulation + per-token quant on [2, 56320, 3072] (fp8 and int8), fused SwiGLU +
+per-token int8 quant on the [32768, 24576] fc1 output, the SwiGLU MLP chain
+(32768 tokens, 3072 -> 2 x 12288 -> 3072) plain and with the SwiGLU in the fc1
+epilogue, a DiT block over 112640 tokens, the reference's `_int_mm` + eager
+epilogue path on the same GPU, and, with N > 1, an NCCL all-gather of one output.
 
-Under torchrun (N > 1) each rank runs the same per-rank workload on its own
-GPU (token-sharded DiT: weights replicated, no collective on the data path):
-weak scaling, timed as the max over ranks.
+Under torchrun (N > 1) the sweep is token-sharded (weights replicated, no
+collective on the data path), timed as the max over ranks: `--scaling weak`
+(default) gives every rank the full sweep on its own tokens, `--scaling strong`
+splits each shape's tokens across the ranks.
 
 `--impl reference` times the reference's CPU path (torch `_int_mm` + float32
 eager epilogue, src/ck_int8_patch_intmm.py:63-71, restated by oracle/) on the
@@ -59,6 +63,9 @@ def parse_args():
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true")
+    ap.add_argument("--scaling", choices=("weak", "strong"), default="weak",
+                    help="weak: every rank runs the full sweep on its own tokens; strong: the sweep's "
+                         "tokens are split across the ranks")
     ap.add_argument("--profile", choices=("gemm_i8", "gemm_fp8", "rms_fp8", "rms_int8", "swiglu_int8", "quant_int8"),
                     help="run one kernel a few times on a mid-size case (for ncu captures) and exit")
     ap.add_argument("--M", type=int, default=32768)
@@ -212,7 +219,9 @@ def make_weight(torch, ops, N, K, gen, dev, kind):
     return q, s
 
 
-def build_gemm_set(torch, ops, dev, kind, seed):
+def build_gemm_set(torch, ops, dev, kind, seed, m_of=None):
+    """The sweep's operands; `m_of(M)` gives this rank's token count for a shape's M
+    (strong scaling), default M itself."""
     gen = torch.Generator(device=dev)
     gen.manual_seed(seed)
     outliers = torch.randperm(K_DIM, generator=gen, device=dev)[: K_DIM // 100]
@@ -221,10 +230,12 @@ def build_gemm_set(torch, ops, dev, kind, seed):
         wq, ws = make_weight(torch, ops, N, K_DIM, gen, dev, kind)
         bias = (torch.randn(N, generator=gen, device=dev) * 0.01).to(torch.bfloat16)
         weights[N] = (wq, ws, bias)
-    acts = {M: make_activation(torch, ops, M, K_DIM, gen, dev, outliers, kind) for M in M_SWEEP}
+    m_of = m_of or (lambda M: M)
+    acts = {M: make_activation(torch, ops, m_of(M), K_DIM, gen, dev, outliers, kind) for M in M_SWEEP}
     items = []
     for M, N, K in SHAPES:
         xq, xs = acts[M]
+        M = m_of(M)
         wq, ws, bias = weights[N]
         out = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
         items.append({"M": M, "N": N, "K": K, "x": xq, "xs": xs, "w": wq, "ws": ws, "bias": bias, "out": out})
@@ -535,7 +546,7 @@ def run_reference(args):
     line = {"impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": "TOPS", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(ops_of(SHAPES) / (v * 1e12) * 1e3, 1), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "scaling": args.scaling, "vs_baseline": None, "dtype": "int8", "data": "synthetic",
             "config": {"workload": WORKLOAD, "shapes_MNK": SHAPES,
                        "sample": "M-slices of 2048 tokens; ms_per_step = one full sweep step at the sampled rate"},
             "cpu_baseline": {"value": round(v, 4), "unit": "TOPS", "cores": torch.get_num_threads(), "kind": "port",
@@ -559,8 +570,15 @@ def run_ours(args):
     load_package()
     from thor_int8_gemm_b200 import ops
 
+    from thor_int8_gemm_b200 import shard
     stream = torch.cuda.Stream(dev)
-    items = build_gemm_set(torch, ops, dev, "int8", seed=1234 + rank)
+    strong = args.scaling == "strong"
+
+    def m_of(M):
+        a, b = shard.token_range(M, rank, world)
+        return b - a
+
+    items = build_gemm_set(torch, ops, dev, "int8", seed=1234 + rank, m_of=m_of if strong else None)
     torch.cuda.synchronize(dev)
 
     def barrier():
@@ -582,10 +600,12 @@ def run_ours(args):
         t = torch.tensor([total_ms], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         total_ms = float(t.item())
-    step_ops = ops_of(SHAPES)
-    value = world * step_ops * args.steps / (total_ms / 1e3) / 1e12
+    step_ops = ops_of(SHAPES)                                            # one full sweep
+    rank_ops = sum(2.0 * it["M"] * it["N"] * it["K"] for it in items)   # this rank's share
+    job_ops = step_ops if strong else world * step_ops
+    value = job_ops * args.steps / (total_ms / 1e3) / 1e12
     launch_ms = sum(per_shape)
-    achieved = step_ops / (launch_ms / 1e3) / 1e12
+    achieved = rank_ops / (launch_ms / 1e3) / 1e12
     peaks, peak_src = read_peaks()
     int8_peak = 2.0 * peaks["bf16_tflops"]
 
@@ -596,10 +616,16 @@ def run_ours(args):
         t = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t.item())
-    e2e_value = world * step_ops * args.e2e_steps / (e2e_ms / 1e3) / 1e12
+    e2e_value = job_ops * args.e2e_steps / (e2e_ms / 1e3) / 1e12
 
     extras = {}
     if not args.no_extras:
+        c0 = build_gemm_set(torch, ops, dev, "int8", seed=5, m_of=lambda M: 256)[0]
+        c0_ms = _event_ms(torch, stream, lambda: ops.gemm_dequant(c0["x"], c0["w"], c0["xs"], c0["ws"], c0["bias"],
+                                                                  out=c0["out"], stream=stream), 50, 5)
+        extras["config0_gemm_256x3072x3072"] = {"us": round(c0_ms * 1e3, 2),
+                                                "tops": round(2.0 * 256 * 3072 * 3072 / (c0_ms / 1e3) / 1e12, 1)}
+        del c0
         extras["per_shape_tops"] = {f"{it['M']}x{it['N']}x{it['K']}": round(2 * it["M"] * it["N"] * it["K"] / (ms / 1e3) / 1e12, 1)
                                     for it, ms in zip(items, per_shape)}
         items8 = None
@@ -668,11 +694,13 @@ def run_ours(args):
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "TOPS", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 4), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "scaling": args.scaling, "vs_baseline": None, "dtype": "int8", "data": "synthetic",
             "config": {"workload": WORKLOAD, "shapes_MNK": SHAPES,
                        "activations": "bf16 N(0,1), 1% channels x20, per-token int8 (amax/127, RNE, clamp 127)",
                        "weights": "N(0,0.02) per-channel int8", "bias": "bf16 N(0,0.01)", "out": "bf16",
-                       "parallelism": f"token-sharded x{world} (weights replicated, no data-path collective)",
+                       "parallelism": f"token-sharded x{world} (weights replicated, no data-path collective)"
+                                      + ("; each rank runs 1/N of every shape's tokens" if strong else
+                                         "; each rank runs the full sweep on its own tokens"),
                        "l2": "inputs larger than L2: one step touches 0.47 GB of activations and writes "
                              "3.8 GB of outputs, so each shape's inputs are evicted before it repeats"},
             "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(int8_peak, 1),
