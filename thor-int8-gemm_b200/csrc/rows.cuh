@@ -805,6 +805,30 @@ __device__ __forceinline__ RowRegs<NV> load_row_regs(const uint8_t* slot, int la
   return r;
 }
 
+// Per-token quantisation, one row of 256 NV elements per warp held in registers (the
+// slot refills as soon as the row is loaded).
+template <int NV, int QK>
+__global__ void __launch_bounds__(512, 1) quant_rows_warp_reg_kernel(const QuantRowsArgs a, const WarpRingGeom g) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const int lane = threadIdx.x & 31;
+  auto src = [&](int64_t r) -> const void* { return a.x + r * a.ld_x; };
+  warp_row_loop_reg(
+      smem, g, a.S, src, [&](const uint8_t* slot) { return load_row_regs<NV>(slot, lane); },
+      [&](int64_t row, const RowRegs<NV>& r) {
+        uint32_t m2 = 0;
+#pragma unroll
+        for (int k = 0; k < NV; ++k) m2 = absmax4(m2, r.v[k]);
+        float m = pair_max(m2);
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, off));
+        const QuantRow qr = quant_row<QK>(m);
+        if (lane == 0) a.q_scale[row] = qr.scale;
+        uint8_t* qrow = static_cast<uint8_t*>(a.q) + row * a.ld_q;
+#pragma unroll
+        for (int k = 0; k < NV; ++k) store_q<QK>(qrow, 32 * k + lane, r.v[k], qr);
+      });
+}
+
 // Mixed-precision helpers: bf16 operands taken straight from the packed pair (no
 // unpacking), one rounding each.
 // acc.x += lo(u)^2, acc.y += hi(u)^2 (the squares of bf16 values are exact in fp32, so

@@ -766,6 +766,18 @@ int t8g_quant_rows(const void* x, int64_t ld_x, void* q, int64_t ld_q, float* q_
   a.S = S;
   a.D = static_cast<int>(D);
   const uint32_t row_bytes = static_cast<uint32_t>(2 * D);
+  if (const int nv = reg_nv(D)) {
+    WarpLaunch o;
+    o.max_warps = kRegWarps;
+    if (quant_kind == T8G_QUANT_FP8_E4M3) {
+      T8G_DISPATCH_NV(nv, rc = launch_warp_rows(quant_rows_warp_reg_kernel<NV, kQuantFp8>, a, row_bytes, S, dev,
+                                                info.sms, st, o, "quant_rows"));
+    } else {
+      T8G_DISPATCH_NV(nv, rc = launch_warp_rows(quant_rows_warp_reg_kernel<NV, kQuantInt8>, a, row_bytes, S, dev,
+                                                info.sms, st, o, "quant_rows"));
+    }
+    return rc;
+  }
   if (row_bytes <= kWarpRowMaxBytes) {
     if (quant_kind == T8G_QUANT_FP8_E4M3)
       return launch_warp_rows(quant_rows_warp_kernel<kQuantFp8>, a, row_bytes, S, dev, info.sms, st, WarpLaunch{}, "quant_rows");
