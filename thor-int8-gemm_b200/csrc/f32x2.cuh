@@ -27,6 +27,24 @@ __device__ __forceinline__ float2 bf2_to_f2(uint32_t u) {
 }
 __device__ __forceinline__ uint32_t f2_to_bf2(float2 v) { return pack_bf16(v.x, v.y); }
 
+// (p.x + lo(b), p.y + hi(b)) with b a packed bf16 (or fp16) pair, each an IEEE add taking
+// the 16-bit operand directly (mixed-precision add, no unpacking); an add with an explicit
+// rounding mode is never contracted with the product that feeds it.
+__device__ __forceinline__ float2 add_f32_bf16x2(float2 p, uint32_t b) {
+  float x, y;
+  asm("{ .reg .b16 lo, hi; mov.b32 {lo, hi}, %2; add.rn.f32.bf16 %0, lo, %3; add.rn.f32.bf16 %1, hi, %4; }"
+      : "=f"(x), "=f"(y)
+      : "r"(b), "f"(p.x), "f"(p.y));
+  return make_float2(x, y);
+}
+__device__ __forceinline__ float2 add_f32_f16x2(float2 p, uint32_t b) {
+  float x, y;
+  asm("{ .reg .b16 lo, hi; mov.b32 {lo, hi}, %2; add.rn.f32.f16 %0, lo, %3; add.rn.f32.f16 %1, hi, %4; }"
+      : "=f"(x), "=f"(y)
+      : "r"(b), "f"(p.x), "f"(p.y));
+  return make_float2(x, y);
+}
+
 // act = (g * sigmoid(g)) * u with sigmoid(g) = 1 / (1 + e^-g), in fp32 with the fast
 // hardware exponential and reciprocal (act is compared with the oracle within one bf16
 // ulp):

@@ -390,6 +390,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 struct TileParams {
   float ws[BN];
   float bias[BN];
+  uint32_t bias2[BN / 2];   // 2-byte outputs: the bias as packed pairs of the output type
 };
 
 template <int OUT>
@@ -399,6 +400,15 @@ __device__ __forceinline__ void stage_tile_params(const Args& args, int n_tile0,
     const bool in = n < args.N;
     tp.ws[j] = in ? __ldg(args.ws + (args.ws_stride ? n : 0)) : 0.f;
     tp.bias[j] = (in && args.bias) ? OutTraits<OUT>::to_f32(args.bias, n) : 0.f;
+  }
+  if constexpr (OutTraits<OUT>::kBytes == 2) {
+    const uint16_t* b16 = static_cast<const uint16_t*>(args.bias);
+    for (int j = e; j < BN / 2; j += ne) {
+      const int n = n_tile0 + 2 * j;
+      const uint32_t lo = (args.bias && n < args.N) ? b16[n] : 0u;
+      const uint32_t hi = (args.bias && n + 1 < args.N) ? b16[n + 1] : 0u;
+      tp.bias2[j] = lo | (hi << 16);
+    }
   }
 }
 
@@ -420,22 +430,44 @@ __device__ __forceinline__ void epilogue_tile_staged(const Args& args, const CUt
     for (int j = 0; j < 32; ++j) v[j] = (IN == kInI8) ? __int2float_rn(static_cast<int>(r[j])) : __uint_as_float(r[j]);
     if (c + 1 < nchunks) tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>((c + 1) * EPI_COLS), r);
     const float4* wq = reinterpret_cast<const float4*>(tp.ws + c * EPI_COLS);
-    const float4* bq = reinterpret_cast<const float4*>(tp.bias + c * EPI_COLS);
+    if constexpr (OutTraits<OUT>::kBytes == 2) {
+      // packed products, then the bias added from its 16-bit pair (mixed-precision add)
+      const uint4* bq2 = reinterpret_cast<const uint4*>(tp.bias2 + c * EPI_COLS / 2);
+      const float2 xs2 = make_float2(xs_r, xs_r);
 #pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      const float4 w4 = wq[q];
-      const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
-      float bb[4] = {0.f, 0.f, 0.f, 0.f};
-      if (has_bias) {
-        const float4 b4 = bq[q];
-        bb[0] = b4.x; bb[1] = b4.y; bb[2] = b4.z; bb[3] = b4.w;
+      for (int q = 0; q < 4; ++q) {
+        const float4 w0 = wq[2 * q], w1 = wq[2 * q + 1];
+        const float2 wp[4] = {make_float2(w0.x, w0.y), make_float2(w0.z, w0.w), make_float2(w1.x, w1.y),
+                              make_float2(w1.z, w1.w)};
+        const uint4 b4 = has_bias ? bq2[q] : make_uint4(0, 0, 0, 0);
+        const uint32_t bw[4] = {b4.x, b4.y, b4.z, b4.w};
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+          const int j = 8 * q + 2 * p;
+          float2 f = mul2_rn(mul2_rn(make_float2(v[j], v[j + 1]), xs2), wp[p]);
+          if (has_bias) f = (OUT == kOutF16) ? add_f32_f16x2(f, bw[p]) : add_f32_bf16x2(f, bw[p]);
+          v[j] = f.x;
+          v[j + 1] = f.y;
+        }
       }
+    } else {
+      const float4* bq = reinterpret_cast<const float4*>(tp.bias + c * EPI_COLS);
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        float f = __fmul_rn(v[4 * q + e], xs_r);
-        f = __fmul_rn(f, wv[e]);
-        if (has_bias) f = __fadd_rn(f, bb[e]);
-        v[4 * q + e] = f;
+      for (int q = 0; q < 8; ++q) {
+        const float4 w4 = wq[q];
+        const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
+        float bb[4] = {0.f, 0.f, 0.f, 0.f};
+        if (has_bias) {
+          const float4 b4 = bq[q];
+          bb[0] = b4.x; bb[1] = b4.y; bb[2] = b4.z; bb[3] = b4.w;
+        }
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          float f = __fmul_rn(v[4 * q + e], xs_r);
+          f = __fmul_rn(f, wv[e]);
+          if (has_bias) f = __fadd_rn(f, bb[e]);
+          v[4 * q + e] = f;
+        }
       }
     }
     const int n0 = n_tile0 + c * EPI_COLS;
@@ -471,6 +503,77 @@ __device__ __forceinline__ void epilogue_tile_staged(const Args& args, const CUt
     ebuf ^= 1;
   }
   if (nchunks == 0) tmem_ld_wait_regs(r);
+}
+
+// Epilogue of one 32-row slice for 2-byte outputs, 64 columns per chunk: two 32-column
+// TMEM loads per chunk (the next chunk's loads overlap this chunk's math), packed
+// products, the bias added from its 16-bit pair, and a 32 x 64 TMA store of full
+// 128-byte rows from a 128-byte-swizzled staging buffer.
+template <int IN, int OUT, int EPB>
+__device__ __forceinline__ void epilogue_tile_staged64(const Args& args, const CUtensorMap* tm_out,
+                                                       uint8_t (*bufs)[EPB], int& ebuf, uint32_t t_row, int row0,
+                                                       int n_tile0, int lane, uint64_t pol_out, float xs_r,
+                                                       const TileParams& tp) {
+  static_assert(EPB >= 32 * 128, "staging buffer holds 32 rows of 128 bytes");
+  const int nchunks = min(BN / 64, (args.N - n_tile0 + 63) / 64);
+  const bool has_bias = args.bias != nullptr;
+  const float2 xs2 = make_float2(xs_r, xs_r);
+  uint32_t r0[32], r1[32];
+  tmem_ld_32x32b_x32(t_row, r0);
+  tmem_ld_32x32b_x32(t_row + 32u, r1);
+  for (int c = 0; c < nchunks; ++c) {
+    tmem_ld_wait_regs(r0);
+    tmem_ld_wait_regs(r1);
+    float v[64];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      v[j] = (IN == kInI8) ? __int2float_rn(static_cast<int>(r0[j])) : __uint_as_float(r0[j]);
+      v[32 + j] = (IN == kInI8) ? __int2float_rn(static_cast<int>(r1[j])) : __uint_as_float(r1[j]);
+    }
+    if (c + 1 < nchunks) {
+      tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>((c + 1) * 64), r0);
+      tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>((c + 1) * 64 + 32), r1);
+    }
+    const float4* wq = reinterpret_cast<const float4*>(tp.ws + c * 64);
+    const uint4* bq2 = reinterpret_cast<const uint4*>(tp.bias2 + c * 32);
+    uint32_t packed[32];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const float4 w0 = wq[2 * q], w1 = wq[2 * q + 1];
+      const float2 wp[4] = {make_float2(w0.x, w0.y), make_float2(w0.z, w0.w), make_float2(w1.x, w1.y),
+                            make_float2(w1.z, w1.w)};
+      const uint4 b4 = has_bias ? bq2[q] : make_uint4(0, 0, 0, 0);
+      const uint32_t bw[4] = {b4.x, b4.y, b4.z, b4.w};
+#pragma unroll
+      for (int p = 0; p < 4; ++p) {
+        const int j = 8 * q + 2 * p;
+        float2 f = mul2_rn(mul2_rn(make_float2(v[j], v[j + 1]), xs2), wp[p]);
+        if (has_bias) f = (OUT == kOutF16) ? add_f32_f16x2(f, bw[p]) : add_f32_bf16x2(f, bw[p]);
+        packed[4 * q + p] = OutTraits<OUT>::pack2(f.x, f.y);
+      }
+    }
+    // the staging buffer used two chunks ago must have been read by its TMA store
+    if (lane == 0) bulk_wait_group_read<1>();
+    __syncwarp();
+    uint8_t* buf = bufs[ebuf];
+    // 32 rows x 128 B, 128-byte swizzle: 16-byte chunk q of row r lives at chunk q ^ (r & 7)
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const uint4 w = make_uint4(packed[4 * q + 0], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+      *reinterpret_cast<uint4*>(buf + lane * 128 + ((q ^ (lane & 7)) * 16)) = w;
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_2d(tm_out, buf, n_tile0 + c * 64, row0, pol_out);
+      bulk_commit_group();
+    }
+    ebuf ^= 1;
+  }
+  if (nchunks == 0) {
+    tmem_ld_wait_regs(r0);
+    tmem_ld_wait_regs(r1);
+  }
 }
 
 // SwiGLU epilogue of one 32-row slice: tile columns [0, 128) are gate and [128, 256) the
@@ -559,7 +662,10 @@ constexpr int P_STAGE_BYTES = P_A_BYTES + P_B_BYTES;   // per CTA
 // (6 x 32 KB ring + 16 KB staging + 4 KB parameters); fp32 outputs keep five.
 template <int OUT>
 struct PairCfg {
-  static constexpr int kEpiBytes = 32 * EPI_COLS * OutTraits<OUT>::kBytes;
+  // 2-byte outputs are stored in 32 x 64 boxes (full 128-byte rows, 128-byte swizzle),
+  // fp32 and the SwiGLU epilogue in 32 x 32 boxes
+  static constexpr int kEpiCols = (OutTraits<OUT>::kBytes == 2 && OUT != kOutSwiglu) ? 64 : EPI_COLS;
+  static constexpr int kEpiBytes = 32 * kEpiCols * OutTraits<OUT>::kBytes;
   static constexpr int kStages = 5;
 };
 
@@ -752,6 +858,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         if constexpr (OUT == kOutSwiglu)
           epilogue_tile_swiglu<IN, Cfg::kEpiBytes>(args, &tm_out, s.epi[ew], ebuf, t_row, row0, tn * BN, lane, pol_out,
                                                    xs_r, s.params[acc]);
+        else if constexpr (Cfg::kEpiCols == 64)
+          epilogue_tile_staged64<IN, OUT, Cfg::kEpiBytes>(args, &tm_out, s.epi[ew], ebuf, t_row, row0, tn * BN, lane,
+                                                          pol_out, xs_r, s.params[acc]);
         else
           epilogue_tile_staged<IN, OUT, Cfg::kEpiBytes>(args, &tm_out, s.epi[ew], ebuf, t_row, row0, tn * BN, lane,
                                                         pol_out, xs_r, s.params[acc]);

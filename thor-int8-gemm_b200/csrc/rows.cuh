@@ -840,15 +840,6 @@ __device__ __forceinline__ float2 sumsq_bf16x2(float2 acc, uint32_t u) {
       : "r"(u), "f"(acc.x), "f"(acc.y));
   return make_float2(x, y);
 }
-// (p.x + lo(b), p.y + hi(b)), each an IEEE add (an add with an explicit rounding mode is
-// never contracted with the product that feeds it).
-__device__ __forceinline__ float2 add_f32_bf16x2(float2 p, uint32_t b) {
-  float x, y;
-  asm("{ .reg .b16 lo, hi; mov.b32 {lo, hi}, %2; add.rn.f32.bf16 %0, lo, %3; add.rn.f32.bf16 %1, hi, %4; }"
-      : "=f"(x), "=f"(y)
-      : "r"(b), "f"(p.x), "f"(p.y));
-  return make_float2(x, y);
-}
 
 // The row-group size of the canonical sum for a row of `nvec` vectors (the host rule).
 __host__ __device__ constexpr int row_group_threads(int nvec) {

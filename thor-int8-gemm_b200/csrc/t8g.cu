@@ -192,8 +192,11 @@ int gemm_entry(int in_kind, const void* x, const void* w, const float* x_scale, 
   const CUtensorMapDataType out_dt = out_dtype == T8G_OUT_BF16  ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                      : out_dtype == T8G_OUT_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
                                                                 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
-  rc = encode_2d(&to, out_dt, out, N, M, ld_out * esz, EPI_COLS, 32,
-                 esz == 2 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B);
+  // the 2-SM kernel stores 2-byte outputs in 32 x 64 boxes (128-byte rows), the 1-SM kernel
+  // and fp32 outputs in 32 x 32 boxes
+  const bool box64 = pair && esz == 2;
+  rc = encode_2d(&to, out_dt, out, N, M, ld_out * esz, box64 ? 64 : EPI_COLS, 32,
+                 esz == 2 && !box64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
 
   Args args;
