@@ -144,52 +144,106 @@ def read_traffic():
 
 # --------------------------------------------------------------------- clocks
 class ClockSampler:
-    """nvidia-smi sampled every 200 ms while the timed region runs."""
+    """SM clock, power and clock-event reasons while the timed region runs: NVML polled every
+    5 ms from a thread (the record that is reported), and nvidia-smi every 200 ms beside it
+    (the same counters through the command-line tool; its reasons are merged in)."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
     REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+    NVML_BITS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+                 0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
 
     def __init__(self, gpu_id: str):
         self.gpu_id = gpu_id
         self.proc = None
+        self.samples = []
+        self.thread = None
+        self.running = False
+        self.nvml = None
+
+    def _nvml_handle(self):
+        import pynvml as nv
+        nv.nvmlInit()
+        if self.gpu_id.startswith("GPU-"):
+            return nv, nv.nvmlDeviceGetHandleByUUID(self.gpu_id)
+        return nv, nv.nvmlDeviceGetHandleByIndex(int(self.gpu_id))
 
     def start(self):
+        import threading
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu_id}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                  "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
-        time.sleep(0.3)
+        try:
+            nv, h = self._nvml_handle()
+            self.nvml = (nv, h)
+            self.max_mhz = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+        except Exception:
+            self.nvml = None
+        if self.nvml:
+            nv, h = self.nvml
+            self.running = True
 
-    def stop(self):
+            def poll():
+                while self.running:
+                    try:
+                        self.samples.append((nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM),
+                                             nv.nvmlDeviceGetPowerUsage(h) / 1000.0,
+                                             nv.nvmlDeviceGetCurrentClocksEventReasons(h)))
+                    except Exception:
+                        pass
+                    time.sleep(0.005)
+
+            self.thread = threading.Thread(target=poll, daemon=True)
+            self.thread.start()
+        time.sleep(0.3)   # nvidia-smi needs a moment before its first sample
+
+    def _smi_rows(self):
         if self.proc is None:
-            return None
-        time.sleep(0.3)
+            return []
         self.proc.terminate()
         try:
             out, _ = self.proc.communicate(timeout=5)
         except subprocess.TimeoutExpired:
             self.proc.kill()
             out, _ = self.proc.communicate()
-        rows = [r.split(",") for r in out.strip().splitlines() if r.count(",") >= 8]
-        if not rows:
-            return None
-        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
-        smax = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
-        power = [float(r[3]) for r in rows if r[3].strip().replace(".", "").isdigit()]
+        return [r.split(",") for r in out.strip().splitlines() if r.count(",") >= 8]
+
+    def stop(self):
+        self.running = False
+        if self.thread is not None:
+            self.thread.join(timeout=2)
+        rows = self._smi_rows()
         reasons = set()
         for r in rows:
             for name, v in zip(self.REASONS, r[5:9]):
                 if v.strip().lower() == "active":
                     reasons.add(name)
+        if self.samples:
+            sm = [s for s, _, _ in self.samples]
+            loaded = [s for s, _, bits in self.samples if not bits & 0x1] or sm   # 0x1: GPU idle
+            for _, _, bits in self.samples:
+                for bit, name in self.NVML_BITS.items():
+                    if bits & bit:
+                        reasons.add(name)
+            return {"sm_mhz": statistics.median(loaded), "sm_mhz_min": min(loaded), "sm_max_mhz": self.max_mhz,
+                    "power_w_max": round(max(p for _, p, _ in self.samples), 1), "samples": len(self.samples),
+                    "source": "nvml every 5 ms during the timed region (+ nvidia-smi reasons)",
+                    "reasons": sorted(reasons)}
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
+        smax = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
+        power = [float(r[3]) for r in rows if r[3].strip().replace(".", "").isdigit()]
         loaded = [s for s in sm if smax and s > 0.5 * max(smax)] or sm
         return {"sm_mhz": statistics.median(loaded) if loaded else None,
                 "sm_max_mhz": max(smax) if smax else None,
                 "power_w_max": max(power) if power else None,
-                "samples": len(rows), "reasons": sorted(reasons)}
+                "samples": len(rows), "source": "nvidia-smi every 200 ms", "reasons": sorted(reasons)}
 
 
 def gpu_smi_id(torch, dev):

@@ -9,6 +9,7 @@
 #include <stdio.h>
 #include <stdlib.h>
 
+#include <atomic>
 #include <mutex>
 
 #include "../../include/thor_int8_gemm_b200.h"
@@ -68,11 +69,12 @@ int current_device(int* dev, DeviceInfo* info) {
 
 // Sets the dynamic shared-memory limit of `fn` once per device.
 template <typename F>
-int ensure_smem_attr(F fn, int dev, size_t bytes, bool* done_per_device) {
-  if (done_per_device[dev]) return T8G_OK;
+int ensure_smem_attr(F fn, int dev, size_t bytes, std::atomic<bool>* done_per_device) {
+  if (done_per_device[dev].load(std::memory_order_acquire)) return T8G_OK;
+  // setting the attribute twice (two threads racing on the first call) is harmless
   T8G_CHECK_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes)),
                  "cudaFuncSetAttribute");
-  done_per_device[dev] = true;
+  done_per_device[dev].store(true, std::memory_order_release);
   return T8G_OK;
 }
 
@@ -117,7 +119,7 @@ template <int IN, int OUT>
 int launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
                      const t8g::gemm::Args& args, int dev, int sms, cudaStream_t stream) {
   using namespace t8g::gemm;
-  static bool attr_done[kMaxDevices] = {};
+  static std::atomic<bool> attr_done[kMaxDevices] = {};
   auto kern = gemm_dequant_pair_kernel<IN, OUT>;
   int rc = ensure_smem_attr(kern, dev, pair_smem_bytes<OUT>(), attr_done);
   if (rc) return rc;
@@ -138,7 +140,7 @@ template <int IN, int OUT>
 int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to, const t8g::gemm::Args& args,
                 int dev, int sms, cudaStream_t stream) {
   using namespace t8g::gemm;
-  static bool attr_done[kMaxDevices] = {};
+  static std::atomic<bool> attr_done[kMaxDevices] = {};
   auto kern = gemm_dequant_kernel<IN, OUT>;
   int rc = ensure_smem_attr(kern, dev, SMEM_BYTES, attr_done);
   if (rc) return rc;
