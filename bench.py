@@ -411,6 +411,13 @@ def time_rows(torch, ops, dev, steps, warmup, stream):
               norm_bytes, f"rms_mod_quant_{kind}")
     sw_bytes = 4 * Mf * F + Mf * F + 4 * Mf
     timed(lambda: ops.swiglu_quant_fc1(y, kind="int8", stream=stream), sw_bytes, "swiglu_quant_int8")
+    # the reference's tensorwise two-phase forms (one fp8 scale per tensor; h / res / act
+    # written by phase A and read back by phase B): 9 bytes per element
+    timed(lambda: ops.rms_mod_quant_tensorwise(x, shift, scale, rows_per_mod=T, eps=1e-6, kind="fp8_e4m3",
+                                               want_res=True, stream=stream),
+          9 * B * T * D + 2 * 2 * B * D, "rms_mod_quant_tensorwise_fp8")
+    timed(lambda: ops.swiglu_quant_tensorwise(y[:, :F], y[:, F:], kind="fp8_e4m3", stream=stream),
+          9 * Mf * F, "swiglu_quant_tensorwise_fp8")
     del x, y
     return res
 

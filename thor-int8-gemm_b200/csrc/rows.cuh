@@ -186,6 +186,14 @@ __device__ __forceinline__ void atomic_max_nonneg(float* addr, float v) {
   atomicMax(reinterpret_cast<int*>(addr), __float_as_int(v));
 }
 
+// Folds each thread's running max of its rows into the tensor's amax word with one atomic
+// per warp, after the warp's last row (an atomic per row serialises on the single word).
+__device__ __forceinline__ void flush_amax(float* amax, float m) {
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, off));
+  if ((threadIdx.x & 31) == 0 && m > 0.f) atomic_max_nonneg(amax, m);
+}
+
 // ---------------------------------------------------------------- row ring
 // Shared-memory layout of every row kernel: mbarriers, reduction scratch, then
 // `stages` slots of `slot_bytes` (1024-byte aligned).
@@ -566,6 +574,7 @@ __global__ void __launch_bounds__(512) rms_mod_kernel(const RmsArgs a, const Rin
   int64_t cur_m = -1;
   int64_t seg_end = -1;          // first row past the current batch element (rows_per_mod layout)
   auto src = [&](int64_t r, int) -> const void* { return a.x + r * a.ld_x; };
+  float tw_max = 0.f;   // tensorwise: running max of |h| over this thread's rows
   row_loop(smem, g, a.S, src, [&](int64_t row, uint8_t* slot, const RingState& rs) {
     // pass 1: sum of squares in the canonical order
     float2 acc = make_float2(0.f, 0.f);
@@ -639,12 +648,9 @@ __global__ void __launch_bounds__(512) rms_mod_kernel(const RmsArgs a, const Rin
         for (int c = threadIdx.x; c < nvec; c += T) store_q<QK>(qrow, c, lds_v4(slot + 16 * c), qr);
       }
     }
-    if constexpr (MODE == kModeTensorwise) {
-#pragma unroll
-      for (int off = 16; off >= 1; off >>= 1) amax32 = fmaxf(amax32, __shfl_xor_sync(0xFFFFFFFFu, amax32, off));
-      if ((threadIdx.x & 31) == 0 && amax32 > 0.f) atomic_max_nonneg(a.amax, amax32);
-    }
+    if constexpr (MODE == kModeTensorwise) tw_max = fmaxf(tw_max, amax32);
   });
+  if constexpr (MODE == kModeTensorwise) flush_amax(a.amax, tw_max);
 }
 
 // RMSNorm + modulation + quantisation, one row per warp (rows of at most
@@ -664,6 +670,7 @@ __global__ void __launch_bounds__(1024) rms_mod_warp_kernel(const RmsArgs a, con
   int64_t cur_m = -1;
   int64_t seg_end = -1;   // first row past the current batch element (rows_per_mod layout)
   auto src = [&](int64_t r) -> const void* { return a.x + r * a.ld_x; };
+  float tw_max = 0.f;   // tensorwise: running max of |h| over this thread's rows
   warp_row_loop(smem, g, a.S, src, [&](int64_t row, uint8_t* slot) {
     // pass 1: sum of squares, virtual warp by virtual warp
     float ss = 0.f;
@@ -711,11 +718,10 @@ __global__ void __launch_bounds__(1024) rms_mod_warp_kernel(const RmsArgs a, con
 #pragma unroll 4
       for (int c = lane; c < nvec; c += 32) store_q<QK>(qrow, c, lds_v4(slot + 16 * c), qr);
     } else {
-#pragma unroll
-      for (int off = 16; off >= 1; off >>= 1) amax32 = fmaxf(amax32, __shfl_xor_sync(0xFFFFFFFFu, amax32, off));
-      if (lane == 0 && amax32 > 0.f) atomic_max_nonneg(a.amax, amax32);
+      tw_max = fmaxf(tw_max, amax32);
     }
   });
+  if constexpr (MODE == kModeTensorwise) flush_amax(a.amax, tw_max);
 }
 
 // ---------------------------------------------------------------- register-resident warp rows
@@ -1006,6 +1012,7 @@ __global__ void __launch_bounds__(512, 1) rms_mod_warp_reg_kernel(const RmsArgs 
   int64_t cur_m = -1;
   int64_t seg_end = -1;
   auto src = [&](int64_t r) -> const void* { return a.x + r * a.ld_x; };
+  float tw_max = 0.f;   // tensorwise: running max of |h| over this thread's rows
   warp_row_loop_reg(
       smem, g, a.S, src, [&](const uint8_t* slot) { return load_row_regs<NV>(slot, lane); },
       [&](int64_t row, RowRegs<NV>& r) {
@@ -1077,11 +1084,10 @@ __global__ void __launch_bounds__(512, 1) rms_mod_warp_reg_kernel(const RmsArgs 
 #pragma unroll
           for (int k = 0; k < NV; ++k) store_q<QK>(qrow, 32 * k + lane, r.v[k], qr);
         } else {
-#pragma unroll
-          for (int off = 16; off >= 1; off >>= 1) amax32 = fmaxf(amax32, __shfl_xor_sync(0xFFFFFFFFu, amax32, off));
-          if (lane == 0 && amax32 > 0.f) atomic_max_nonneg(a.amax, amax32);
+          tw_max = fmaxf(tw_max, amax32);
         }
       });
+  if constexpr (MODE == kModeTensorwise) flush_amax(a.amax, tw_max);
 }
 
 // ---------------------------------------------------------------- SwiGLU
@@ -1114,6 +1120,7 @@ __global__ void __launch_bounds__(1024) swiglu_kernel(const SwigluArgs a, const 
   const int T = blockDim.x;
   const int nvec = a.F >> 3;
   auto src = [&](int64_t r, int part) -> const void* { return (part ? a.up : a.gate) + r * a.ld_in; };
+  float tw_max = 0.f;   // tensorwise: running max of |h| over this thread's rows
   row_loop(smem, g, a.M, src, [&](int64_t row, uint8_t* slot, const RingState& rs) {
     const uint8_t* up = slot + g.part_bytes;
     uint8_t* qrow = static_cast<uint8_t*>(a.q) + row * a.ld_q;
@@ -1157,12 +1164,9 @@ __global__ void __launch_bounds__(1024) swiglu_kernel(const SwigluArgs a, const 
         for (int c = threadIdx.x; c < nvec; c += T) store_q<QK>(qrow, c, lds_v4(slot + 16 * c), qr);
       }
     }
-    if constexpr (kTw) {
-#pragma unroll
-      for (int off = 16; off >= 1; off >>= 1) amax32 = fmaxf(amax32, __shfl_xor_sync(0xFFFFFFFFu, amax32, off));
-      if ((threadIdx.x & 31) == 0 && amax32 > 0.f) atomic_max_nonneg(a.amax, amax32);
-    }
+    if constexpr (kTw) tw_max = fmaxf(tw_max, amax32);
   });
+  if constexpr (MODE == kModeTensorwise) flush_amax(a.amax, tw_max);
 }
 
 // ---------------------------------------------------------------------------
@@ -1185,14 +1189,42 @@ __global__ void __launch_bounds__(256) quant_given_amax_kernel(const QuantGivenA
   const QuantRow qr = quant_row<QK>(*a.amax);
   if (blockIdx.x == 0 && threadIdx.x == 0 && a.scale_out) *a.scale_out = qr.scale;
   const int nvec = a.D >> 3;
-  const int64_t total = a.S * nvec;
-  for (int64_t v = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; v < total;
-       v += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t row = v / nvec;
-    const int c = static_cast<int>(v - row * nvec);
-    float2 f[4];
-    unpack_pairs(ld_v4(a.h + row * a.ld_h + 8 * c), f);
-    *reinterpret_cast<uint2*>(static_cast<uint8_t*>(a.q) + row * a.ld_q + 8 * c) = quant8<QK>(f, qr);
+  const int64_t G = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  const int64_t t0 = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (a.ld_h == a.D && a.ld_q == a.D) {
+    // contiguous rows: one flat run of vectors, four loads in flight per thread
+    const int64_t total = a.S * nvec;
+    const uint4* hv = reinterpret_cast<const uint4*>(a.h);
+    uint2* qv = reinterpret_cast<uint2*>(a.q);
+    int64_t v = t0;
+    for (; v + 3 * G < total; v += 4 * G) {
+      uint4 u[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) u[i] = ld_v4(hv + v + i * G);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float2 f[4];
+        unpack_pairs(u[i], f);
+        qv[v + i * G] = quant8<QK>(f, qr);
+      }
+    }
+    for (; v < total; v += G) {
+      float2 f[4];
+      unpack_pairs(ld_v4(hv + v), f);
+      qv[v] = quant8<QK>(f, qr);
+    }
+  } else {
+    // strided rows: warps over rows, lanes over a row's vectors
+    const int lane = threadIdx.x & 31;
+    for (int64_t row = t0 >> 5; row < a.S; row += G >> 5) {
+      const __nv_bfloat16* hrow = a.h + row * a.ld_h;
+      uint8_t* qrow = static_cast<uint8_t*>(a.q) + row * a.ld_q;
+      for (int c = lane; c < nvec; c += 32) {
+        float2 f[4];
+        unpack_pairs(ld_v4(hrow + 8 * c), f);
+        *reinterpret_cast<uint2*>(qrow + 8 * c) = quant8<QK>(f, qr);
+      }
+    }
   }
 }
 

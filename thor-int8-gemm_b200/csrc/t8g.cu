@@ -498,9 +498,10 @@ int launch_checked(const char* what) {
 
 int launch_quant_given(const t8g::rows::QuantGivenArgs& b, int quant_kind, int sms, cudaStream_t st) {
   using namespace t8g::rows;
+  // 8 CTAs of 256 threads per SM; the kernel strides over vectors (contiguous rows) or rows
   const int64_t vecs = b.S * (b.D / 8);
   const int64_t want = (vecs + 255) / 256;
-  const unsigned grid = static_cast<unsigned>(want < int64_t(sms) * 16 ? want : int64_t(sms) * 16);
+  const unsigned grid = static_cast<unsigned>(want < int64_t(sms) * 8 ? want : int64_t(sms) * 8);
   if (quant_kind == T8G_QUANT_FP8_E4M3)
     quant_given_amax_kernel<kQuantFp8><<<grid, 256, 0, st>>>(b);
   else
