@@ -140,6 +140,31 @@ def test_gemm_i8_full_size_row_sampled(ops, path):
     np.testing.assert_array_equal(out_bits(out[torch.from_numpy(rows).to(dev)]), ref)
 
 
+@pytest.mark.parametrize("M,K,N,bias", [(128, 6144, 6144, True), (8000, 6144, 6144, False),
+                                        (32000, 6144, 16384, True), (96, 16384, 6144, False)])
+def test_gemm_reference_exact_test_shapes(ops, M, K, N, bias):
+    """The shapes and input distributions of the reference's bit-exactness check
+    (tests/exact_test.py:8-13: int8 weights in [-127, 127), scales rand + 0.5, bf16 bias,
+    activations randn * 8 clamped to +-120 and quantised per token; its K = 6143 case is
+    outside the proxy's K % 16 rule and goes to stock).  Sampled rows bit-exact, and a
+    second call gives the same bits (the reference's repeat check, bench/a2_fused_bench.py:127-128)."""
+    dev = "cuda"
+    g = torch.Generator(device=dev).manual_seed(M + N)
+    w8 = torch.randint(-127, 127, (N, K), dtype=torch.int8, device=dev, generator=g)
+    ws = torch.rand(N, device=dev, generator=g) + 0.5
+    b = torch.randn(N, device=dev, dtype=torch.bfloat16, generator=g) if bias else None
+    x = (torch.randn(M, K, device=dev, dtype=torch.bfloat16, generator=g) * 8).clamp(-120, 120)
+    xq, xs = ops.quant_rows(x, "int8")
+    out = ops.gemm_dequant(xq, w8, xs, ws, b)
+    again = ops.gemm_dequant(xq, w8, xs, ws, b)
+    assert torch.equal(out, again)
+    rows = np.unique(np.concatenate([[0, M - 1], np.random.default_rng(M).choice(M, 24, replace=False)]))
+    ridx = torch.from_numpy(rows).to(dev)
+    ref = O.gemm_i8_dequant(xq[ridx].cpu().numpy(), w8.cpu().numpy(), xs[ridx].cpu().numpy(), ws.cpu().numpy(),
+                            None if b is None else b.float().cpu().numpy(), "bf16")
+    np.testing.assert_array_equal(out_bits(out[ridx]), ref)
+
+
 @pytest.mark.parametrize("M,N,K,dt", [(256, 512, 512, "bf16"), (1000, 272, 3072, "f32"), (130, 136, 96, "f16")])
 def test_gemm_fp8_within_accumulation_tolerance(ops, path, M, N, K, dt):
     dev = "cuda"

@@ -147,8 +147,8 @@ def _tie_row(kind, D):
 @pytest.mark.parametrize("D", [1024, 3072, 2560])
 def test_rms_mod_quant_quantiser_ties(ops, kind, D):
     """scale = -1 makes s = bf16(1 + scale) = 0, so h = shift exactly: rows of tie values
-    reach the norm kernels' quantiser (the deferred exact path of every vector slot of
-    the register-resident kernels; D = 2560 takes the shared-memory warp kernel)."""
+    reach the norm kernels' quantiser in every vector slot of the register-resident
+    kernels (D = 2560 takes the shared-memory warp kernel)."""
     S = 40
     rng = np.random.default_rng(D)
     x = O.round_bf16(rng.standard_normal((S, D)).astype(np.float32))
@@ -350,3 +350,24 @@ def test_quantiser_ties_and_format_midpoints(ops, kind):
     assert np.all(s_ref == 1.0)
     np.testing.assert_array_equal(s.cpu().numpy(), s_ref)
     np.testing.assert_array_equal(qbits(q, kind), q_ref)
+
+
+def test_row_kernels_deterministic(ops):
+    """Repeat calls give identical bits (the reference's repeat check,
+    bench/a2_fused_bench.py:127-128), including the tensorwise forms, whose amax is an
+    atomic max (order-free)."""
+    g = torch.Generator(device="cuda").manual_seed(2)
+    x = torch.randn(6000, 3072, generator=g, device="cuda").to(torch.bfloat16)
+    sh = (torch.randn(2, 3072, generator=g, device="cuda") * 0.1).to(torch.bfloat16)
+    sc = (torch.randn(2, 3072, generator=g, device="cuda") * 0.1).to(torch.bfloat16)
+    y = torch.randn(3000, 2 * 2048, generator=g, device="cuda").to(torch.bfloat16)
+    calls = [lambda: ops.quant_rows(x, "int8"),
+             lambda: ops.rms_mod_quant(x, sh, sc, rows_per_mod=3000, eps=1e-6, kind="fp8_e4m3"),
+             lambda: ops.rms_mod_quant_tensorwise(x, sh, sc, rows_per_mod=3000, eps=1e-6, kind="fp8_e4m3")[:3],
+             lambda: ops.swiglu_quant_fc1(y, kind="int8"),
+             lambda: ops.swiglu_quant_tensorwise(y[:, :2048], y[:, 2048:], kind="fp8_e4m3")]
+    for fn in calls:
+        a, b = fn(), fn()
+        for ta, tb in zip(a, b):
+            assert torch.equal(ta.view(torch.uint8) if ta.dtype == torch.float8_e4m3fn else ta,
+                               tb.view(torch.uint8) if tb.dtype == torch.float8_e4m3fn else tb)
