@@ -322,13 +322,24 @@ def time_gemm_sweep(torch, ops, items, steps, warmup, stream):
     return total_ms, per_shape
 
 
+class _NoStock:
+    """The comfy-kitchen `_C` behind the proxy: the e2e sweep must never fall back to it."""
+
+    def cutlass_int8_dequant(self, *args):
+        raise RuntimeError("the B200 GEMM declined a call the bench expects it to take")
+
+
 def time_e2e(torch, ops, items, steps, dev):
-    """Same sweep through the public API with host activations in and outputs out.
+    """Same sweep through the reference-facing entry point -- comfy-kitchen's
+    `_C.cutlass_int8_dequant(x, w, x_scale, w_scale, bias, out, dtype_code, stream)` as the
+    `.pth` proxy serves it, DLPack capsules in -- with host activations in and outputs out.
 
     Three streams pipeline the shapes: copy-in of shape i+1 and copy-out of
     shape i-1 overlap the GEMM of shape i.  Weights stay resident on the device
     (model parameters); activations + their scales are copied in and every
     output is copied back, every step."""
+    from thor_int8_gemm_b200 import patch_int8
+    proxy = patch_int8._CProxy(_NoStock())
     h2d, comp, d2h = (torch.cuda.Stream(dev) for _ in range(3))
     host_x = [it["x"].cpu().pin_memory() for it in items]
     host_xs = [it["xs"].cpu().pin_memory() for it in items]
@@ -352,7 +363,8 @@ def time_e2e(torch, ops, items, steps, dev):
             comp.wait_event(ev_in[i])
             if not first[i]:
                 comp.wait_event(ev_out[i])
-            ops.gemm_dequant(dx[i], it["w"], dxs[i], it["ws"], it["bias"], out=it["out"], stream=comp)
+            caps = tuple(t.__dlpack__(stream=-1) for t in (dx[i], it["w"], dxs[i], it["ws"], it["bias"], it["out"]))
+            assert proxy.cutlass_int8_dequant(*caps, 0, comp.cuda_stream) is True
             ev_gemm[i].record(comp)
             with torch.cuda.stream(d2h):
                 d2h.wait_event(ev_gemm[i])
@@ -775,8 +787,9 @@ def run_ours(args):
                          "kernel": "gemm_dequant_kernel<int8,bf16>"},
             "e2e": {"value": round(e2e_value, 2), "unit": "TOPS", "h2d_bytes_per_step": h2d_b,
                     "d2h_bytes_per_step": d2h_b, "outputs_verified": bool(e2e_ok),
-                    "note": "activations + scales copied in and all outputs copied back every step; "
-                            "weights resident; 3-stream pipeline"},
+                    "note": "through the _C.cutlass_int8_dequant proxy (DLPack capsules); activations + scales "
+                            "copied in and all outputs copied back every step; weights resident; "
+                            "3-stream pipeline"},
             "gpu_launches": len(SHAPES) * args.steps,
             "clocks": clk,
             "device_status": status,
