@@ -526,9 +526,19 @@ def time_dit_block(torch, dev, steps, warmup, stream, seed, tokens=112640, batch
     full_ms = _event_ms(torch, stream, lambda: blk(x, cond, batch), steps, warmup)
     lin_ms = _event_ms(torch, stream, lambda: blk.linears_and_norms(x, cond, batch, attn_fn=values_only), steps, warmup)
     lin_ops = blk.linear_ops(tokens)
+    del blk
+    torch.cuda.empty_cache()
+    # the same block with fc1's SwiGLU and both gated residuals in the GEMM epilogues
+    fblk = dit.DiTBlock(3072, 24, 12288, kind="int8", device=dev, seed=seed, fused_mlp=True, fused_gate=True)
+    ffull_ms = _event_ms(torch, stream, lambda: fblk(x, cond, batch), steps, warmup)
+    flin_ms = _event_ms(torch, stream, lambda: fblk.linears_and_norms(x, cond, batch, attn_fn=values_only), steps,
+                        warmup)
     return {"tokens": tokens, "batch": batch, "block_ms": round(full_ms, 3),
             "linears_and_norms_ms": round(lin_ms, 3), "linear_tops": round(lin_ops / (lin_ms / 1e3) / 1e12, 1),
-            "note": "block_ms includes torch SDPA attention (outside the hot path)"}
+            "fused_block_ms": round(ffull_ms, 3), "fused_linears_and_norms_ms": round(flin_ms, 3),
+            "fused_linear_tops": round(lin_ops / (flin_ms / 1e3) / 1e12, 1),
+            "note": "block_ms includes torch SDPA attention (outside the hot path); fused_*: fc1 with the "
+                    "SwiGLU epilogue, proj and fc2 with the gated-residual epilogue"}
 
 
 def time_reference_path_gpu(torch, items, steps, stream):

@@ -105,6 +105,30 @@ int t8g_gemm_fp8_swiglu(const void* x, const void* w, const float* x_scale, cons
                         int64_t K, int64_t ld_x, int64_t ld_w, int64_t ld_act, void* stream);
 
 /*
+ * Fused-dequant GEMM whose epilogue applies the DiT block's gated residual, the stock
+ * `x = _mod_gate(x, gate, proj(h), mod_segments)` after the attention and MLP projections
+ * (the block's call order, src/ck_fused_patch.py:153-172), in torch's bf16 operation order:
+ *   y   = bf16(f32(acc) * x_scale[m] * w_scale[n] + f32(bias[n]))      (as t8g_gemm_i8_dequant)
+ *   t   = bf16(f32(gate[g, n]) * f32(y))
+ *   out = bf16(f32(res[m, n]) + f32(t)),   g = gate_index[m] if non-NULL, else m / rows_per_gate.
+ *   res, out bf16 [M, N] (ld_res, ld_out); gate bf16 [n_gate, N] (ld_gate); gate_index int32 [M]
+ *   (trusted to hold rows of gate).  out may be res itself (in-place update); otherwise the
+ *   two must not overlap.  The bf16 projection output y is never written to memory.
+ * Requirements as t8g_gemm_i8_dequant with a bf16 output, plus N a multiple of 8, res/gate
+ * 16-byte aligned and ld_res, ld_gate multiples of 8.
+ */
+int t8g_gemm_i8_gated(const void* x, const void* w, const float* x_scale, const float* w_scale,
+                      int64_t w_scale_numel, const void* bias, int64_t bias_numel, const void* res, int64_t ld_res,
+                      const void* gate, int64_t ld_gate, const int32_t* gate_index, int64_t rows_per_gate, void* out,
+                      int64_t M, int64_t N, int64_t K, int64_t ld_x, int64_t ld_w, int64_t ld_out, void* stream);
+
+/* float8_e4m3fn twin of t8g_gemm_i8_gated. */
+int t8g_gemm_fp8_gated(const void* x, const void* w, const float* x_scale, const float* w_scale,
+                       int64_t w_scale_numel, const void* bias, int64_t bias_numel, const void* res, int64_t ld_res,
+                       const void* gate, int64_t ld_gate, const int32_t* gate_index, int64_t rows_per_gate, void* out,
+                       int64_t M, int64_t N, int64_t K, int64_t ld_x, int64_t ld_w, int64_t ld_out, void* stream);
+
+/*
  * Per-token quantisation of a bf16 matrix: q_scale[m] = max(amax_k |x[m,k]| / qmax, 1e-12),
  * q[m, k] = cvt(clamp(x[m, k] / q_scale[m])).  This is the activation quantiser that
  * comfy-kitchen's int8_linear runs in front of _C.cutlass_int8_dequant (its code is not

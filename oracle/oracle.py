@@ -16,6 +16,7 @@ Reference functions restated here (paths inside the reference project):
 * `fused_rms_mod_quant`              src/ck_fused_mod_norm_quant.py:121-145
 * `fused_swiglu_quant`               src/ck_fused_mod_norm_quant.py:148-167
 * `1 + scale` rounded in bf16        src/ck_fused_patch.py:119-121
+* the block's gated residual         src/ck_fused_patch.py:160-161, :172 (comfy `_mod_gate`)
 
 Per-token quantisation (scale = amax/127 or amax/448 per row, round half to
 even, clamp) has no code in the reference: it lives in comfy-kitchen's
@@ -269,6 +270,17 @@ def fp8_gemm_tolerance(a_codes, w_codes, xs, ws, K: int) -> np.ndarray:
     ws = np.asarray(ws, np.float64).reshape(-1)
     sc = np.abs(np.asarray(xs, np.float64)).reshape(-1, 1) * np.abs(ws.reshape(1, -1) if ws.size > 1 else ws.reshape(1, 1))
     return mag * sc * (max(K, 1) * 2.0 ** -22)
+
+
+def gated_residual(res_f32, gate_rows_f32, y_f32) -> np.ndarray:
+    """The block's gated residual update after the attention and MLP projections,
+    `x = _mod_gate(x, gate, y, mod_segments)` (call sites src/ck_fused_patch.py:160-161 and
+    :172; comfy's `_mod_gate` itself is not vendored, so this is the plain x + gate * y
+    form, unpinned against comfy) in torch's bf16 eager order: t = bf16(gate * y) computed
+    in float32, then bf16(x + t).  All inputs are bf16 values held as float32, gate_rows
+    already expanded to the rows of y.  Returns bf16 bits."""
+    t = round_bf16((np.asarray(gate_rows_f32, np.float32) * np.asarray(y_f32, np.float32)).astype(np.float32))
+    return f32_to_bf16((np.asarray(res_f32, np.float32) + t).astype(np.float32))
 
 
 # --------------------------------------------------------------------------

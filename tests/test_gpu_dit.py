@@ -115,3 +115,20 @@ def test_dit_block_fused_mlp_matches(mods, kind):
         assert torch.equal(a, b)
     else:
         assert O.bf16_ulp_distance(bits16(a), bits16(b)).max() <= 2
+
+
+@pytest.mark.parametrize("B,T,fused_mlp", [(2, 96, False), (2, 96, True), (1, 100, True), (3, 200, False)])
+def test_dit_block_fused_gate_matches(mods, B, T, fused_mlp):
+    """proj and fc2 with the gated residual in their epilogue give the stock block's output
+    bit for bit (int8), and leave the caller's x untouched."""
+    dit, ops = mods
+    hidden, heads, ffn = 256, 2, 512
+    g = torch.Generator(device="cuda").manual_seed(B * T)
+    x = torch.randn(B * T, hidden, generator=g, device="cuda").to(torch.bfloat16)
+    x0 = x.clone()
+    cond = (torch.randn(B, 6 * hidden, generator=g, device="cuda") * 0.1).to(torch.bfloat16)
+    plain = dit.DiTBlock(hidden, heads, ffn, kind="int8", device="cuda", seed=31)
+    fused = dit.DiTBlock(hidden, heads, ffn, kind="int8", device="cuda", seed=31, fused_mlp=fused_mlp,
+                         fused_gate=True)
+    assert torch.equal(plain(x, cond, B), fused(x, cond, B))
+    assert torch.equal(x, x0)

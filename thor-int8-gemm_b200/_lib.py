@@ -35,6 +35,10 @@ SIGNATURES = {
                                     _i64, _i64, _i64, _i64, _i64, _i64, _vp]),
     "t8g_gemm_i8_swiglu": (_i32, [_vp, _vp, _vp, _vp, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _vp]),
     "t8g_gemm_fp8_swiglu": (_i32, [_vp, _vp, _vp, _vp, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _vp]),
+    "t8g_gemm_i8_gated": (_i32, [_vp, _vp, _vp, _vp, _i64, _vp, _i64, _vp, _i64, _vp, _i64, _vp, _i64, _vp,
+                                 _i64, _i64, _i64, _i64, _i64, _i64, _vp]),
+    "t8g_gemm_fp8_gated": (_i32, [_vp, _vp, _vp, _vp, _i64, _vp, _i64, _vp, _i64, _vp, _i64, _vp, _i64, _vp,
+                                  _i64, _i64, _i64, _i64, _i64, _i64, _vp]),
     "t8g_quant_rows": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _i64, _i32, _vp]),
     "t8g_rms_mod_quant": (_i32, [_vp, _i64, _vp, _vp, _vp, _i64, _vp, _i64, _i32, _f32,
                                  _vp, _i64, _vp, _vp, _i64, _vp, _i64, _i64, _i64, _i32, _vp]),

@@ -30,10 +30,12 @@ namespace t8g {
 namespace gemm {
 
 enum InKind : int { kInI8 = 0, kInE4M3 = 1 };
-enum OutKind : int { kOutBF16 = 0, kOutF16 = 1, kOutF32 = 2, kOutSwiglu = 3 };
+enum OutKind : int { kOutBF16 = 0, kOutF16 = 1, kOutF32 = 2, kOutSwiglu = 3, kOutGated = 4 };
 // kOutSwiglu: the GEMM's bf16 output columns come in 128-column gate / up blocks (weights
 // interleaved so that every 256-column tile holds 128 gate columns and the matching 128 up
 // columns); the epilogue stores act = silu(gate) * up (bf16, half the columns) instead.
+// kOutGated: bf16 output updated as a gated residual, out = res + gate[row's gate row] * y
+// (the DiT block's `x + gate * proj(...)`), with y the bf16 GEMM output; out may be res.
 
 constexpr int BM = 128;          // tile rows (tokens)
 constexpr int BN = 256;          // tile columns (output channels)
@@ -69,6 +71,12 @@ struct Args {
   int ws_stride;      // 1: per channel, 0: one scalar
   int vec_ok;         // ws and bias are 16-byte aligned
   int M, N, K;
+  // kOutGated only: out = bf16(res + bf16(gate[grow] * bf16(y))), y the dequantised GEMM
+  // output and grow = gate_index[m] (or m / rows_per_gate); res and gate are bf16
+  const void* res;
+  const void* gate;
+  const int32_t* gate_index;
+  int64_t ld_res, ld_gate, rows_per_gate;
 };
 
 template <int OUT>
@@ -86,6 +94,8 @@ struct OutTraits<kOutBF16> {
 };
 template <>
 struct OutTraits<kOutSwiglu> : OutTraits<kOutBF16> {};
+template <>
+struct OutTraits<kOutGated> : OutTraits<kOutBF16> {};
 template <>
 struct OutTraits<kOutF16> {
   static constexpr int kBytes = 2;
@@ -505,6 +515,26 @@ __device__ __forceinline__ void epilogue_tile_staged(const Args& args, const CUt
   if (nchunks == 0) tmem_ld_wait_regs(r);
 }
 
+__device__ __align__(16) uint8_t g_zero16[16];
+__device__ __forceinline__ const void* rbuf_src_dummy() { return g_zero16; }
+
+// Copies one lane's residual row for the 64 columns [col0, col0 + 64) of a tile into its
+// 128-byte slot of the warp's residual buffer (16-byte piece q at q ^ (lane & 7), the
+// staging buffers' swizzle), asynchronously; pieces at or past `ncols` (the columns the tile
+// has left; N is a multiple of 8) and rows past M (res_row null) become zeros.  The copy
+// reads global memory before this lane's own store of the same chunk: out may be res.
+__device__ __forceinline__ void copy_res_chunk(uint8_t* rbuf, const uint16_t* res_row, int col0, int ncols,
+                                               int lane) {
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    const int col = col0 + 8 * q;
+    const bool in = res_row != nullptr && col < ncols;
+    cp_async_16(rbuf + lane * 128 + ((q ^ (lane & 7)) * 16), in ? static_cast<const void*>(res_row + col) : rbuf_src_dummy(),
+                in ? 16u : 0u);
+  }
+  cp_async_commit();
+}
+
 // Epilogue of one 32-row slice for 2-byte outputs, 64 columns per chunk: two 32-column
 // TMEM loads per chunk (the next chunk's loads overlap this chunk's math), packed
 // products, the bias added from its 16-bit pair, and a 32 x 64 TMA store of full
@@ -513,11 +543,25 @@ template <int IN, int OUT, int EPB>
 __device__ __forceinline__ void epilogue_tile_staged64(const Args& args, const CUtensorMap* tm_out,
                                                        uint8_t (*bufs)[EPB], int& ebuf, uint32_t t_row, int row0,
                                                        int n_tile0, int lane, uint64_t pol_out, float xs_r,
-                                                       const TileParams& tp) {
+                                                       const TileParams& tp, uint8_t* rbuf) {
   static_assert(EPB >= 32 * 128, "staging buffer holds 32 rows of 128 bytes");
   const int nchunks = min(BN / 64, (args.N - n_tile0 + 63) / 64);
   const bool has_bias = args.bias != nullptr;
   const float2 xs2 = make_float2(xs_r, xs_r);
+  // gated residual (kOutGated): this lane's row of res, 64 columns per chunk, copied into
+  // the warp's residual buffer one chunk ahead; its gate row read through L1
+  [[maybe_unused]] const uint16_t* res_row = nullptr;
+  [[maybe_unused]] const uint16_t* gate_row = nullptr;
+  [[maybe_unused]] const int tile_cols = min(BN, args.N - n_tile0);
+  if constexpr (OUT == kOutGated) {
+    const int m = row0 + lane;
+    if (m < args.M) {
+      res_row = static_cast<const uint16_t*>(args.res) + static_cast<int64_t>(m) * args.ld_res + n_tile0;
+      const int64_t grow = args.gate_index ? static_cast<int64_t>(__ldg(args.gate_index + m)) : m / args.rows_per_gate;
+      gate_row = static_cast<const uint16_t*>(args.gate) + grow * args.ld_gate + n_tile0;
+    }
+    copy_res_chunk(rbuf, res_row, 0, tile_cols, lane);
+  }
   uint32_t r0[32], r1[32];
   tmem_ld_32x32b_x32(t_row, r0);
   tmem_ld_32x32b_x32(t_row + 32u, r1);
@@ -534,6 +578,7 @@ __device__ __forceinline__ void epilogue_tile_staged64(const Args& args, const C
       tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>((c + 1) * 64), r0);
       tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>((c + 1) * 64 + 32), r1);
     }
+    if constexpr (OUT == kOutGated) cp_async_wait_all();
     const float4* wq = reinterpret_cast<const float4*>(tp.ws + c * 64);
     const uint4* bq2 = reinterpret_cast<const uint4*>(tp.bias2 + c * 32);
     uint32_t packed[32];
@@ -551,6 +596,24 @@ __device__ __forceinline__ void epilogue_tile_staged64(const Args& args, const C
         if (has_bias) f = (OUT == kOutF16) ? add_f32_f16x2(f, bw[p]) : add_f32_bf16x2(f, bw[p]);
         packed[4 * q + p] = OutTraits<OUT>::pack2(f.x, f.y);
       }
+      if constexpr (OUT == kOutGated) {
+        // torch's bf16 order: t = bf16(gate * y), then bf16(res + t), both computed in f32
+        const int col = c * 64 + 8 * q;
+        const uint4 r4 = *reinterpret_cast<const uint4*>(rbuf + lane * 128 + ((q ^ (lane & 7)) * 16));
+        const uint4 g4 = (gate_row != nullptr && col < tile_cols) ? __ldg(reinterpret_cast<const uint4*>(gate_row + col))
+                                                                  : make_uint4(0, 0, 0, 0);
+        const uint32_t rw[4] = {r4.x, r4.y, r4.z, r4.w};
+        const uint32_t gw[4] = {g4.x, g4.y, g4.z, g4.w};
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+          const float2 t = bf2_to_f2(f2_to_bf2(mul2_rn(bf2_to_f2(gw[p]), bf2_to_f2(packed[4 * q + p]))));
+          packed[4 * q + p] = f2_to_bf2(add2_rn(bf2_to_f2(rw[p]), t));
+        }
+      }
+    }
+    // this lane has read its residual slot: copy the next chunk's residual into it
+    if constexpr (OUT == kOutGated) {
+      if (c + 1 < nchunks) copy_res_chunk(rbuf, res_row, (c + 1) * 64, tile_cols, lane);
     }
     // the staging buffer used two chunks ago must have been read by its TMA store
     if (lane == 0) bulk_wait_group_read<1>();
@@ -667,13 +730,16 @@ struct PairCfg {
   static constexpr int kEpiCols = (OutTraits<OUT>::kBytes == 2 && OUT != kOutSwiglu) ? 64 : EPI_COLS;
   static constexpr int kEpiBytes = 32 * kEpiCols * OutTraits<OUT>::kBytes;
   static constexpr int kStages = 5;
+  // kOutGated: a 32-row x 128-byte residual buffer per epilogue warp
+  static constexpr int kResBytes = OUT == kOutGated ? 32 * 128 : 16;
 };
 
-template <int STAGES, int EPB>
+template <int STAGES, int EPB, int RESB>
 struct SmemPair {
   uint8_t a[STAGES][P_A_BYTES];
   uint8_t b[STAGES][P_B_BYTES];
   uint8_t epi[EPI_WARPS][2][EPB];
+  uint8_t res[EPI_WARPS][RESB];   // kOutGated: each lane's residual row chunk
   TileParams params[2];   // channel parameters of the tile in each accumulator
   uint64_t full[STAGES];
   uint64_t empty[STAGES];
@@ -683,10 +749,11 @@ struct SmemPair {
   uint32_t tmem_base;
 };
 template <int OUT>
-using SmemPairOf = SmemPair<PairCfg<OUT>::kStages, PairCfg<OUT>::kEpiBytes>;
+using SmemPairOf = SmemPair<PairCfg<OUT>::kStages, PairCfg<OUT>::kEpiBytes, PairCfg<OUT>::kResBytes>;
 template <int OUT>
 constexpr size_t pair_smem_bytes() { return sizeof(SmemPairOf<OUT>) + 1024; }   // + slack to align to 1024 B
-static_assert(pair_smem_bytes<kOutBF16>() <= 227 * 1024 && pair_smem_bytes<kOutF32>() <= 227 * 1024,
+static_assert(pair_smem_bytes<kOutBF16>() <= 227 * 1024 && pair_smem_bytes<kOutF32>() <= 227 * 1024 &&
+                  pair_smem_bytes<kOutGated>() <= 227 * 1024,
               "pair kernel shared memory exceeds the per-CTA limit");
 
 template <int IN, int OUT>
@@ -860,7 +927,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
                                                    xs_r, s.params[acc]);
         else if constexpr (Cfg::kEpiCols == 64)
           epilogue_tile_staged64<IN, OUT, Cfg::kEpiBytes>(args, &tm_out, s.epi[ew], ebuf, t_row, row0, tn * BN, lane,
-                                                          pol_out, xs_r, s.params[acc]);
+                                                          pol_out, xs_r, s.params[acc], s.res[ew]);
         else
           epilogue_tile_staged<IN, OUT, Cfg::kEpiBytes>(args, &tm_out, s.epi[ew], ebuf, t_row, row0, tn * BN, lane,
                                                         pol_out, xs_r, s.params[acc]);

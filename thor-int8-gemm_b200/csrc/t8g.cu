@@ -201,7 +201,7 @@ int gemm_entry(int in_kind, const void* x, const void* w, const float* x_scale, 
                  esz == 2 && !box64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
 
-  Args args;
+  Args args = {};
   args.xs = x_scale;
   args.ws = w_scale;
   args.bias = bias_numel ? bias : nullptr;
@@ -276,7 +276,7 @@ int gemm_swiglu_entry(int in_kind, const void* x, const void* w, const float* x_
   if (rc) return rc;
   rc = encode_2d(&to, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, act, F, M, ld_act * 2, EPI_COLS, 32, CU_TENSOR_MAP_SWIZZLE_64B);
   if (rc) return rc;
-  Args args;
+  Args args = {};
   args.xs = x_scale;
   args.ws = w_scale;
   args.bias = bias_numel ? bias : nullptr;
@@ -288,6 +288,78 @@ int gemm_swiglu_entry(int in_kind, const void* x, const void* w, const float* x_
   cudaStream_t st = static_cast<cudaStream_t>(stream_);
   if (in_kind == kInI8) return launch_gemm_pair<kInI8, kOutSwiglu>(ta, tb, to, args, dev, info.sms, st);
   return launch_gemm_pair<kInE4M3, kOutSwiglu>(ta, tb, to, args, dev, info.sms, st);
+}
+
+// GEMM whose epilogue applies the DiT block's gated residual: out = bf16(res + bf16(gate[g] *
+// y)) with y the bf16 dequantised GEMM output and g = gate_index[m] (or m / rows_per_gate).
+// bf16 output only; out may be res itself (each element is read before it is stored).
+// Always the 2-SM kernel.
+int gemm_gated_entry(int in_kind, const void* x, const void* w, const float* x_scale, const float* w_scale,
+                     int64_t w_scale_numel, const void* bias, int64_t bias_numel, const void* res, int64_t ld_res,
+                     const void* gate, int64_t ld_gate, const int32_t* gate_index, int64_t rows_per_gate, void* out,
+                     int64_t M, int64_t N, int64_t K, int64_t ld_x, int64_t ld_w, int64_t ld_out, void* stream_) {
+  using namespace t8g::gemm;
+  g_last_error[0] = '\0';
+  if (M < 0 || N < 0 || K < 1) return fail(T8G_ERR_INVALID_ARGUMENT, "bad sizes M=%lld N=%lld K=%lld", (long long)M, (long long)N, (long long)K);
+  if (M >= (int64_t(1) << 31) || N >= (int64_t(1) << 31) || K >= (int64_t(1) << 31))
+    return fail(T8G_ERR_UNSUPPORTED, "M, N and K must each be below 2^31");
+  if (N % 8) return fail(T8G_ERR_INVALID_ARGUMENT, "N=%lld must be a multiple of 8", (long long)N);
+  if (M == 0 || N == 0) return T8G_OK;
+  if (!x || !w || !x_scale || !w_scale || !out || !res || !gate)
+    return fail(T8G_ERR_INVALID_ARGUMENT, "null operand pointer");
+  if (!gate_index && rows_per_gate < 1)
+    return fail(T8G_ERR_INVALID_ARGUMENT, "rows_per_gate must be positive when gate_index is null");
+  if (w_scale_numel != 1 && w_scale_numel != N)
+    return fail(T8G_ERR_INVALID_ARGUMENT, "w_scale numel %lld is neither 1 nor N=%lld", (long long)w_scale_numel, (long long)N);
+  if (bias_numel != 0 && bias_numel != N)
+    return fail(T8G_ERR_INVALID_ARGUMENT, "bias numel %lld is neither 0 nor N=%lld", (long long)bias_numel, (long long)N);
+  if (bias_numel == N && !bias) return fail(T8G_ERR_INVALID_ARGUMENT, "bias numel is N but bias is null");
+  if (ld_x < K || ld_w < K || ld_out < N || ld_res < N || ld_gate < N)
+    return fail(T8G_ERR_INVALID_ARGUMENT, "row stride smaller than the row");
+  if (ld_x % 16 || ld_w % 16 || ld_out % 8 || ld_res % 8 || ld_gate % 8)
+    return fail(T8G_ERR_INVALID_ARGUMENT, "row strides must be multiples of 16 bytes");
+  if (!aligned(x, 16) || !aligned(w, 16) || !aligned(out, 16) || !aligned(res, 16) || !aligned(gate, 16))
+    return fail(T8G_ERR_INVALID_ARGUMENT, "x, w, out, res and gate must be 16-byte aligned");
+  if (!aligned(x_scale, 4) || !aligned(w_scale, 4) || !aligned(gate_index, 4))
+    return fail(T8G_ERR_INVALID_ARGUMENT, "scales and gate_index must be 4-byte aligned");
+  if (out != res) {
+    // out and res are either the same matrix or disjoint
+    const uintptr_t o0 = reinterpret_cast<uintptr_t>(out), r0 = reinterpret_cast<uintptr_t>(res);
+    const uintptr_t o1 = o0 + static_cast<uintptr_t>(((M - 1) * ld_out + N) * 2);
+    const uintptr_t r1 = r0 + static_cast<uintptr_t>(((M - 1) * ld_res + N) * 2);
+    if (o0 < r1 && r0 < o1) return fail(T8G_ERR_INVALID_ARGUMENT, "out overlaps res without being res");
+  } else if (ld_out != ld_res) {
+    return fail(T8G_ERR_INVALID_ARGUMENT, "out is res but ld_out != ld_res");
+  }
+  int dev;
+  DeviceInfo info;
+  int rc = current_device(&dev, &info);
+  if (rc) return rc;
+  CUtensorMap ta, tb, to;
+  rc = encode_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, x, K, M, ld_x, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  rc = encode_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, K, N, ld_w, BK, P_ROWS, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  rc = encode_2d(&to, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, out, N, M, ld_out * 2, 64, 32, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  Args args = {};
+  args.xs = x_scale;
+  args.ws = w_scale;
+  args.bias = bias_numel ? bias : nullptr;
+  args.ws_stride = w_scale_numel == 1 ? 0 : 1;
+  args.vec_ok = aligned(w_scale, 16) && (bias_numel == 0 || aligned(bias, 16));
+  args.M = static_cast<int>(M);
+  args.N = static_cast<int>(N);
+  args.K = static_cast<int>(K);
+  args.res = res;
+  args.gate = gate;
+  args.gate_index = gate_index;
+  args.ld_res = ld_res;
+  args.ld_gate = ld_gate;
+  args.rows_per_gate = gate_index ? 1 : rows_per_gate;
+  cudaStream_t st = static_cast<cudaStream_t>(stream_);
+  if (in_kind == kInI8) return launch_gemm_pair<kInI8, kOutGated>(ta, tb, to, args, dev, info.sms, st);
+  return launch_gemm_pair<kInE4M3, kOutGated>(ta, tb, to, args, dev, info.sms, st);
 }
 
 // ----------------------------------------------------------------- row kernels
@@ -747,6 +819,22 @@ int t8g_gemm_fp8_swiglu(const void* x, const void* w, const float* x_scale, cons
                         int64_t K, int64_t ld_x, int64_t ld_w, int64_t ld_act, void* stream) {
   return gemm_swiglu_entry(t8g::gemm::kInE4M3, x, w, x_scale, w_scale, w_scale_numel, bias, bias_numel, act, M, F,
                            K, ld_x, ld_w, ld_act, stream);
+}
+
+int t8g_gemm_i8_gated(const void* x, const void* w, const float* x_scale, const float* w_scale,
+                      int64_t w_scale_numel, const void* bias, int64_t bias_numel, const void* res, int64_t ld_res,
+                      const void* gate, int64_t ld_gate, const int32_t* gate_index, int64_t rows_per_gate, void* out,
+                      int64_t M, int64_t N, int64_t K, int64_t ld_x, int64_t ld_w, int64_t ld_out, void* stream) {
+  return gemm_gated_entry(t8g::gemm::kInI8, x, w, x_scale, w_scale, w_scale_numel, bias, bias_numel, res, ld_res, gate,
+                          ld_gate, gate_index, rows_per_gate, out, M, N, K, ld_x, ld_w, ld_out, stream);
+}
+
+int t8g_gemm_fp8_gated(const void* x, const void* w, const float* x_scale, const float* w_scale,
+                       int64_t w_scale_numel, const void* bias, int64_t bias_numel, const void* res, int64_t ld_res,
+                       const void* gate, int64_t ld_gate, const int32_t* gate_index, int64_t rows_per_gate, void* out,
+                       int64_t M, int64_t N, int64_t K, int64_t ld_x, int64_t ld_w, int64_t ld_out, void* stream) {
+  return gemm_gated_entry(t8g::gemm::kInE4M3, x, w, x_scale, w_scale, w_scale_numel, bias, bias_numel, res, ld_res,
+                          gate, ld_gate, gate_index, rows_per_gate, out, M, N, K, ld_x, ld_w, ld_out, stream);
 }
 
 int t8g_quant_rows(const void* x, int64_t ld_x, void* q, int64_t ld_q, float* q_scale, int64_t S, int64_t D,

@@ -7,7 +7,8 @@ reference's fused block (src/ck_fused_patch.py:152-172) with per-token quantisat
 
     h1  = rms_norm(x) * (1 + scale_msa) + shift_msa     -> int8/fp8 + per-token scale
     qkv = h1 @ Wqkv^T (fused dequant GEMM)               -> SDPA (torch, outside the hot path)
-    o   = quant(attn) @ Wproj^T;  x += gate_msa * o       (gated residual: stock torch)
+    o   = quant(attn) @ Wproj^T;  x += gate_msa * o       (gated residual: stock torch, or
+                                                          the GEMM's epilogue, fused_gate)
     h2  = rms_norm(x) * (1 + scale_mlp) + shift_mlp     -> int8/fp8 + per-token scale
     y   = h2 @ Wfc1^T  [M, 2F];  a = quant(silu(y[:, :F]) * y[:, F:]) (read in place)
     z   = a @ Wfc2^T;  x += gate_mlp * z
@@ -43,7 +44,8 @@ class DiTBlock:
     """Synthetic DiT block (see module docstring)."""
 
     def __init__(self, hidden: int = 3072, heads: int = 24, ffn: int = 12288, kind: str = "int8",
-                 device=None, seed: int = 0, eps: float = 1e-6, fused_mlp: bool = False):
+                 device=None, seed: int = 0, eps: float = 1e-6, fused_mlp: bool = False,
+                 fused_gate: bool = False):
         if hidden % heads:
             raise ValueError("hidden must be a multiple of heads")
         self.hidden, self.heads, self.ffn, self.kind, self.eps = hidden, heads, ffn, kind, eps
@@ -63,6 +65,8 @@ class DiTBlock:
         self.fc2 = QuantLinear(w(hidden, ffn), b(hidden), kind)
         # fused_mlp: fc1 with the SwiGLU in its epilogue (gate / up rows interleaved once)
         self.fused_mlp = fused_mlp
+        # fused_gate: proj and fc2 apply the gated residual in their epilogue (gemm_gated)
+        self.fused_gate = fused_gate
         if fused_mlp:
             il = ops.interleave_gate_up
             self.fc1_il = (il(self.fc1.w), il(self.fc1.ws), il(self.fc1.bias))
@@ -96,7 +100,11 @@ class DiTBlock:
         qkv = self.qkv(q1, s1)
         attn = (attn_fn or self.attention)(qkv, batch)
         aq, as_ = ops.quant_rows(attn.contiguous(), self.kind)
-        x = self.gated(x, gate_msa, self.proj(aq, as_), batch)
+        if self.fused_gate:
+            p = self.proj
+            x = ops.gemm_gated(aq, p.w, as_, p.ws, p.bias, x, gate_msa, rows_per_gate=T)
+        else:
+            x = self.gated(x, gate_msa, self.proj(aq, as_), batch)
         q2, s2 = self.norm_quant(x, shift_mlp, scale_mlp, T)
         if self.fused_mlp:
             w_il, ws_il, b_il = self.fc1_il
@@ -104,6 +112,10 @@ class DiTBlock:
         else:
             y = self.fc1(q2, s2)
             q3, s3 = ops.swiglu_quant_fc1(y, kind=self.kind)
+        if self.fused_gate:
+            f = self.fc2
+            # x is this block's own tensor here: update it in place
+            return ops.gemm_gated(q3, f.w, s3, f.ws, f.bias, x, gate_mlp, rows_per_gate=T, out=x)
         return self.gated(x, gate_mlp, self.fc2(q3, s3), batch)
 
     def __call__(self, x: torch.Tensor, cond: torch.Tensor, batch: int) -> torch.Tensor:

@@ -143,6 +143,69 @@ def gemm_swiglu(x: torch.Tensor, w_il: torch.Tensor, x_scale: torch.Tensor, w_sc
     return out
 
 
+def gemm_gated(x: torch.Tensor, w: torch.Tensor, x_scale: torch.Tensor, w_scale: torch.Tensor,
+               bias: torch.Tensor | None, res: torch.Tensor, gate: torch.Tensor, *,
+               rows_per_gate: int | None = None, gate_index: torch.Tensor | None = None,
+               out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    """The DiT block's gated residual with the projection GEMM fused in front of it:
+    out = res + gate[g] * y in torch's bf16 order (t = bf16(gate * y), out = bf16(res + t)),
+    y = gemm_dequant(x, w, x_scale, w_scale, bias) as bf16, never stored.  g is
+    gate_index[m] (int32 [M]) or m // rows_per_gate (default: M // gate rows, which must
+    divide M).  res [M, N] bf16; gate [n_gate, N] bf16; out [M, N] bf16, may be res itself
+    (in-place update)."""
+    _need_cuda("x", x, (torch.int8, torch.float8_e4m3fn), 2)
+    _need_cuda("w", w, x.dtype, 2)
+    M, K = x.shape
+    N = w.shape[0]
+    if w.shape[1] != K:
+        raise ValueError(f"w has K={w.shape[1]}, x has K={K}")
+    _need_cuda("x_scale", x_scale, torch.float32)
+    _need_cuda("w_scale", w_scale, torch.float32)
+    if x_scale.numel() != M or not x_scale.is_contiguous():
+        raise ValueError("x_scale must be a contiguous float32 tensor with M elements")
+    if w_scale.numel() not in (1, N) or not w_scale.is_contiguous():
+        raise ValueError("w_scale must be a contiguous float32 tensor with 1 or N elements")
+    _need_cuda("res", res, torch.bfloat16, 2)
+    if tuple(res.shape) != (M, N):
+        raise ValueError(f"res has shape {tuple(res.shape)}, expected {(M, N)}")
+    if gate.dim() == 1:
+        gate = gate.view(1, -1)
+    _need_cuda("gate", gate, torch.bfloat16, 2)
+    if gate.shape[1] != N or gate.shape[0] < 1:
+        raise ValueError(f"gate must be [n_gate, {N}], got {tuple(gate.shape)}")
+    if gate_index is not None:
+        _need_cuda("gate_index", gate_index, torch.int32, 1)
+        if gate_index.numel() != M or not gate_index.is_contiguous():
+            raise ValueError("gate_index must be a contiguous int32 tensor with M elements")
+        rpg = 0
+    else:
+        if rows_per_gate is None:
+            if M % gate.shape[0]:
+                raise ValueError(f"{M} rows do not split evenly over {gate.shape[0]} gate rows; pass gate_index")
+            rows_per_gate = max(1, M // gate.shape[0])
+        rpg = int(rows_per_gate)
+        if rpg < 1 or (M and (M - 1) // rpg >= gate.shape[0]):
+            raise ValueError(f"rows_per_gate={rpg} maps rows past the {gate.shape[0]} gate rows")
+    if out is None:
+        out = torch.empty(M, N, dtype=torch.bfloat16, device=x.device)
+    _need_cuda("out", out, torch.bfloat16, 2)
+    if tuple(out.shape) != (M, N):
+        raise ValueError(f"out has shape {tuple(out.shape)}, expected {(M, N)}")
+    nb = 0 if bias is None else bias.numel()
+    if nb:
+        _need_cuda("bias", bias, torch.bfloat16)
+        if nb != N or not bias.is_contiguous():
+            raise ValueError("bias must be contiguous bf16 with N elements")
+    lib = _lib.load()
+    fn = lib.t8g_gemm_i8_gated if x.dtype == torch.int8 else lib.t8g_gemm_fp8_gated
+    with torch.cuda.device(x.device):
+        rc = fn(_ptr(x), _ptr(w), _ptr(x_scale), _ptr(w_scale), w_scale.numel(), _ptr(bias) if nb else None, nb,
+                _ptr(res), res.stride(0), _ptr(gate), gate.stride(0), _ptr(gate_index), rpg, _ptr(out),
+                M, N, K, x.stride(0), w.stride(0), out.stride(0), _stream_handle(x.device, stream))
+    _lib.check(rc)
+    return out
+
+
 def quant_rows(x: torch.Tensor, kind: str = "int8", q: torch.Tensor | None = None,
                q_scale: torch.Tensor | None = None, stream=None):
     """Per-token quantisation of a bf16 [S, D] matrix -> (q [S, D], q_scale [S] float32)."""
