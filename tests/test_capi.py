@@ -22,7 +22,8 @@ def test_header_declares_the_expected_entry_points():
     names = declared_symbols()
     for n in ("t8g_gemm_i8_dequant", "t8g_gemm_fp8_dequant", "t8g_quant_rows", "t8g_rms_mod_quant",
               "t8g_rms_mod_quant_tensorwise", "t8g_swiglu_quant", "t8g_swiglu_quant_tensorwise",
-              "t8g_device_status", "t8g_last_error", "t8g_version", "t8g_wait_selftest"):
+              "t8g_device_status", "t8g_last_error", "t8g_version", "t8g_wait_selftest", "t8g_gemm_i8_swiglu",
+              "t8g_gemm_fp8_swiglu", "t8g_gemm_i8_gated", "t8g_gemm_fp8_gated"):
         assert n in names
 
 

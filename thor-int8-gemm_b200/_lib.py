@@ -68,6 +68,8 @@ _lib = None
 def load(path: str | None = None) -> ctypes.CDLL:
     """Load the shared library once and attach the signatures."""
     global _lib
+    if _lib is not None and path is None:
+        return _lib
     with _lock:
         if _lib is not None:
             return _lib

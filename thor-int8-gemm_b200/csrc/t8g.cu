@@ -96,9 +96,8 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// 2-D row-major tensor [outer, inner] with row pitch `ld_bytes`, box [box_outer, box_inner].
-int encode_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t outer,
-              uint64_t ld_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle sw) {
+int encode_2d_uncached(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t outer,
+                       uint64_t ld_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle sw) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return fail(T8G_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
   cuuint64_t dims[2] = {inner, outer};
@@ -108,6 +107,47 @@ int encode_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t
   CUresult r = fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(T8G_ERR_CUDA, "cuTensorMapEncodeTiled failed (CUresult %d)", static_cast<int>(r));
+  return T8G_OK;
+}
+
+// Recently encoded tensor maps of this thread: a layer calls the GEMM with the same weight,
+// and often the same activation and output buffers, every step, so most maps repeat.
+struct MapKey {
+  const void* base;
+  uint64_t inner, outer, ld_bytes;
+  uint32_t box_inner, box_outer;
+  int dt, sw;
+  bool operator==(const MapKey& o) const {
+    return base == o.base && inner == o.inner && outer == o.outer && ld_bytes == o.ld_bytes &&
+           box_inner == o.box_inner && box_outer == o.box_outer && dt == o.dt && sw == o.sw;
+  }
+};
+struct MapCache {
+  static constexpr int kEntries = 16;
+  MapKey key[kEntries] = {};
+  CUtensorMap map[kEntries];
+  bool used[kEntries] = {};
+  int next = 0;
+};
+
+// 2-D row-major tensor [outer, inner] with row pitch `ld_bytes`, box [box_outer, box_inner].
+int encode_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t outer,
+              uint64_t ld_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle sw) {
+  static thread_local MapCache cache;
+  const MapKey key = {base, inner, outer, ld_bytes, box_inner, box_outer, static_cast<int>(dt), static_cast<int>(sw)};
+  for (int i = 0; i < MapCache::kEntries; ++i) {
+    if (cache.used[i] && cache.key[i] == key) {
+      *m = cache.map[i];
+      return T8G_OK;
+    }
+  }
+  int rc = encode_2d_uncached(m, dt, base, inner, outer, ld_bytes, box_inner, box_outer, sw);
+  if (rc) return rc;
+  const int slot = cache.next;
+  cache.next = (slot + 1) % MapCache::kEntries;
+  cache.key[slot] = key;
+  cache.map[slot] = *m;
+  cache.used[slot] = true;
   return T8G_OK;
 }
 

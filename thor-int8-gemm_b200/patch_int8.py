@@ -53,8 +53,7 @@ def _kitchen_version():
 def _b200_gemm(x8, w8, x_scale, w_scale, bias, out, stream=None):
     """The replacement kernel: this library's int8 fused-dequant GEMM on `stream`."""
     from . import ops
-    return ops.gemm_dequant(x8, w8, x_scale.reshape(-1), w_scale.reshape(-1),
-                            bias if bias.numel() else None, out=out, stream=stream)
+    return ops.gemm_dequant(x8, w8, x_scale, w_scale, bias, out=out, stream=stream)
 
 
 def _stream_arg(stream):
