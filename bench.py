@@ -66,7 +66,8 @@ def parse_args():
     ap.add_argument("--scaling", choices=("weak", "strong"), default="weak",
                     help="weak: every rank runs the full sweep on its own tokens; strong: the sweep's "
                          "tokens are split across the ranks")
-    ap.add_argument("--profile", choices=("gemm_i8", "gemm_fp8", "rms_fp8", "rms_int8", "swiglu_int8", "quant_int8"),
+    ap.add_argument("--profile", choices=("gemm_i8", "gemm_fp8", "gemm_gated", "rms_fp8", "rms_int8", "swiglu_int8",
+                                          "quant_int8"),
                     help="run one kernel a few times on a mid-size case (for ncu captures) and exit")
     ap.add_argument("--M", type=int, default=32768)
     ap.add_argument("--N", type=int, default=9216)
@@ -76,7 +77,8 @@ def parse_args():
 def run_profile_case(args):
     """One kernel, `warmup + steps` launches, on a case whose inputs exceed L2 but stay
     within a few GB: GEMM M x N x 3072; norm/quant and per-token quant [2*56320, 3072];
-    SwiGLU [32768, 2*12288]."""
+    SwiGLU [32768, 2*12288]; gemm_gated: the GEMM with the gated residual updating a bf16
+    [M, N] residual in place (two gate rows)."""
     import torch
     from __graft_entry__ import load_package
     load_package()
@@ -86,7 +88,15 @@ def run_profile_case(args):
     gen = torch.Generator(device=dev)
     gen.manual_seed(5)
     n = args.warmup + args.steps
-    if args.profile.startswith("gemm"):
+    if args.profile == "gemm_gated":
+        x, xs = ops.quant_rows(torch.randn(args.M, K_DIM, generator=gen, device=dev).to(torch.bfloat16), "int8")
+        w, ws = ops.quant_rows((torch.randn(args.N, K_DIM, generator=gen, device=dev) * 0.02).to(torch.bfloat16), "int8")
+        bias = (torch.randn(args.N, generator=gen, device=dev) * 0.01).to(torch.bfloat16)
+        res = torch.randn(args.M, args.N, generator=gen, device=dev).to(torch.bfloat16)
+        gate = (torch.randn(2, args.N, generator=gen, device=dev) * 0.1).to(torch.bfloat16)
+        for _ in range(n):
+            ops.gemm_gated(x, w, xs, ws, bias, res, gate, rows_per_gate=(args.M + 1) // 2, out=res)
+    elif args.profile.startswith("gemm"):
         kind = "int8" if args.profile == "gemm_i8" else "fp8_e4m3"
         x, xs = ops.quant_rows(torch.randn(args.M, K_DIM, generator=gen, device=dev).to(torch.bfloat16), kind)
         w, ws = ops.quant_rows((torch.randn(args.N, K_DIM, generator=gen, device=dev) * 0.02).to(torch.bfloat16), kind)

@@ -37,6 +37,17 @@ __device__ __forceinline__ float2 add_f32_bf16x2(float2 p, uint32_t b) {
       : "r"(b), "f"(p.x), "f"(p.y));
   return make_float2(x, y);
 }
+// (lo(a) * lo(b), hi(a) * hi(b)) for two packed bf16 pairs: the product of two bf16 values
+// is exact in fp32, formed as fma(a, b, -0) with the 16-bit operands taken directly
+// (adding -0 keeps every product, signed zeros included, as the IEEE multiply gives it).
+__device__ __forceinline__ float2 mul_bf16x2_exact(uint32_t a, uint32_t b) {
+  float x, y;
+  asm("{ .reg .b16 alo, ahi, blo, bhi; mov.b32 {alo, ahi}, %2; mov.b32 {blo, bhi}, %3;"
+      " fma.rn.f32.bf16 %0, alo, blo, 0f80000000; fma.rn.f32.bf16 %1, ahi, bhi, 0f80000000; }"
+      : "=f"(x), "=f"(y)
+      : "r"(a), "r"(b));
+  return make_float2(x, y);
+}
 __device__ __forceinline__ float2 add_f32_f16x2(float2 p, uint32_t b) {
   float x, y;
   asm("{ .reg .b16 lo, hi; mov.b32 {lo, hi}, %2; add.rn.f32.f16 %0, lo, %3; add.rn.f32.f16 %1, hi, %4; }"

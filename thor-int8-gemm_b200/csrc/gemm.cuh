@@ -518,21 +518,172 @@ __device__ __forceinline__ void epilogue_tile_staged(const Args& args, const CUt
 __device__ __align__(16) uint8_t g_zero16[16];
 __device__ __forceinline__ const void* rbuf_src_dummy() { return g_zero16; }
 
-// Copies one lane's residual row for the 64 columns [col0, col0 + 64) of a tile into its
-// 128-byte slot of the warp's residual buffer (16-byte piece q at q ^ (lane & 7), the
-// staging buffers' swizzle), asynchronously; pieces at or past `ncols` (the columns the tile
-// has left; N is a multiple of 8) and rows past M (res_row null) become zeros.  The copy
-// reads global memory before this lane's own store of the same chunk: out may be res.
-__device__ __forceinline__ void copy_res_chunk(uint8_t* rbuf, const uint16_t* res_row, int col0, int ncols,
-                                               int lane) {
+// acc -> float for 64 columns: int32 converted (RN), fp32 taken as is
+template <int IN>
+__device__ __forceinline__ void acc_to_f32_64(const uint32_t (&r0)[32], const uint32_t (&r1)[32], float (&v)[64]) {
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    v[j] = (IN == kInI8) ? __int2float_rn(static_cast<int>(r0[j])) : __uint_as_float(r0[j]);
+    v[32 + j] = (IN == kInI8) ? __int2float_rn(static_cast<int>(r1[j])) : __uint_as_float(r1[j]);
+  }
+}
+
+// Dequantise 64 columns (chunk c of the tile) of one row and pack them to the 2-byte output
+// type: ((acc * xs) * ws) + bias in f32, the bias added from its 16-bit pair.
+template <int OUT>
+__device__ __forceinline__ void dequant_pack64(const TileParams& tp, int c, const float (&v)[64], float2 xs2,
+                                               bool has_bias, uint32_t (&packed)[32]) {
+  const float4* wq = reinterpret_cast<const float4*>(tp.ws + c * 64);
+  const uint4* bq2 = reinterpret_cast<const uint4*>(tp.bias2 + c * 32);
 #pragma unroll
   for (int q = 0; q < 8; ++q) {
-    const int col = col0 + 8 * q;
-    const bool in = res_row != nullptr && col < ncols;
-    cp_async_16(rbuf + lane * 128 + ((q ^ (lane & 7)) * 16), in ? static_cast<const void*>(res_row + col) : rbuf_src_dummy(),
-                in ? 16u : 0u);
+    const float4 w0 = wq[2 * q], w1 = wq[2 * q + 1];
+    const float2 wp[4] = {make_float2(w0.x, w0.y), make_float2(w0.z, w0.w), make_float2(w1.x, w1.y),
+                          make_float2(w1.z, w1.w)};
+    const uint4 b4 = has_bias ? bq2[q] : make_uint4(0, 0, 0, 0);
+    const uint32_t bw[4] = {b4.x, b4.y, b4.z, b4.w};
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      const int j = 8 * q + 2 * p;
+      float2 f = mul2_rn(mul2_rn(make_float2(v[j], v[j + 1]), xs2), wp[p]);
+      if (has_bias) f = (OUT == kOutF16) ? add_f32_f16x2(f, bw[p]) : add_f32_bf16x2(f, bw[p]);
+      packed[4 * q + p] = OutTraits<OUT>::pack2(f.x, f.y);
+    }
+  }
+}
+
+// Stage one row's 64 packed 2-byte values in the warp's staging buffer (32 rows x 128 B,
+// 128-byte swizzle: 16-byte piece q of row r at q ^ (r & 7)) and store the 32 x 64 box at
+// (x, y) with TMA; the buffer used two stores ago must have been read first.
+template <int EPB>
+__device__ __forceinline__ void store_chunk64(const CUtensorMap* tm_out, uint8_t (*bufs)[EPB], int& ebuf, int lane,
+                                              const uint32_t (&packed)[32], int x, int y, uint64_t pol_out) {
+  if (lane == 0) bulk_wait_group_read<1>();
+  __syncwarp();
+  uint8_t* buf = bufs[ebuf];
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    const uint4 w = make_uint4(packed[4 * q + 0], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+    *reinterpret_cast<uint4*>(buf + lane * 128 + ((q ^ (lane & 7)) * 16)) = w;
+  }
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    tma_store_2d(tm_out, buf, x, y, pol_out);
+    bulk_commit_group();
+  }
+  ebuf ^= 1;
+}
+
+// ---------------------------------------------------------------- gated residual
+// The residual rows of a warp's 32 x 256 slice of a tile are copied into shared memory
+// (4 chunks of 32 rows x 128 B, the staging layout: 16-byte piece q of row r at q ^ (r & 7))
+// with cp.async when the tile's epilogue begins, before the accumulator is ready, so the
+// copies overlap the tile's MMA; each chunk's output then replaces its residual in place and
+// is stored from there with TMA.  When the 32 rows share one gate row (one batch element),
+// that row's 256 columns are copied next to them and read as broadcasts.
+struct GatedSlice {
+  const uint16_t* gate_row;   // this lane's gate row at the tile's first column (null: row >= M)
+  bool shared_gate;           // every valid row of the warp uses lane 0's gate row
+};
+
+__device__ __forceinline__ GatedSlice gated_prefetch(const Args& args, uint8_t* rbuf, uint8_t* gbuf, int row0,
+                                                     int n_tile0, int lane) {
+  GatedSlice g;
+  const int m = row0 + lane;
+  const int tile_cols = min(BN, args.N - n_tile0);
+  const uint16_t* res_row = nullptr;
+  int64_t grow = -1;
+  if (m < args.M) {
+    res_row = static_cast<const uint16_t*>(args.res) + static_cast<int64_t>(m) * args.ld_res + n_tile0;
+    grow = args.gate_index ? static_cast<int64_t>(__ldg(args.gate_index + m)) : m / args.rows_per_gate;
+  }
+  g.gate_row = m < args.M ? static_cast<const uint16_t*>(args.gate) + grow * args.ld_gate + n_tile0 : nullptr;
+  const int64_t grow0 = __shfl_sync(0xffffffffu, grow, 0);
+  g.shared_gate = __all_sync(0xffffffffu, m >= args.M || grow == grow0);
+  // the previous tile's stores must have read the buffer before it is refilled
+  if (lane == 0) bulk_wait_group_read<0>();
+  __syncwarp();
+#pragma unroll
+  for (int c = 0; c < BN / 64; ++c) {
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const int col = c * 64 + 8 * q;
+      const bool in = res_row != nullptr && col < tile_cols;
+      cp_async_16(rbuf + c * 4096 + lane * 128 + ((q ^ (lane & 7)) * 16),
+                  in ? static_cast<const void*>(res_row + col) : rbuf_src_dummy(), in ? 16u : 0u);
+    }
+  }
+  if (g.shared_gate) {
+    const uint16_t* g0 = static_cast<const uint16_t*>(args.gate) + grow0 * args.ld_gate + n_tile0;
+    const bool in = 8 * lane < tile_cols;
+    cp_async_16(gbuf + lane * 16, in ? static_cast<const void*>(g0 + 8 * lane) : rbuf_src_dummy(), in ? 16u : 0u);
   }
   cp_async_commit();
+  return g;
+}
+
+// Epilogue of one 32-row slice with the gated residual (kOutGated, bf16): for each 64-column
+// chunk, y = the plain epilogue's bf16 value, then out = bf16(res + bf16(gate * y)) in
+// torch's order, written over the chunk's residual and stored from there.
+template <int IN>
+__device__ __forceinline__ void epilogue_tile_gated(const Args& args, const CUtensorMap* tm_out, uint8_t* rbuf,
+                                                    const uint8_t* gbuf, const GatedSlice& gs, uint32_t t_row,
+                                                    int row0, int n_tile0, int lane, uint64_t pol_out, float xs_r,
+                                                    const TileParams& tp) {
+  const int tile_cols = min(BN, args.N - n_tile0);
+  const int nchunks = (tile_cols + 63) / 64;
+  const bool has_bias = args.bias != nullptr;
+  const float2 xs2 = make_float2(xs_r, xs_r);
+  uint32_t r0[32], r1[32];
+  tmem_ld_32x32b_x32(t_row, r0);
+  tmem_ld_32x32b_x32(t_row + 32u, r1);
+  cp_async_wait_all();   // issued when the tile began: long done
+  __syncwarp();          // the shared gate row came from every lane's copy
+  for (int c = 0; c < nchunks; ++c) {
+    tmem_ld_wait_regs(r0);
+    tmem_ld_wait_regs(r1);
+    float v[64];
+    acc_to_f32_64<IN>(r0, r1, v);
+    if (c + 1 < nchunks) {
+      tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>((c + 1) * 64), r0);
+      tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>((c + 1) * 64 + 32), r1);
+    }
+    uint32_t packed[32];
+    dequant_pack64<kOutGated>(tp, c, v, xs2, has_bias, packed);
+    uint8_t* slot = rbuf + c * 4096;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const int col = c * 64 + 8 * q;
+      uint4* cell = reinterpret_cast<uint4*>(slot + lane * 128 + ((q ^ (lane & 7)) * 16));
+      const uint4 r4 = *cell;
+      uint4 g4;
+      if (gs.shared_gate)
+        g4 = *reinterpret_cast<const uint4*>(gbuf + (c * 8 + q) * 16);
+      else
+        g4 = (gs.gate_row != nullptr && col < tile_cols) ? __ldg(reinterpret_cast<const uint4*>(gs.gate_row + col))
+                                                         : make_uint4(0, 0, 0, 0);
+      const uint32_t rw[4] = {r4.x, r4.y, r4.z, r4.w};
+      const uint32_t gw[4] = {g4.x, g4.y, g4.z, g4.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int p = 0; p < 4; ++p) {
+        const uint32_t t = f2_to_bf2(mul_bf16x2_exact(gw[p], packed[4 * q + p]));   // bf16(gate * y)
+        o[p] = f2_to_bf2(add_f32_bf16x2(bf2_to_f2(rw[p]), t));                      // bf16(res + t)
+      }
+      *cell = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_2d(tm_out, slot, n_tile0 + c * 64, row0, pol_out);
+      bulk_commit_group();
+    }
+  }
+  if (nchunks == 0) {
+    tmem_ld_wait_regs(r0);
+    tmem_ld_wait_regs(r1);
+  }
 }
 
 // Epilogue of one 32-row slice for 2-byte outputs, 64 columns per chunk: two 32-column
@@ -543,25 +694,11 @@ template <int IN, int OUT, int EPB>
 __device__ __forceinline__ void epilogue_tile_staged64(const Args& args, const CUtensorMap* tm_out,
                                                        uint8_t (*bufs)[EPB], int& ebuf, uint32_t t_row, int row0,
                                                        int n_tile0, int lane, uint64_t pol_out, float xs_r,
-                                                       const TileParams& tp, uint8_t* rbuf) {
+                                                       const TileParams& tp) {
   static_assert(EPB >= 32 * 128, "staging buffer holds 32 rows of 128 bytes");
   const int nchunks = min(BN / 64, (args.N - n_tile0 + 63) / 64);
   const bool has_bias = args.bias != nullptr;
   const float2 xs2 = make_float2(xs_r, xs_r);
-  // gated residual (kOutGated): this lane's row of res, 64 columns per chunk, copied into
-  // the warp's residual buffer one chunk ahead; its gate row read through L1
-  [[maybe_unused]] const uint16_t* res_row = nullptr;
-  [[maybe_unused]] const uint16_t* gate_row = nullptr;
-  [[maybe_unused]] const int tile_cols = min(BN, args.N - n_tile0);
-  if constexpr (OUT == kOutGated) {
-    const int m = row0 + lane;
-    if (m < args.M) {
-      res_row = static_cast<const uint16_t*>(args.res) + static_cast<int64_t>(m) * args.ld_res + n_tile0;
-      const int64_t grow = args.gate_index ? static_cast<int64_t>(__ldg(args.gate_index + m)) : m / args.rows_per_gate;
-      gate_row = static_cast<const uint16_t*>(args.gate) + grow * args.ld_gate + n_tile0;
-    }
-    copy_res_chunk(rbuf, res_row, 0, tile_cols, lane);
-  }
   uint32_t r0[32], r1[32];
   tmem_ld_32x32b_x32(t_row, r0);
   tmem_ld_32x32b_x32(t_row + 32u, r1);
@@ -569,69 +706,14 @@ __device__ __forceinline__ void epilogue_tile_staged64(const Args& args, const C
     tmem_ld_wait_regs(r0);
     tmem_ld_wait_regs(r1);
     float v[64];
-#pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      v[j] = (IN == kInI8) ? __int2float_rn(static_cast<int>(r0[j])) : __uint_as_float(r0[j]);
-      v[32 + j] = (IN == kInI8) ? __int2float_rn(static_cast<int>(r1[j])) : __uint_as_float(r1[j]);
-    }
+    acc_to_f32_64<IN>(r0, r1, v);
     if (c + 1 < nchunks) {
       tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>((c + 1) * 64), r0);
       tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>((c + 1) * 64 + 32), r1);
     }
-    if constexpr (OUT == kOutGated) cp_async_wait_all();
-    const float4* wq = reinterpret_cast<const float4*>(tp.ws + c * 64);
-    const uint4* bq2 = reinterpret_cast<const uint4*>(tp.bias2 + c * 32);
     uint32_t packed[32];
-#pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      const float4 w0 = wq[2 * q], w1 = wq[2 * q + 1];
-      const float2 wp[4] = {make_float2(w0.x, w0.y), make_float2(w0.z, w0.w), make_float2(w1.x, w1.y),
-                            make_float2(w1.z, w1.w)};
-      const uint4 b4 = has_bias ? bq2[q] : make_uint4(0, 0, 0, 0);
-      const uint32_t bw[4] = {b4.x, b4.y, b4.z, b4.w};
-#pragma unroll
-      for (int p = 0; p < 4; ++p) {
-        const int j = 8 * q + 2 * p;
-        float2 f = mul2_rn(mul2_rn(make_float2(v[j], v[j + 1]), xs2), wp[p]);
-        if (has_bias) f = (OUT == kOutF16) ? add_f32_f16x2(f, bw[p]) : add_f32_bf16x2(f, bw[p]);
-        packed[4 * q + p] = OutTraits<OUT>::pack2(f.x, f.y);
-      }
-      if constexpr (OUT == kOutGated) {
-        // torch's bf16 order: t = bf16(gate * y), then bf16(res + t), both computed in f32
-        const int col = c * 64 + 8 * q;
-        const uint4 r4 = *reinterpret_cast<const uint4*>(rbuf + lane * 128 + ((q ^ (lane & 7)) * 16));
-        const uint4 g4 = (gate_row != nullptr && col < tile_cols) ? __ldg(reinterpret_cast<const uint4*>(gate_row + col))
-                                                                  : make_uint4(0, 0, 0, 0);
-        const uint32_t rw[4] = {r4.x, r4.y, r4.z, r4.w};
-        const uint32_t gw[4] = {g4.x, g4.y, g4.z, g4.w};
-#pragma unroll
-        for (int p = 0; p < 4; ++p) {
-          const float2 t = bf2_to_f2(f2_to_bf2(mul2_rn(bf2_to_f2(gw[p]), bf2_to_f2(packed[4 * q + p]))));
-          packed[4 * q + p] = f2_to_bf2(add2_rn(bf2_to_f2(rw[p]), t));
-        }
-      }
-    }
-    // this lane has read its residual slot: copy the next chunk's residual into it
-    if constexpr (OUT == kOutGated) {
-      if (c + 1 < nchunks) copy_res_chunk(rbuf, res_row, (c + 1) * 64, tile_cols, lane);
-    }
-    // the staging buffer used two chunks ago must have been read by its TMA store
-    if (lane == 0) bulk_wait_group_read<1>();
-    __syncwarp();
-    uint8_t* buf = bufs[ebuf];
-    // 32 rows x 128 B, 128-byte swizzle: 16-byte chunk q of row r lives at chunk q ^ (r & 7)
-#pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      const uint4 w = make_uint4(packed[4 * q + 0], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
-      *reinterpret_cast<uint4*>(buf + lane * 128 + ((q ^ (lane & 7)) * 16)) = w;
-    }
-    fence_proxy_async_smem();
-    __syncwarp();
-    if (lane == 0) {
-      tma_store_2d(tm_out, buf, n_tile0 + c * 64, row0, pol_out);
-      bulk_commit_group();
-    }
-    ebuf ^= 1;
+    dequant_pack64<OUT>(tp, c, v, xs2, has_bias, packed);
+    store_chunk64<EPB>(tm_out, bufs, ebuf, lane, packed, n_tile0 + c * 64, row0, pol_out);
   }
   if (nchunks == 0) {
     tmem_ld_wait_regs(r0);
@@ -728,18 +810,20 @@ struct PairCfg {
   // 2-byte outputs are stored in 32 x 64 boxes (full 128-byte rows, 128-byte swizzle),
   // fp32 and the SwiGLU epilogue in 32 x 32 boxes
   static constexpr int kEpiCols = (OutTraits<OUT>::kBytes == 2 && OUT != kOutSwiglu) ? 64 : EPI_COLS;
-  static constexpr int kEpiBytes = 32 * kEpiCols * OutTraits<OUT>::kBytes;
-  static constexpr int kStages = 5;
-  // kOutGated: a 32-row x 128-byte residual buffer per epilogue warp
-  static constexpr int kResBytes = OUT == kOutGated ? 32 * 128 : 16;
+  static constexpr int kEpiBytes = OUT == kOutGated ? 16 : 32 * kEpiCols * OutTraits<OUT>::kBytes;
+  // kOutGated stores from its residual buffers (a warp's 32 x 256 slice of the tile, 16 KB)
+  // instead of the staging buffers, and keeps four stages to make room for them
+  static constexpr int kStages = OUT == kOutGated ? 4 : 5;
+  static constexpr int kResBytes = OUT == kOutGated ? 4 * 32 * 128 : 16;
 };
 
 template <int STAGES, int EPB, int RESB>
 struct SmemPair {
   uint8_t a[STAGES][P_A_BYTES];
   uint8_t b[STAGES][P_B_BYTES];
-  uint8_t epi[EPI_WARPS][2][EPB];
-  uint8_t res[EPI_WARPS][RESB];   // kOutGated: each lane's residual row chunk
+  alignas(1024) uint8_t epi[EPI_WARPS][2][EPB];
+  alignas(1024) uint8_t res[EPI_WARPS][RESB];        // kOutGated: residual / output chunks
+  uint8_t gate[EPI_WARPS][RESB > 16 ? 512 : 16];     // kOutGated: a shared gate row
   TileParams params[2];   // channel parameters of the tile in each accumulator
   uint64_t full[STAGES];
   uint64_t empty[STAGES];
@@ -915,19 +999,27 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       const int row0 = tm * P_BM + static_cast<int>(rank) * P_ROWS + quarter * 32;
       // channel parameters and the row scale load while the MMA still runs
       stage_tile_params<OUT>(args, tn * BN, e, 128, s.params[acc]);
+
       const float xs_r = row0 + lane < args.M ? __ldg(args.xs + row0 + lane) : 0.f;
+      [[maybe_unused]] GatedSlice gs{};
+      if constexpr (OUT == kOutGated) {
+        if (row0 < args.M) gs = gated_prefetch(args, s.res[ew], s.gate[ew], row0, tn * BN, lane);
+      }
       const bool ok = mbar_wait(&s.tmem_full[acc], acc_phase, kStatusTimeoutEpilogue);
       // all four warps staged the parameters; they leave together if any wait ran out
       if (named_bar_any(1, 128, !ok)) break;
       tc_fence_after();
       if (row0 < args.M) {
         const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
-        if constexpr (OUT == kOutSwiglu)
+        if constexpr (OUT == kOutGated)
+          epilogue_tile_gated<IN>(args, &tm_out, s.res[ew], s.gate[ew], gs, t_row, row0, tn * BN, lane, pol_out, xs_r,
+                                  s.params[acc]);
+        else if constexpr (OUT == kOutSwiglu)
           epilogue_tile_swiglu<IN, Cfg::kEpiBytes>(args, &tm_out, s.epi[ew], ebuf, t_row, row0, tn * BN, lane, pol_out,
                                                    xs_r, s.params[acc]);
         else if constexpr (Cfg::kEpiCols == 64)
           epilogue_tile_staged64<IN, OUT, Cfg::kEpiBytes>(args, &tm_out, s.epi[ew], ebuf, t_row, row0, tn * BN, lane,
-                                                          pol_out, xs_r, s.params[acc], s.res[ew]);
+                                                          pol_out, xs_r, s.params[acc]);
         else
           epilogue_tile_staged<IN, OUT, Cfg::kEpiBytes>(args, &tm_out, s.epi[ew], ebuf, t_row, row0, tn * BN, lane,
                                                         pol_out, xs_r, s.params[acc]);
@@ -936,6 +1028,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty_bar[acc]);
     }
+    if constexpr (OUT == kOutGated) cp_async_wait_all();   // a residual copy left by a wait that gave up
     if (lane == 0) bulk_wait_group_all();
     __syncwarp();
   }
