@@ -52,3 +52,31 @@ def test_int8_linear_op(mods):
     xq, xs = ops.quant_rows(x.reshape(300, 768), "int8")
     ref = ops.gemm_dequant(xq, w, xs, ws, bias).reshape(3, 100, 1536)
     assert torch.equal(out, ref)
+
+
+def test_compiled_fused_block_tail_matches_eager(mods):
+    """fc1 with the SwiGLU epilogue and fc2 with the gated residual, compiled, against the
+    eager library calls."""
+    ops, _ = mods
+    g = torch.Generator(device="cuda").manual_seed(5)
+    T, D, F = 512, 1024, 2048
+    x = torch.randn(T, D, generator=g, device="cuda").to(torch.bfloat16)
+    gate = (torch.randn(2, D, generator=g, device="cuda") * 0.1).to(torch.bfloat16)
+    q, qs = ops.quant_rows(x, "int8")
+    w1, ws1 = ops.quant_rows((torch.randn(2 * F, D, generator=g, device="cuda") * 0.02).to(torch.bfloat16), "int8")
+    w2, ws2 = ops.quant_rows((torch.randn(D, F, generator=g, device="cuda") * 0.02).to(torch.bfloat16), "int8")
+    il = ops.interleave_gate_up
+    w1i, ws1i = il(w1), il(ws1)
+
+    def tail(q, qs, w1i, ws1i, w2, ws2, x, gate):
+        act = torch.ops.t8g.gemm_swiglu(q, w1i, qs, ws1i, None)
+        a, as_ = torch.ops.t8g.quant_rows(act, "int8")
+        return torch.ops.t8g.gemm_gated(a, w2, as_, ws2, None, x, gate, T // 2)
+
+    def eager(q, qs, w1i, ws1i, w2, ws2, x, gate):
+        a, as_ = ops.quant_rows(ops.gemm_swiglu(q, w1i, qs, ws1i), "int8")
+        return ops.gemm_gated(a, w2, as_, ws2, None, x, gate, rows_per_gate=T // 2)
+
+    args = (q, qs, w1i, ws1i, w2, ws2, x, gate)
+    compiled = torch.compile(tail, backend="aot_eager", fullgraph=True)
+    assert torch.equal(compiled(*args), eager(*args))

@@ -40,6 +40,11 @@ def test_fake_shapes(t8g):
         assert q.shape == (300, 1024) and s.shape == (300,)
         with pytest.raises(Exception):
             torch.ops.t8g.gemm_dequant(x8, _fake(mode, (9216, 1024), torch.int8), xs, ws, None, torch.bfloat16)
+        a = torch.ops.t8g.gemm_swiglu(x8, w8, xs, ws, None)
+        assert a.shape == (300, 4608) and a.dtype == torch.bfloat16
+        res = _fake(mode, (300, 9216), torch.bfloat16)
+        g = torch.ops.t8g.gemm_gated(x8, w8, xs, ws, None, res, _fake(mode, (2, 9216), torch.bfloat16), 150)
+        assert g.shape == (300, 9216) and g.dtype == torch.bfloat16
 
 
 def test_mlp_traces_to_t8g_ops(t8g):

@@ -14,6 +14,8 @@ dtypes), at run time the op calls the CUDA kernel on the current stream.
     t8g::rms_mod_quant(x, shift, scale, w?, mod_index?, rows_per_mod, scale_is_multiplier,
                        eps, kind) -> (q, q_scale)
     t8g::swiglu_quant(y, kind) -> (q, q_scale)                     (y = [M, 2F] fc1 output)
+    t8g::gemm_swiglu(x, w_il, x_scale, w_scale_il, bias_il?) -> act  (fc1 + SwiGLU epilogue)
+    t8g::gemm_gated(x, w, x_scale, w_scale, bias?, res, gate, rows_per_gate) -> res + gate * y
 """
 from __future__ import annotations
 
@@ -95,3 +97,28 @@ def _(y, kind):
     torch._check(y.dim() == 2 and y.shape[1] % 2 == 0, lambda: "y must be [M, 2F]")
     return y.new_empty((y.shape[0], y.shape[1] // 2), dtype=_qdtype(kind)), \
         y.new_empty((y.shape[0],), dtype=torch.float32)
+
+
+@torch.library.custom_op("t8g::gemm_swiglu", mutates_args=())
+def gemm_swiglu(x: torch.Tensor, w_il: torch.Tensor, x_scale: torch.Tensor, w_scale_il: torch.Tensor,
+                bias_il: Optional[torch.Tensor]) -> torch.Tensor:
+    return ops.gemm_swiglu(x, w_il, x_scale, w_scale_il, bias_il)
+
+
+@gemm_swiglu.register_fake
+def _(x, w_il, x_scale, w_scale_il, bias_il):
+    torch._check(x.dim() == 2 and w_il.dim() == 2 and x.shape[1] == w_il.shape[1], lambda: "x [M, K], w [2F, K]")
+    return x.new_empty((x.shape[0], w_il.shape[0] // 2), dtype=torch.bfloat16)
+
+
+@torch.library.custom_op("t8g::gemm_gated", mutates_args=())
+def gemm_gated(x: torch.Tensor, w: torch.Tensor, x_scale: torch.Tensor, w_scale: torch.Tensor,
+               bias: Optional[torch.Tensor], res: torch.Tensor, gate: torch.Tensor, rows_per_gate: int) -> torch.Tensor:
+    return ops.gemm_gated(x, w, x_scale, w_scale, bias, res, gate, rows_per_gate=rows_per_gate)
+
+
+@gemm_gated.register_fake
+def _(x, w, x_scale, w_scale, bias, res, gate, rows_per_gate):
+    torch._check(x.dim() == 2 and w.dim() == 2 and x.shape[1] == w.shape[1], lambda: "x [M, K], w [N, K]")
+    torch._check(res.shape[0] == x.shape[0] and res.shape[1] == w.shape[0], lambda: "res must be [M, N]")
+    return res.new_empty(res.shape, dtype=torch.bfloat16)
