@@ -52,6 +52,11 @@ const char* t8g_last_error(void);
  * in which case that kernel's output is incomplete. */
 int t8g_device_status(void* stream, int* status);
 
+/* The calling thread's current CUDA device, and setting it (cudaGetDevice /
+ * cudaSetDevice of the runtime this library uses), for callers without their own. */
+int t8g_get_device(int* device);
+int t8g_set_device(int device);
+
 /*
  * out[m, n] = cast( ((float(acc[m, n]) * x_scale[m]) * w_scale[n or 0]) + float(bias[n]) )
  * acc[m, n] = sum_k x[m, k] * w[n, k]   (int8 x int8, exact int32)

@@ -101,3 +101,19 @@ def test_missing_library_fails_loudly(tmp_path, monkeypatch):
     monkeypatch.setattr(_lib, "_lib", None)
     with pytest.raises(ImportError, match="build it"):
         _lib.load(str(tmp_path / "nope.so"))
+
+
+def test_capsule_module_declines_what_it_does_not_serve():
+    """The compiled proxy entry reads DLPack capsules without consuming them and launches only
+    for CUDA tensors; anything else is left to the general path (None)."""
+    import torch
+    from thor_int8_gemm_b200 import _t8g_capsule as C
+    ts = (torch.zeros(256, 64, dtype=torch.int8), torch.zeros(32, 64, dtype=torch.int8), torch.ones(256),
+          torch.ones(32), torch.zeros(0, dtype=torch.bfloat16), torch.zeros(256, 32, dtype=torch.bfloat16))
+    caps = [t.__dlpack__() for t in ts]
+    assert C.cutlass_int8_dequant(*caps, 0) is None                  # host tensors
+    assert C.cutlass_int8_dequant(*ts, 0) is None                    # tensors, not capsules
+    assert C.cutlass_int8_dequant(*caps[:6], "stream") is None       # stream not an integer
+    assert all(torch.from_dlpack(c).shape == t.shape for c, t in zip(caps, ts))   # not consumed
+    with pytest.raises(TypeError):
+        C.cutlass_int8_dequant(*caps)

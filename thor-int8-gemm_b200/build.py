@@ -1,9 +1,11 @@
-"""Build the C-ABI shared library libthor_int8_gemm_b200.so in place (sm_100a).
+"""Build the C-ABI shared library libthor_int8_gemm_b200.so in place (sm_100a), and the
+small CPython module _t8g_capsule that serves the `_C.cutlass_int8_dequant` proxy straight
+from DLPack capsules (linked against the library, found next to it at run time).
 
     python thor-int8-gemm_b200/build.py [--force]
 
-nvcc cross-compiles for sm_100a on a machine without a GPU; the resulting .so
-sits next to this file and is what the Python layer loads.
+nvcc cross-compiles for sm_100a on a machine without a GPU; the resulting .so files sit next
+to this file and are what the Python layer loads.
 """
 from __future__ import annotations
 
@@ -11,6 +13,7 @@ import os
 import shutil
 import subprocess
 import sys
+import sysconfig
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
@@ -20,6 +23,9 @@ LIB_PATH = os.path.join(HERE, LIB_NAME)
 SOURCES = [os.path.join(CSRC, "t8g.cu")]
 DEPENDS = SOURCES + [os.path.join(CSRC, f) for f in sorted(os.listdir(CSRC)) if f.endswith(".cuh")] + [
     os.path.join(ROOT, "include", "thor_int8_gemm_b200.h")]
+
+EXT_SOURCE = os.path.join(CSRC, "capsule.c")
+EXT_PATH = os.path.join(HERE, "_t8g_capsule" + sysconfig.get_config_var("EXT_SUFFIX"))
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
@@ -44,9 +50,28 @@ def up_to_date() -> bool:
     return all(os.path.getmtime(p) <= t for p in DEPENDS if os.path.exists(p))
 
 
+def build_ext(force: bool = False) -> str:
+    """Compile the capsule module (C, against Python's headers and the library)."""
+    deps = [EXT_SOURCE, LIB_PATH, os.path.join(ROOT, "include", "thor_int8_gemm_b200.h")]
+    if not force and os.path.exists(EXT_PATH) and all(os.path.getmtime(p) <= os.path.getmtime(EXT_PATH) for p in deps):
+        return EXT_PATH
+    cc = os.environ.get("CC") or shutil.which("gcc") or "cc"
+    tmp = EXT_PATH + ".tmp"
+    cmd = [cc, "-O2", "-shared", "-fPIC", "-std=c11", "-I" + sysconfig.get_paths()["include"], "-o", tmp, EXT_SOURCE,
+           "-L" + HERE, "-lthor_int8_gemm_b200", "-Wl,-rpath,$ORIGIN"]
+    proc = subprocess.run(cmd, capture_output=True, text=True)
+    if proc.returncode != 0:
+        sys.stderr.write(proc.stdout + proc.stderr)
+        raise RuntimeError(f"building {os.path.basename(EXT_PATH)} failed ({proc.returncode})")
+    os.replace(tmp, EXT_PATH)
+    return EXT_PATH
+
+
 def build(force: bool = False, verbose: bool = False) -> str:
-    """Compile the library if any source is newer than it; return its path."""
+    """Compile the library (and the capsule module) if any source is newer; return the
+    library's path."""
     if not force and up_to_date():
+        build_ext()
         return LIB_PATH
     tmp = LIB_PATH + ".tmp"
     cmd = [nvcc_path(), *NVCC_FLAGS, "-o", tmp, *SOURCES]
@@ -60,6 +85,7 @@ def build(force: bool = False, verbose: bool = False) -> str:
     os.replace(tmp, LIB_PATH)
     if verbose:
         sys.stdout.write(proc.stderr)
+    build_ext(force=True)
     return LIB_PATH
 
 

@@ -819,6 +819,19 @@ const char* t8g_version(void) { return "0.1.0"; }
 
 const char* t8g_last_error(void) { return g_last_error; }
 
+int t8g_get_device(int* device) {
+  g_last_error[0] = '\0';
+  if (!device) return fail(T8G_ERR_INVALID_ARGUMENT, "device is null");
+  T8G_CHECK_CUDA(cudaGetDevice(device), "cudaGetDevice");
+  return T8G_OK;
+}
+
+int t8g_set_device(int device) {
+  g_last_error[0] = '\0';
+  T8G_CHECK_CUDA(cudaSetDevice(device), "cudaSetDevice");
+  return T8G_OK;
+}
+
 int t8g_device_status(void* stream, int* status) {
   g_last_error[0] = '\0';
   if (!status) return fail(T8G_ERR_INVALID_ARGUMENT, "status is null");

@@ -56,6 +56,24 @@ def _b200_gemm(x8, w8, x_scale, w_scale, bias, out, stream=None):
     return ops.gemm_dequant(x8, w8, x_scale, w_scale, bias, out=out, stream=stream)
 
 
+_capsule_fn = None
+_capsule_tried = False
+
+
+def _capsule_entry():
+    """The compiled capsule fast path (`_t8g_capsule.cutlass_int8_dequant`), or None when the
+    module is not built (the general path below then serves every call)."""
+    global _capsule_fn, _capsule_tried
+    if not _capsule_tried:
+        _capsule_tried = True
+        try:
+            from . import _t8g_capsule
+            _capsule_fn = _t8g_capsule.cutlass_int8_dequant
+        except ImportError:
+            _capsule_fn = None
+    return _capsule_fn
+
+
 def _stream_arg(stream):
     """comfy passes the raw cudaStream_t; anything unusable means torch's current stream."""
     try:
@@ -82,6 +100,19 @@ class _CProxy:
         return self._real.cutlass_int8_dequant(*(t.__dlpack__(stream=-1) for t in tensors), dtype_code, stream)
 
     def cutlass_int8_dequant(self, x, w, x_scale, w_scale, bias, out, dtype_code, stream):
+        fast = _capsule_entry() if (self._gemm is _b200_gemm and not self._broken) else None
+        if fast is not None:
+            # capsules read in place (not consumed): eligible calls launch here, the rest
+            # take the general path below
+            try:
+                if fast(x, w, x_scale, w_scale, bias, out, stream) is True:
+                    return True
+            except Exception as exc:  # a rejected launch: stock for the rest of the process
+                import traceback
+                self._broken = True
+                print(f"{TAG} B200 GEMM failed ({exc!r:.200}); stock CUTLASS for the rest of this process\n"
+                      + traceback.format_exc(), file=sys.stderr, flush=True)
+                return self._real.cutlass_int8_dequant(x, w, x_scale, w_scale, bias, out, dtype_code, stream)
         import torch
         tensors = tuple(torch.from_dlpack(t) for t in (x, w, x_scale, w_scale, bias, out))
         tx, tw, txs, tws, tb, tout = tensors
