@@ -35,7 +35,11 @@ def fast_counter(monkeypatch):
     seen = []
 
     def counting(*a):
-        r = fn(*a)
+        try:
+            r = fn(*a)
+        except Exception:
+            seen.append("raised")
+            raise
         seen.append(r)
         return r
 
@@ -116,4 +120,4 @@ def test_rejected_launch_latches_to_stock(ops, fast_counter, capsys):
     assert proxy._broken and stock.calls == 1
     assert "B200 GEMM failed" in capsys.readouterr().err
     assert call(proxy, (x_misaligned, wq, xs, ws, b, out)) == "stock"   # latched: no second try
-    assert len(fast_counter) == 1
+    assert fast_counter == ["raised"]
