@@ -72,6 +72,10 @@ CASES = [
     (1, 8, 32, True, "bf16", True),              # single row, tiny N
     (2048, 9216, 512, False, "bf16", True),      # N = QKV width, many tiles per CTA
     (333, 24576 // 8, 12288 // 8, True, "bf16", False),
+    # few 256-wide tiles: the 2-SM kernel narrows its tiles to 128 or 64 columns
+    (64, 9216, 3072, True, "bf16", False),        # 36 tiles -> 128-column tiles
+    (200, 1000, 1008, True, "f16", False),        # 4 tiles -> 64-column tiles, ragged last chunk
+    (512, 200, 256, False, "bf16", True),         # N below one 64-column chunk per tile
 ]
 
 

@@ -403,9 +403,9 @@ struct TileParams {
   uint32_t bias2[BN / 2];   // 2-byte outputs: the bias as packed pairs of the output type
 };
 
-template <int OUT>
+template <int OUT, int TBN = BN>
 __device__ __forceinline__ void stage_tile_params(const Args& args, int n_tile0, int e, int ne, TileParams& tp) {
-  for (int j = e; j < BN; j += ne) {
+  for (int j = e; j < TBN; j += ne) {
     const int n = n_tile0 + j;
     const bool in = n < args.N;
     tp.ws[j] = in ? __ldg(args.ws + (args.ws_stride ? n : 0)) : 0.f;
@@ -413,7 +413,7 @@ __device__ __forceinline__ void stage_tile_params(const Args& args, int n_tile0,
   }
   if constexpr (OutTraits<OUT>::kBytes == 2) {
     const uint16_t* b16 = static_cast<const uint16_t*>(args.bias);
-    for (int j = e; j < BN / 2; j += ne) {
+    for (int j = e; j < TBN / 2; j += ne) {
       const int n = n_tile0 + 2 * j;
       const uint32_t lo = (args.bias && n < args.N) ? b16[n] : 0u;
       const uint32_t hi = (args.bias && n + 1 < args.N) ? b16[n + 1] : 0u;
@@ -690,13 +690,13 @@ __device__ __forceinline__ void epilogue_tile_gated(const Args& args, const CUte
 // TMEM loads per chunk (the next chunk's loads overlap this chunk's math), packed
 // products, the bias added from its 16-bit pair, and a 32 x 64 TMA store of full
 // 128-byte rows from a 128-byte-swizzled staging buffer.
-template <int IN, int OUT, int EPB>
+template <int IN, int OUT, int EPB, int TBN = BN>
 __device__ __forceinline__ void epilogue_tile_staged64(const Args& args, const CUtensorMap* tm_out,
                                                        uint8_t (*bufs)[EPB], int& ebuf, uint32_t t_row, int row0,
                                                        int n_tile0, int lane, uint64_t pol_out, float xs_r,
                                                        const TileParams& tp) {
   static_assert(EPB >= 32 * 128, "staging buffer holds 32 rows of 128 bytes");
-  const int nchunks = min(BN / 64, (args.N - n_tile0 + 63) / 64);
+  const int nchunks = min(TBN / 64, (args.N - n_tile0 + 63) / 64);
   const bool has_bias = args.bias != nullptr;
   const float2 xs2 = make_float2(xs_r, xs_r);
   uint32_t r0[32], r1[32];
@@ -805,8 +805,12 @@ constexpr int P_STAGE_BYTES = P_A_BYTES + P_B_BYTES;   // per CTA
 // Ring depth and epilogue staging per output type: a staging buffer holds 32 rows x
 // 32 columns of the output type, so 2-byte outputs leave room for a sixth stage
 // (6 x 32 KB ring + 16 KB staging + 4 KB parameters); fp32 outputs keep five.
-template <int OUT>
+template <int OUT, int TBN = BN>
 struct PairCfg {
+  static_assert(TBN == BN || ((TBN == 128 || TBN == 64) && (OUT == kOutBF16 || OUT == kOutF16)),
+                "narrow tiles serve the plain 2-byte outputs");
+  static constexpr int kBRows = TBN / 2;             // rows of W per CTA
+  static constexpr int kBBytes = kBRows * BK;
   // 2-byte outputs are stored in 32 x 64 boxes (full 128-byte rows, 128-byte swizzle),
   // fp32 and the SwiGLU epilogue in 32 x 32 boxes
   static constexpr int kEpiCols = (OutTraits<OUT>::kBytes == 2 && OUT != kOutSwiglu) ? 64 : EPI_COLS;
@@ -817,10 +821,10 @@ struct PairCfg {
   static constexpr int kResBytes = OUT == kOutGated ? 4 * 32 * 128 : 16;
 };
 
-template <int STAGES, int EPB, int RESB>
+template <int STAGES, int EPB, int RESB, int BBYTES = P_B_BYTES>
 struct SmemPair {
   uint8_t a[STAGES][P_A_BYTES];
-  uint8_t b[STAGES][P_B_BYTES];
+  uint8_t b[STAGES][BBYTES];
   alignas(1024) uint8_t epi[EPI_WARPS][2][EPB];
   alignas(1024) uint8_t res[EPI_WARPS][RESB];        // kOutGated: residual / output chunks
   uint8_t gate[EPI_WARPS][RESB > 16 ? 512 : 16];     // kOutGated: a shared gate row
@@ -832,30 +836,32 @@ struct SmemPair {
   uint64_t drain;
   uint32_t tmem_base;
 };
-template <int OUT>
-using SmemPairOf = SmemPair<PairCfg<OUT>::kStages, PairCfg<OUT>::kEpiBytes, PairCfg<OUT>::kResBytes>;
-template <int OUT>
-constexpr size_t pair_smem_bytes() { return sizeof(SmemPairOf<OUT>) + 1024; }   // + slack to align to 1024 B
+template <int OUT, int TBN = BN>
+using SmemPairOf = SmemPair<PairCfg<OUT, TBN>::kStages, PairCfg<OUT, TBN>::kEpiBytes, PairCfg<OUT, TBN>::kResBytes,
+                            PairCfg<OUT, TBN>::kBBytes>;
+template <int OUT, int TBN = BN>
+constexpr size_t pair_smem_bytes() { return sizeof(SmemPairOf<OUT, TBN>) + 1024; }   // + slack to align to 1024 B
 static_assert(pair_smem_bytes<kOutBF16>() <= 227 * 1024 && pair_smem_bytes<kOutF32>() <= 227 * 1024 &&
                   pair_smem_bytes<kOutGated>() <= 227 * 1024,
               "pair kernel shared memory exceeds the per-CTA limit");
 
-template <int IN, int OUT>
+template <int IN, int OUT, int TBN = BN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     gemm_dequant_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                              const __grid_constant__ CUtensorMap tm_out, const Args args) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
-  using Cfg = PairCfg<OUT>;
+  using Cfg = PairCfg<OUT, TBN>;
   constexpr int P_STAGES = Cfg::kStages;
-  SmemPairOf<OUT>& s = *reinterpret_cast<SmemPairOf<OUT>*>(smem_raw + pad);
+  constexpr uint32_t kTmemCols = 2 * TBN;   // double-buffered accumulator
+  SmemPairOf<OUT, TBN>& s = *reinterpret_cast<SmemPairOf<OUT, TBN>*>(smem_raw + pad);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
   const int pair = static_cast<int>(blockIdx.x >> 1);
   const int npairs = static_cast<int>(gridDim.x >> 1);
-  const int tiles_n = (args.N + BN - 1) / BN;
+  const int tiles_n = (args.N + TBN - 1) / TBN;
   const int tiles_m = (args.M + P_BM - 1) / P_BM;
   const int num_tiles = tiles_m * tiles_n;
   const int kblocks = (args.K + BK - 1) / BK;
@@ -878,7 +884,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     prefetch_tensormap(&tm_out);
   }
   if (warp == 1) {
-    tmem_alloc_pair(&s.tmem_base, TMEM_COLS);
+    tmem_alloc_pair(&s.tmem_base, kTmemCols);
     tmem_relinquish_pair();
   }
   tc_fence_before();
@@ -904,10 +910,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
             ok = false;
             break;
           }
-          if (rank == 0) mbar_arrive_expect_tx(&s.full[stage], 2 * P_STAGE_BYTES);
+          if (rank == 0) mbar_arrive_expect_tx(&s.full[stage], 2 * (P_A_BYTES + Cfg::kBBytes));
           const uint32_t bar = mapa_shared(smem_u32(&s.full[stage]), 0);
           tma_load_2d_pair(s.a[stage], &tm_a, bar, kb * BK, tm * P_BM + static_cast<int>(rank) * P_ROWS, pol_a);
-          tma_load_2d_pair(s.b[stage], &tm_b, bar, kb * BK, tn * BN + static_cast<int>(rank) * P_ROWS, pol_b);
+          tma_load_2d_pair(s.b[stage], &tm_b, bar, kb * BK, tn * TBN + static_cast<int>(rank) * Cfg::kBRows, pol_b);
           ++issued;
           if (++stage == P_STAGES) {
             stage = 0;
@@ -926,8 +932,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer (leader only)
     if (lane == 0 && rank == 0) {
-      constexpr uint32_t idesc = (IN == kInI8) ? make_idesc(2, 1, 1, P_BM, BN)   // s32 <- s8 x s8
-                                               : make_idesc(1, 0, 0, P_BM, BN);  // f32 <- e4m3 x e4m3
+      constexpr uint32_t idesc = (IN == kInI8) ? make_idesc(2, 1, 1, P_BM, TBN)   // s32 <- s8 x s8
+                                               : make_idesc(1, 0, 0, P_BM, TBN);  // f32 <- e4m3 x e4m3
       // cluster addresses of the barrier arrays in both CTAs (8 bytes per barrier)
       const uint32_t empty0[2] = {mapa_shared(smem_u32(&s.empty[0]), 0), mapa_shared(smem_u32(&s.empty[0]), 1)};
       const uint32_t tfull0[2] = {mapa_shared(smem_u32(&s.tmem_full[0]), 0),
@@ -944,7 +950,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
           break;
         }
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * TBN);
         for (int kb = 0; kb < kblocks; ++kb) {
           if (!mbar_wait(&s.full[stage], phase, kStatusTimeoutMma)) {
             ok = false;
@@ -998,30 +1004,30 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       const uint32_t acc_phase = static_cast<uint32_t>((local >> 1) & 1);
       const int row0 = tm * P_BM + static_cast<int>(rank) * P_ROWS + quarter * 32;
       // channel parameters and the row scale load while the MMA still runs
-      stage_tile_params<OUT>(args, tn * BN, e, 128, s.params[acc]);
+      stage_tile_params<OUT, TBN>(args, tn * TBN, e, 128, s.params[acc]);
 
       const float xs_r = row0 + lane < args.M ? __ldg(args.xs + row0 + lane) : 0.f;
       [[maybe_unused]] GatedSlice gs{};
       if constexpr (OUT == kOutGated) {
-        if (row0 < args.M) gs = gated_prefetch(args, s.res[ew], s.gate[ew], row0, tn * BN, lane);
+        if (row0 < args.M) gs = gated_prefetch(args, s.res[ew], s.gate[ew], row0, tn * TBN, lane);
       }
       const bool ok = mbar_wait(&s.tmem_full[acc], acc_phase, kStatusTimeoutEpilogue);
       // all four warps staged the parameters; they leave together if any wait ran out
       if (named_bar_any(1, 128, !ok)) break;
       tc_fence_after();
       if (row0 < args.M) {
-        const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
+        const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * TBN);
         if constexpr (OUT == kOutGated)
-          epilogue_tile_gated<IN>(args, &tm_out, s.res[ew], s.gate[ew], gs, t_row, row0, tn * BN, lane, pol_out, xs_r,
+          epilogue_tile_gated<IN>(args, &tm_out, s.res[ew], s.gate[ew], gs, t_row, row0, tn * TBN, lane, pol_out, xs_r,
                                   s.params[acc]);
         else if constexpr (OUT == kOutSwiglu)
-          epilogue_tile_swiglu<IN, Cfg::kEpiBytes>(args, &tm_out, s.epi[ew], ebuf, t_row, row0, tn * BN, lane, pol_out,
+          epilogue_tile_swiglu<IN, Cfg::kEpiBytes>(args, &tm_out, s.epi[ew], ebuf, t_row, row0, tn * TBN, lane, pol_out,
                                                    xs_r, s.params[acc]);
         else if constexpr (Cfg::kEpiCols == 64)
-          epilogue_tile_staged64<IN, OUT, Cfg::kEpiBytes>(args, &tm_out, s.epi[ew], ebuf, t_row, row0, tn * BN, lane,
-                                                          pol_out, xs_r, s.params[acc]);
+          epilogue_tile_staged64<IN, OUT, Cfg::kEpiBytes, TBN>(args, &tm_out, s.epi[ew], ebuf, t_row, row0, tn * TBN,
+                                                               lane, pol_out, xs_r, s.params[acc]);
         else
-          epilogue_tile_staged<IN, OUT, Cfg::kEpiBytes>(args, &tm_out, s.epi[ew], ebuf, t_row, row0, tn * BN, lane,
+          epilogue_tile_staged<IN, OUT, Cfg::kEpiBytes>(args, &tm_out, s.epi[ew], ebuf, t_row, row0, tn * TBN, lane,
                                                         pol_out, xs_r, s.params[acc]);
       }
       tc_fence_before();
@@ -1038,7 +1044,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   cluster_sync();   // the pair's MMAs, copies and cross-CTA signals are all done
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc_pair(tmem_base, TMEM_COLS);
+    tmem_dealloc_pair(tmem_base, kTmemCols);
   }
 }
 

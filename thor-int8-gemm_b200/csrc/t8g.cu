@@ -155,20 +155,20 @@ bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p
 
 // ----------------------------------------------------------------- GEMM
 // 2-SM launch: clusters of two CTAs, grid = 2 x min(tiles, SMs / 2).
-template <int IN, int OUT>
+template <int IN, int OUT, int TBN = t8g::gemm::BN>
 int launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
                      const t8g::gemm::Args& args, int dev, int sms, cudaStream_t stream) {
   using namespace t8g::gemm;
   static std::atomic<bool> attr_done[kMaxDevices] = {};
-  auto kern = gemm_dequant_pair_kernel<IN, OUT>;
-  int rc = ensure_smem_attr(kern, dev, pair_smem_bytes<OUT>(), attr_done);
+  auto kern = gemm_dequant_pair_kernel<IN, OUT, TBN>;
+  int rc = ensure_smem_attr(kern, dev, pair_smem_bytes<OUT, TBN>(), attr_done);
   if (rc) return rc;
-  const int64_t tiles = static_cast<int64_t>((args.M + P_BM - 1) / P_BM) * ((args.N + BN - 1) / BN);
+  const int64_t tiles = static_cast<int64_t>((args.M + P_BM - 1) / P_BM) * ((args.N + TBN - 1) / TBN);
   const int64_t pairs = tiles < sms / 2 ? tiles : sms / 2;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs), 1, 1);
   cfg.blockDim = dim3(NUM_THREADS, 1, 1);
-  cfg.dynamicSmemBytes = pair_smem_bytes<OUT>();
+  cfg.dynamicSmemBytes = pair_smem_bytes<OUT, TBN>();
   cfg.stream = stream;
   cfg.attrs = nullptr;   // the kernel declares its cluster shape (2, 1, 1)
   cfg.numAttrs = 0;
@@ -222,14 +222,25 @@ int gemm_entry(int in_kind, const void* x, const void* w, const float* x_scale, 
   if (rc) return rc;
 
   // The 2-SM kernel (CTA pairs, 256-row tiles) runs whenever there is more than one
-  // 128-row block; T8G_GEMM_SM=1 in the environment forces the 1-SM kernel.
+  // 128-row block or narrow tiles apply; T8G_GEMM_SM=1 in the environment forces the 1-SM
+  // kernel.
   const char* sm_env = getenv("T8G_GEMM_SM");
-  const bool pair = M > BM && !(sm_env && sm_env[0] == '1');
+  const bool force_1sm = sm_env && sm_env[0] == '1';
+  // Tile width of the 2-SM kernel: 256 columns, or 128 / 64 for 2-byte outputs when 256-wide
+  // tiles would leave more than half of the CTA pairs idle (small M): narrower tiles put more
+  // SMs on the problem, each with a shorter tile.
+  const int64_t pairs_avail = info.sms / 2;
+  const int64_t tiles_m = (M + P_BM - 1) / P_BM;
+  int tbn = BN;
+  if (esz == 2) {
+    while (tbn > 64 && tiles_m * ((N + tbn - 1) / tbn) * 2 < pairs_avail) tbn /= 2;
+  }
+  const bool pair = (M > BM || tbn < BN) && !force_1sm;
   const CUtensorMapDataType in_dt = CU_TENSOR_MAP_DATA_TYPE_UINT8;
   CUtensorMap ta, tb, to;
   rc = encode_2d(&ta, in_dt, x, K, M, ld_x, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
-  rc = encode_2d(&tb, in_dt, w, K, N, ld_w, BK, pair ? P_ROWS : BN, CU_TENSOR_MAP_SWIZZLE_128B);
+  rc = encode_2d(&tb, in_dt, w, K, N, ld_w, BK, pair ? static_cast<uint32_t>(tbn / 2) : BN, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   const CUtensorMapDataType out_dt = out_dtype == T8G_OUT_BF16  ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                      : out_dtype == T8G_OUT_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
@@ -251,6 +262,22 @@ int gemm_entry(int in_kind, const void* x, const void* w, const float* x_scale, 
   args.N = static_cast<int>(N);
   args.K = static_cast<int>(K);
   cudaStream_t st = static_cast<cudaStream_t>(stream_);
+  if (pair && tbn != BN) {
+    // narrow tiles (2-byte outputs only)
+    const bool f16 = out_dtype == T8G_OUT_F16;
+    if (in_kind == kInI8) {
+      if (tbn == 128)
+        return f16 ? launch_gemm_pair<kInI8, kOutF16, 128>(ta, tb, to, args, dev, info.sms, st)
+                   : launch_gemm_pair<kInI8, kOutBF16, 128>(ta, tb, to, args, dev, info.sms, st);
+      return f16 ? launch_gemm_pair<kInI8, kOutF16, 64>(ta, tb, to, args, dev, info.sms, st)
+                 : launch_gemm_pair<kInI8, kOutBF16, 64>(ta, tb, to, args, dev, info.sms, st);
+    }
+    if (tbn == 128)
+      return f16 ? launch_gemm_pair<kInE4M3, kOutF16, 128>(ta, tb, to, args, dev, info.sms, st)
+                 : launch_gemm_pair<kInE4M3, kOutBF16, 128>(ta, tb, to, args, dev, info.sms, st);
+    return f16 ? launch_gemm_pair<kInE4M3, kOutF16, 64>(ta, tb, to, args, dev, info.sms, st)
+               : launch_gemm_pair<kInE4M3, kOutBF16, 64>(ta, tb, to, args, dev, info.sms, st);
+  }
   if (pair) {
     if (in_kind == kInI8) {
       switch (out_dtype) {
