@@ -774,7 +774,7 @@ def run_ours(args):
             mlp[t] = round(world * chain_ops / (mlp[k] / 1e3) / 1e12, 1)
         extras["mlp_chain_int8"] = mlp
         torch.cuda.empty_cache()
-        blk = time_dit_block(torch, dev, 2, 1, stream, seed=11 + rank)
+        blk = time_dit_block(torch, dev, 5, 2, stream, seed=11 + rank)
         for k in ("block_ms", "linears_and_norms_ms"):
             blk[k] = round(shard.max_over_ranks(blk[k], device=dev), 3)
         blk["linear_tops"] = round(world * 2.0 * 112640 * (3 * 3072 * 3072 + 3072 * 3072 + 2 * 12288 * 3072 + 3072 * 12288)
