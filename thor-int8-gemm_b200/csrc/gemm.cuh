@@ -731,34 +731,47 @@ __device__ __forceinline__ void epilogue_tile_swiglu(const Args& args, const CUt
                                                      int n_tile0, int lane, uint64_t pol_out, float xs_r,
                                                      const TileParams& tp) {
   const bool has_bias = args.bias != nullptr;
+  const float2 xs2 = make_float2(xs_r, xs_r);
+  const float2 quarter = make_float2(0.25f, 0.25f);
+  constexpr int kChunks = BN / 2 / EPI_COLS;
+  uint32_t rg[32], ru[32];
+  tmem_ld_32x32b_x32(t_row, rg);
+  tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(BN / 2), ru);
 #pragma unroll 1
-  for (int c = 0; c < BN / 2 / EPI_COLS; ++c) {
-    uint32_t rg[32], ru[32];
-    tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(c * EPI_COLS), rg);
-    tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(BN / 2 + c * EPI_COLS), ru);
+  for (int c = 0; c < kChunks; ++c) {
     tmem_ld_wait_regs(rg);
     tmem_ld_wait_regs(ru);
+    float2 gf[16], uf[16];
+#pragma unroll
+    for (int p = 0; p < 16; ++p) {
+      gf[p] = (IN == kInI8) ? make_float2(__int2float_rn(static_cast<int>(rg[2 * p])),
+                                          __int2float_rn(static_cast<int>(rg[2 * p + 1])))
+                            : make_float2(__uint_as_float(rg[2 * p]), __uint_as_float(rg[2 * p + 1]));
+      uf[p] = (IN == kInI8) ? make_float2(__int2float_rn(static_cast<int>(ru[2 * p])),
+                                          __int2float_rn(static_cast<int>(ru[2 * p + 1])))
+                            : make_float2(__uint_as_float(ru[2 * p]), __uint_as_float(ru[2 * p + 1]));
+    }
+    // the next chunk's accumulator loads while this one computes
+    if (c + 1 < kChunks) {
+      tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>((c + 1) * EPI_COLS), rg);
+      tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(BN / 2 + (c + 1) * EPI_COLS), ru);
+    }
+    const float2* wg = reinterpret_cast<const float2*>(tp.ws + c * EPI_COLS);
+    const float2* wu = reinterpret_cast<const float2*>(tp.ws + BN / 2 + c * EPI_COLS);
+    const uint32_t* bg = tp.bias2 + c * EPI_COLS / 2;
+    const uint32_t* bu = tp.bias2 + (BN / 2 + c * EPI_COLS) / 2;
     uint32_t act[16];
 #pragma unroll
     for (int p = 0; p < 16; ++p) {
-      float gv[2], uv[2];
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int j = 2 * p + e;
-        const int cg = c * EPI_COLS + j, cu = BN / 2 + c * EPI_COLS + j;
-        float g = (IN == kInI8) ? __int2float_rn(static_cast<int>(rg[j])) : __uint_as_float(rg[j]);
-        float u = (IN == kInI8) ? __int2float_rn(static_cast<int>(ru[j])) : __uint_as_float(ru[j]);
-        g = __fmul_rn(__fmul_rn(g, xs_r), tp.ws[cg]);
-        u = __fmul_rn(__fmul_rn(u, xs_r), tp.ws[cu]);
-        if (has_bias) {
-          g = __fadd_rn(g, tp.bias[cg]);
-          u = __fadd_rn(u, tp.bias[cu]);
-        }
-        gv[e] = __bfloat162float(__float2bfloat16_rn(g));
-        uv[e] = __bfloat162float(__float2bfloat16_rn(u));
+      // gate and up exactly as the plain epilogue stores them: ((acc * xs) * ws) + bias, bf16
+      float2 g = mul2_rn(mul2_rn(gf[p], xs2), wg[p]);
+      float2 u = mul2_rn(mul2_rn(uf[p], xs2), wu[p]);
+      if (has_bias) {
+        g = add_f32_bf16x2(g, bg[p]);
+        u = add_f32_bf16x2(u, bu[p]);
       }
       // g / 4 is exact for a bf16 g
-      act[p] = f2_to_bf2(silu_mul2(make_float2(gv[0] * 0.25f, gv[1] * 0.25f), make_float2(uv[0], uv[1])));
+      act[p] = f2_to_bf2(silu_mul2(mul2_rn(bf2_to_f2(f2_to_bf2(g)), quarter), bf2_to_f2(f2_to_bf2(u))));
     }
     if (lane == 0) bulk_wait_group_read<1>();
     __syncwarp();
