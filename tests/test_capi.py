@@ -115,5 +115,8 @@ def test_capsule_module_declines_what_it_does_not_serve():
     assert C.cutlass_int8_dequant(*ts, 0) is None                    # tensors, not capsules
     assert C.cutlass_int8_dequant(*caps[:6], "stream") is None       # stream not an integer
     assert all(torch.from_dlpack(c).shape == t.shape for c, t in zip(caps, ts))   # not consumed
+    vcaps = [t.__dlpack__(max_version=(1, 0)) for t in ts]                # DLPack 1.x capsules
+    assert C.cutlass_int8_dequant(*vcaps, 0) is None
+    assert all(torch.from_dlpack(c).shape == t.shape for c, t in zip(vcaps, ts))
     with pytest.raises(TypeError):
         C.cutlass_int8_dequant(*caps)

@@ -121,3 +121,13 @@ def test_rejected_launch_latches_to_stock(ops, fast_counter, capsys):
     assert "B200 GEMM failed" in capsys.readouterr().err
     assert call(proxy, (x_misaligned, wq, xs, ws, b, out)) == "stock"   # latched: no second try
     assert fast_counter == ["raised"]
+
+
+def test_capsule_module_takes_dlpack_1_capsules(ops):
+    """DLPack 1.x ("dltensor_versioned") capsules launch the same GEMM."""
+    from thor_int8_gemm_b200 import _t8g_capsule as C
+    xq, wq, xs, ws, b, out = problem(ops, 512, 3072, 1024, seed=9)
+    caps = [t.__dlpack__(max_version=(1, 0)) for t in (xq, wq, xs, ws, b, out)]
+    assert C.cutlass_int8_dequant(*caps, torch.cuda.current_stream().cuda_stream) is True
+    torch.cuda.synchronize()
+    assert torch.equal(out, ops.gemm_dequant(xq, wq, xs, ws, b))
