@@ -66,8 +66,8 @@ def parse_args():
     ap.add_argument("--scaling", choices=("weak", "strong"), default="weak",
                     help="weak: every rank runs the full sweep on its own tokens; strong: the sweep's "
                          "tokens are split across the ranks")
-    ap.add_argument("--profile", choices=("gemm_i8", "gemm_fp8", "gemm_gated", "rms_fp8", "rms_int8", "swiglu_int8",
-                                          "quant_int8"),
+    ap.add_argument("--profile", choices=("gemm_i8", "gemm_fp8", "gemm_gated", "gemm_swiglu", "rms_fp8", "rms_int8",
+                                          "swiglu_int8", "quant_int8"),
                     help="run one kernel a few times on a mid-size case (for ncu captures) and exit")
     ap.add_argument("--M", type=int, default=32768)
     ap.add_argument("--N", type=int, default=9216)
@@ -78,7 +78,8 @@ def run_profile_case(args):
     """One kernel, `warmup + steps` launches, on a case whose inputs exceed L2 but stay
     within a few GB: GEMM M x N x 3072; norm/quant and per-token quant [2*56320, 3072];
     SwiGLU [32768, 2*12288]; gemm_gated: the GEMM with the gated residual updating a bf16
-    [M, N] residual in place (two gate rows)."""
+    [M, N] residual in place (two gate rows); gemm_swiglu: fc1 (N = 2F) with the SwiGLU
+    epilogue."""
     import torch
     from __graft_entry__ import load_package
     load_package()
@@ -88,7 +89,17 @@ def run_profile_case(args):
     gen = torch.Generator(device=dev)
     gen.manual_seed(5)
     n = args.warmup + args.steps
-    if args.profile == "gemm_gated":
+    if args.profile == "gemm_swiglu":
+        # fc1 of the MLP with the SwiGLU epilogue: x [M, 3072] -> act [M, N / 2] (N = 2F)
+        x, xs = ops.quant_rows(torch.randn(args.M, K_DIM, generator=gen, device=dev).to(torch.bfloat16), "int8")
+        w, ws = ops.quant_rows((torch.randn(args.N, K_DIM, generator=gen, device=dev) * 0.02).to(torch.bfloat16), "int8")
+        bias = (torch.randn(args.N, generator=gen, device=dev) * 0.01).to(torch.bfloat16)
+        il = ops.interleave_gate_up
+        w, ws, bias = il(w), il(ws), il(bias)
+        act = torch.empty(args.M, args.N // 2, dtype=torch.bfloat16, device=dev)
+        for _ in range(n):
+            ops.gemm_swiglu(x, w, xs, ws, bias, out=act)
+    elif args.profile == "gemm_gated":
         x, xs = ops.quant_rows(torch.randn(args.M, K_DIM, generator=gen, device=dev).to(torch.bfloat16), "int8")
         w, ws = ops.quant_rows((torch.randn(args.N, K_DIM, generator=gen, device=dev) * 0.02).to(torch.bfloat16), "int8")
         bias = (torch.randn(args.N, generator=gen, device=dev) * 0.01).to(torch.bfloat16)
