@@ -7,7 +7,8 @@ One step = the DiT attention-projection GEMM sweep, int8 fused-dequant:
 K = 3072, N in {3072 (out-proj), 9216 (fused QKV)}, M in {8192, 32768, 112640}
 tokens -- six launches of the tcgen05 GEMM per step.  `value` is whole-job
 TOPS (2*M*N*K summed over the six shapes, all ranks) with inputs resident in
-HBM; `e2e` is the same metric through the public API with host (pinned)
+HBM; `e2e` is the same metric through the reference-facing entry point (the
+`_C.cutlass_int8_dequant` proxy, DLPack capsules in) with host (pinned)
 activations copied in and every output copied back inside the timed region.
 Secondary figures timed in the same run (not part of `value`, under `extras`):
 the single 256x3072x3072 GEMM, the fp8 e4m3 GEMM sweep, fused RMSNorm + adaLN
