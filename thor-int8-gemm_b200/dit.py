@@ -99,7 +99,8 @@ class DiTBlock:
         q1, s1 = self.norm_quant(x, shift_msa, scale_msa, T)
         qkv = self.qkv(q1, s1)
         attn = (attn_fn or self.attention)(qkv, batch)
-        aq, as_ = ops.quant_rows(attn.contiguous(), self.kind)
+        # the quantiser takes row-strided input; only a non-unit inner stride needs a copy
+        aq, as_ = ops.quant_rows(attn if attn.stride(-1) == 1 else attn.contiguous(), self.kind)
         if self.fused_gate:
             p = self.proj
             x = ops.gemm_gated(aq, p.w, as_, p.ws, p.bias, x, gate_msa, rows_per_gate=T)
