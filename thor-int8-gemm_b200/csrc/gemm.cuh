@@ -807,7 +807,8 @@ __device__ __forceinline__ void epilogue_tile_swiglu(const Args& args, const CUt
 // Per SM this halves W's share of the shared-memory fill and of the tensor
 // core's operand reads compared with the 1-SM kernel.  The epilogue stages each
 // tile's channel parameters in shared memory before waiting for its accumulator
-// and pipelines its TMEM loads.
+// and pipelines its TMEM loads.  With few 256-wide tiles (small M) the host picks
+// 128- or 64-column tiles (template TBN), so that more pairs share the problem.
 // ===========================================================================
 constexpr int P_BM = 256;                   // tile rows per CTA pair
 constexpr int P_ROWS = 128;                 // rows of A (and of W) per CTA
@@ -815,9 +816,11 @@ constexpr int P_A_BYTES = P_ROWS * BK;
 constexpr int P_B_BYTES = P_ROWS * BK;
 constexpr int P_STAGE_BYTES = P_A_BYTES + P_B_BYTES;   // per CTA
 
-// Ring depth and epilogue staging per output type: a staging buffer holds 32 rows x
-// 32 columns of the output type, so 2-byte outputs leave room for a sixth stage
-// (6 x 32 KB ring + 16 KB staging + 4 KB parameters); fp32 outputs keep five.
+// Ring depth, tile width and epilogue staging per output type: five 32 KB stages (per CTA)
+// and two staging buffers per epilogue warp (32 x 64 of a 2-byte output, 32 x 32 of fp32);
+// the gated epilogue keeps four stages and stores from its residual buffers instead; narrow
+// tiles (TBN = 128 / 64 columns, plain 2-byte outputs, for problems with few tiles) load
+// TBN / 2 rows of W per CTA.
 template <int OUT, int TBN = BN>
 struct PairCfg {
   static_assert(TBN == BN || ((TBN == 128 || TBN == 64) && (OUT == kOutBF16 || OUT == kOutF16)),
