@@ -35,8 +35,11 @@ every operation rounded separately, no fused multiply-add):
 the GEMM epilogue is  out = cast(((f32(acc) * xs[m]) * ws[n]) + f32(bias[n]));
 the RMS norm is       inv = 1 / sqrt(ss / D + eps),
                       h   = (((x * inv) * w) * s) + b;
-where the sum of squares `ss` follows the canonical reduction tree described
-in `rms_sum_squares`, which the CUDA kernel implements the same way.
+where the sum of squares `ss` follows, in the tensorwise (reference-signature)
+forms, the reference's own order (`rms_sum_squares_reference`), and in the
+per-token forms, which have no reference counterpart, the library's canonical
+tree (`rms_sum_squares`); the CUDA kernels implement each the same way.
+The SwiGLU's exponential is correctly rounded (`exp_f32`).
 """
 from __future__ import annotations
 
@@ -341,6 +344,45 @@ def rms_sum_squares(x: np.ndarray) -> np.ndarray:
     return tot
 
 
+REF_BLOCK_K = 2048     # src/ck_fused_mod_norm_quant.py:124 and src/ck_fused_patch.py:115
+
+
+def rms_sum_squares_reference(x: np.ndarray, block: int = REF_BLOCK_K) -> np.ndarray:
+    """Sum of squares of each row in the order of the reference's norm kernel
+    (src/ck_fused_mod_norm_quant.py:35-41), as its tl.sum evaluates:
+
+    * a float32 vector of `block` lanes accumulates the squares chunk by chunk,
+      lane i += x[block * c + i]^2 for c = 0, 1, ... (missing elements count 0);
+    * tl.sum of that vector is numpy's pairwise summation (Triton's interpreter
+      calls np.sum): for 2048 lanes a balanced binary tree over 16 leaves of 128
+      lanes, each leaf summed by 8 interleaved accumulators r_j (lanes 8t + j,
+      t = 0..15, in order) combined as ((r0 + r1) + (r2 + r3)) + ((r4 + r5) + (r6 + r7)).
+
+    The tensorwise CUDA kernels (`rms_mod_tw_*`) compute exactly this.
+    """
+    x = np.asarray(x, dtype=np.float32)
+    S, D = x.shape
+    if block % 128 or block & (block - 1):
+        raise ValueError("block must be a power of two multiple of 128")
+    nch = max(1, -(-D // block))
+    padded = np.zeros((S, nch * block), dtype=np.float32)
+    padded[:, :D] = x
+    sq = (padded * padded).astype(np.float32)            # exact: squares of bf16 values
+    lanes = sq[:, :block].copy()
+    for c in range(1, nch):
+        lanes = (lanes + sq[:, c * block:(c + 1) * block]).astype(np.float32)
+    leaves = lanes.reshape(S, block // 128, 16, 8)        # [row, leaf, t, j]
+    r = leaves[:, :, 0, :].copy()
+    for t in range(1, 16):
+        r = (r + leaves[:, :, t, :]).astype(np.float32)
+    f = lambda a, b: (a + b).astype(np.float32)           # noqa: E731
+    leaf = f(f(f(r[..., 0], r[..., 1]), f(r[..., 2], r[..., 3])),
+             f(f(r[..., 4], r[..., 5]), f(r[..., 6], r[..., 7])))
+    while leaf.shape[1] > 1:
+        leaf = f(leaf[:, 0::2], leaf[:, 1::2])
+    return leaf[:, 0]
+
+
 def rms_inv(ss: np.ndarray, D: int, eps: float) -> np.ndarray:
     """inv = 1 / sqrt(ss / D + eps) in float32 (reference: rsqrt(sum/K + eps),
     src/ck_fused_mod_norm_quant.py:41)."""
@@ -401,12 +443,13 @@ def rms_mod_res_tensorwise(x, w, s, b, eps=1e-5):
     :54-55), scale = max(amax/448, 1e-12), q = e4m3(clamp(h16/scale, +-448)).
     Returns (q codes, scale, h16 bits, res bits, amax).
 
-    The sum of squares uses the canonical tree of `rms_sum_squares`; the
-    Triton kernel's reduction order differs, so h may differ by one bf16 ulp.
+    The sum of squares follows the reference's own order
+    (`rms_sum_squares_reference`), so h, the float32 amax and the scale are the
+    reference's bit for bit.
     """
     x = np.asarray(x, np.float32)
     S, D = x.shape
-    inv = rms_inv(rms_sum_squares(x), D, eps)
+    inv = rms_inv(rms_sum_squares_reference(x), D, eps)
     h = rms_mod_h(x, inv, None if w is None else np.asarray(w, np.float32),
                   np.asarray(s, np.float32), np.asarray(b, np.float32))
     amax = np.float32(np.max(np.abs(h))) if h.size else np.float32(0)
@@ -419,15 +462,39 @@ def rms_mod_res_tensorwise(x, w, s, b, eps=1e-5):
 # --------------------------------------------------------------------------
 # SwiGLU (+ quant)
 # --------------------------------------------------------------------------
+def exp_f32(x) -> np.ndarray:
+    """exp of float32 values, correctly rounded to float32.
+
+    Evaluated in float64 (numpy's exp is accurate to well under one float64 ulp) and
+    rounded once to float32.  A double rounding can only differ from the correctly
+    rounded result when exp(x) lies within about 2^-29 float32 ulps of a rounding
+    boundary; tests/test_oracle_golden.py checks every bf16 input against a
+    multi-precision evaluation, and bf16 inputs are all this oracle feeds it.
+
+    numpy's own float32 exp (which Triton's CPU interpreter calls for tl.exp) is not
+    correctly rounded: it is off by one or two ulps on ~5 % of bf16 inputs, and its
+    SIMD kernels differ between CPUs.  The GPU's compiled Triton uses an approximate
+    exp2 instead.  The correctly rounded value is the one definition of
+    sigmoid(g) = 1 / (1 + exp(-g)) that no platform's shortcut decides; on every golden
+    vector the reference produced it gives the same act bits as the interpreter did."""
+    with np.errstate(over="ignore", under="ignore", invalid="ignore"):
+        return np.exp(np.asarray(x, np.float32).astype(np.float64)).astype(np.float32)
+
+
+def sigmoid_f32(g) -> np.ndarray:
+    """sigmoid(g) = RN(1 / RN(1 + exp_f32(-g))) in float32 (Triton's tl.sigmoid,
+    `1 / (1 + exp(-x))`, with the exponential correctly rounded)."""
+    e = exp_f32(-np.asarray(g, np.float32))
+    with np.errstate(over="ignore"):
+        return (np.float32(1.0) / (np.float32(1.0) + e)).astype(np.float32)
+
+
 def silu_mul(gate, up) -> np.ndarray:
     """act = (g * sigmoid(g)) * u in float32 (src/ck_fused_mod_norm_quant.py:71),
-    sigmoid(g) = 1 / (1 + exp(-g))."""
+    each product rounded separately."""
     g = np.asarray(gate, np.float32)
     u = np.asarray(up, np.float32)
-    with np.errstate(over="ignore"):
-        e = np.exp(-g).astype(np.float32)
-    sig = (np.float32(1.0) / (np.float32(1.0) + e)).astype(np.float32)
-    return ((g * sig).astype(np.float32) * u).astype(np.float32)
+    return ((g * sigmoid_f32(g)).astype(np.float32) * u).astype(np.float32)
 
 
 def swiglu_quant_per_token(gate, up, kind=QUANT_INT8):

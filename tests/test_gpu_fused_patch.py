@@ -96,3 +96,62 @@ def test_per_token_rows_equal_segment_rows(patched):
     b = blk(x, t, [(0, S, rows)], None)
     assert not m.DiTBlock.forward._t8g_runtime.broken
     assert torch.equal(a, b)
+
+
+class _CallCounter:
+    """Wraps a comfy linear: attributes pass through, calls are counted."""
+
+    def __init__(self, inner):
+        self._inner = inner
+        self.calls = 0
+
+    def __getattr__(self, name):
+        return getattr(self._inner, name)
+
+    def __call__(self, *a, **k):
+        self.calls += 1
+        return self._inner(*a, **k)
+
+
+@pytest.mark.parametrize("patched", ["on", "c2"], indirect=True)
+def test_cluster2_fp8_linears_run_on_library_kernels(patched):
+    """With fp8 QuantizedTensor weights, cluster 2 runs fc1 + SwiGLU, the per-token fp8
+    quantisation of act and fc2 + the gated residual on the library's fp8 GEMMs: comfy's fc1
+    and fc2 are never called, and the block's output equals, bit for bit, the same steps
+    done one kernel at a time (plain fp8 GEMM -> SwiGLU + per-token fp8 quant -> plain fp8
+    GEMM -> the stock gated residual)."""
+    from thor_int8_gemm_b200 import ops
+    m = patched
+    rt = m.DiTBlock.forward._t8g_runtime
+    blk, x, t, segs = _problem(m, S=300, d=256, ffn=512)
+    blk.mlp.fc1 = _CallCounter(blk.mlp.fc1)
+    blk.mlp.fc2 = _CallCounter(blk.mlp.fc2)
+    out = blk(x, t, segs, None)
+    assert not rt.broken
+    assert blk.mlp.fc1.calls == 0 and blk.mlp.fc2.calls == 0
+
+    # the same block, step by step
+    shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp = blk.adaln_proj(t)
+    rows = rt.row_map(segs, x.shape[0], x.device)
+    if rt.c1:
+        h1 = rt.norm_quant(blk.norm1, x, shift_msa, scale_msa, rows)
+    else:
+        h1 = m._mod_scale_shift(blk.norm1(x), shift_msa, scale_msa, segs)
+    x1 = m._mod_gate(x, gate_msa, blk.attn(h1), segs)
+    if rt.c1:
+        h2 = rt.norm_quant(blk.norm2, x1, shift_mlp, scale_mlp, rows)
+        a, a_s = h2.qdata, h2.params.scale.float().reshape(1).expand(x.shape[0]).contiguous()
+    else:
+        h2 = m._mod_scale_shift(blk.norm2(x1), shift_mlp, scale_mlp, segs)
+        a, a_s = ops.quant_rows(h2, "fp8_e4m3")
+    fc1, fc2 = blk.mlp.fc1._inner, blk.mlp.fc2._inner
+    w1 = fc1.weight
+    y = ops.gemm_dequant(a, w1.qdata, a_s, w1.params.scale.float().reshape(-1), fc1.bias)
+    q3, s3 = ops.swiglu_quant_fc1(y, kind="fp8_e4m3")
+    w2 = fc2.weight
+    z = ops.gemm_dequant(q3, w2.qdata, s3, w2.params.scale.float().reshape(-1), fc2.bias)
+    expect = m._mod_gate(x1, gate_mlp, z, segs)
+    assert torch.equal(out, expect)
+    # and the fused block stays close to comfy's stock block
+    stock = m.DiTBlock.forward.__wrapped__(blk, x, t, segs, None)
+    assert _rel(out, stock) < 0.02

@@ -186,8 +186,11 @@ def test_gemm_fp8_within_accumulation_tolerance(ops, path, M, N, K, dt):
     got = O.out_to_f32(out_bits(out), dt).astype(np.float64)
     ref = O.out_to_f32(O.gemm_fp8_dequant(aq, wq, xs, ws, bias, dt), dt).astype(np.float64)
     tol = O.fp8_gemm_tolerance(aq, wq, xs, ws, K)
-    ulp = {"bf16": 2.0 ** -8, "f16": 2.0 ** -11, "f32": 2.0 ** -24}[dt]
-    bound = tol * 1.01 + np.abs(ref) * ulp * 1.01 + 1e-30
+    # both sides are roundings to the output type of float32 values within tol: add one
+    # spacing of the output type at the larger magnitude
+    scale = {"bf16": 65536.0, "f16": 8192.0, "f32": 1.0}[dt]
+    spacing = np.spacing(np.maximum(np.abs(got), np.abs(ref)).astype(np.float32)).astype(np.float64) * scale
+    bound = tol * 1.01 + spacing + 1e-30
     assert np.all(np.abs(got - ref) <= bound), float(np.max(np.abs(got - ref) / bound))
 
 

@@ -186,94 +186,130 @@ def test_rms_mod_quant_config3_full_size(ops):
 
 @pytest.mark.parametrize("i", range(int(FUSED["n_rms"])))
 def test_fused_rms_mod_quant_vs_reference_golden(ops, i):
-    """The reference-signature fused_rms_mod_quant against the reference's own outputs."""
+    """The reference-signature fused_rms_mod_quant against the reference's own outputs:
+    h, res, the fp8 codes and the one scale, all bit for bit."""
     from thor_int8_gemm_b200.fused import fused_rms_mod_quant
     p = f"r{i}_"
     q, scale, h, res = fused_rms_mod_quant(bf16_dev(FUSED[p + "x"]), bf16_dev(FUSED[p + "w"]),
                                            bf16_dev(FUSED[p + "s"]), bf16_dev(FUSED[p + "b"]),
                                            float(FUSED[p + "eps"]))
-    assert bf16_ulp_diff(bits16(h), FUSED[p + "h"]).max() <= 1
-    assert bf16_ulp_diff(bits16(res), FUSED[p + "res"]).max() <= 1
-    # q is exact given this call's own h and scale
-    q_given = O.quantize_with_scale(O.bf16_to_f32(bits16(h)), scale.cpu().numpy(), O.QUANT_FP8)
-    np.testing.assert_array_equal(qbits(q, "fp8_e4m3"), q_given)
-    # and the oracle (same reduction tree) reproduces the whole call bit for bit
-    x = O.bf16_to_f32(FUSED[p + "x"])
-    w, s, b = (O.bf16_to_f32(FUSED[p + k]) for k in "wsb")
-    q_o, sc_o, h_o, res_o, _ = O.rms_mod_res_tensorwise(x, w, s, b, float(FUSED[p + "eps"]))
-    np.testing.assert_array_equal(bits16(h), h_o)
-    np.testing.assert_array_equal(bits16(res), res_o)
-    assert scale.item() == sc_o
-    np.testing.assert_array_equal(qbits(q, "fp8_e4m3"), q_o)
+    np.testing.assert_array_equal(bits16(h), FUSED[p + "h"])
+    np.testing.assert_array_equal(bits16(res), FUSED[p + "res"])
+    assert np.float32(scale.item()) == FUSED[p + "scale"][0]
+    np.testing.assert_array_equal(qbits(q, "fp8_e4m3"), FUSED[p + "q"])
 
 
 def test_tensorwise_segments_vs_reference_golden(ops):
     """The per-segment driver (src/ck_fused_patch.py:105-136): two batch segments,
-    s = bf16(1 + scale[row]), one global amax."""
+    s = bf16(1 + scale[row]), one global amax -- bit for bit."""
     x = bf16_dev(FUSED["seg_x"])
     S_seg = int(FUSED["seg_rows"])
     q, scale, h, res = ops.rms_mod_quant_tensorwise(x, bf16_dev(FUSED["seg_shift"]), bf16_dev(FUSED["seg_scale"]),
                                                     rows_per_mod=S_seg, eps=1e-6, kind="fp8_e4m3")
-    assert bf16_ulp_diff(bits16(h), FUSED["seg_h"]).max() <= 1
-    assert bf16_ulp_diff(bits16(res), FUSED["seg_res"]).max() <= 1
-    q_given, _ = O.quant_tensorwise_given(O.bf16_to_f32(bits16(h)), scale.item() * 448.0)
-    ref_scale = O.scale_from_amax(FUSED["seg_amax"][0], O.QUANT_FP8)
-    assert abs(scale.item() - float(ref_scale)) <= 2 * np.spacing(np.float32(ref_scale))
-    q_own = O.quantize_with_scale(O.bf16_to_f32(bits16(h)), np.float32(scale.item()), O.QUANT_FP8)
-    np.testing.assert_array_equal(qbits(q, "fp8_e4m3"), q_own)
+    np.testing.assert_array_equal(bits16(h), FUSED["seg_h"])
+    np.testing.assert_array_equal(bits16(res), FUSED["seg_res"])
+    assert np.float32(scale.item()) == O.scale_from_amax(FUSED["seg_amax"][0], O.QUANT_FP8)
+    np.testing.assert_array_equal(qbits(q, "fp8_e4m3"), FUSED["seg_q"])
+
+
+@pytest.mark.parametrize("kind", ["fp8_e4m3", "int8"])
+@pytest.mark.parametrize("S,D,n_mod,with_w", [(37, 256, 1, True), (64, 1000, 2, False), (300, 3072, 3, True),
+                                              (40, 5376, 2, True), (17, 8192, 1, False), (9, 8200, 2, True),
+                                              (6, 12288, 3, False), (3, 49152, 1, True)])
+def test_rms_mod_quant_tensorwise_bit_exact(ops, kind, S, D, n_mod, with_w):
+    """The tensorwise form (warp kernel for rows up to 16 KB, CTA kernel beyond) against
+    the oracle, whose sum of squares is the reference's order: h, res, the float32 amax
+    behind the one scale and every code, bit for bit, with per-token modulation rows."""
+    rng = np.random.default_rng(S * 7 + D)
+    x = O.round_bf16((rng.standard_normal((S, D)) * 1.5).astype(np.float32))
+    x[S // 2, : min(D, 16)] *= 40.0
+    x = O.round_bf16(x)
+    shift = O.round_bf16((rng.standard_normal((n_mod, D)) * 0.1).astype(np.float32))
+    scale = O.round_bf16((rng.standard_normal((n_mod, D)) * 0.1).astype(np.float32))
+    w = O.round_bf16((np.abs(rng.standard_normal(D)) + 0.5).astype(np.float32)) if with_w else None
+    mod_index = rng.integers(0, n_mod, S).astype(np.int32)
+    q, qs, h, res = ops.rms_mod_quant_tensorwise(
+        bf16_dev(to_bf16_bits(x)), bf16_dev(to_bf16_bits(shift)), bf16_dev(to_bf16_bits(scale)),
+        w=None if w is None else bf16_dev(to_bf16_bits(w)), mod_index=torch.from_numpy(mod_index).cuda(), eps=1e-6,
+        kind=kind)
+    s_rows = O.mod_multiplier(scale, False)[mod_index]
+    b_rows = shift[mod_index]
+    x32 = x.astype(np.float32)
+    inv = O.rms_inv(O.rms_sum_squares_reference(x32), D, 1e-6)
+    h_ref32 = O.rms_mod_h(x32, inv, w, s_rows, b_rows)
+    amax = np.float32(np.max(np.abs(h_ref32)))
+    h_ref = O.f32_to_bf16(h_ref32)
+    np.testing.assert_array_equal(bits16(h), h_ref)
+    np.testing.assert_array_equal(bits16(res), O.f32_to_bf16((h_ref32 + x32).astype(np.float32)))
+    q_ref, s_ref = O.quant_tensorwise_given(O.bf16_to_f32(h_ref), amax, KINDS[kind])
+    assert np.float32(qs.item()) == s_ref
+    np.testing.assert_array_equal(qbits(q, kind), q_ref)
 
 
 @pytest.mark.parametrize("kind", ["int8", "fp8_e4m3"])
 @pytest.mark.parametrize("M,F", [(8, 512), (33, 1536), (64, 12288), (5, 16384), (3, 24576)])
 def test_swiglu_quant_per_token(ops, kind, M, F):
+    """act, the scales and the codes bit for bit against the oracle (exact sigmoid)."""
     rng = np.random.default_rng(M * F)
     y = O.round_bf16(rng.standard_normal((M, 2 * F)).astype(np.float32) * 2)
     y[0, :8] = [-100.0, -30.0, -0.0, 0.0, 30.0, 88.0, 1e-30, -1e-30]
     y = O.round_bf16(y)
     yd = bf16_dev(to_bf16_bits(y))
     q, qs, act = ops.swiglu_quant_fc1(yd, kind=kind, return_act=True)
-    _, _, act_ref = O.swiglu_quant_per_token(y[:, :F], y[:, F:], KINDS[kind])
-    # act within one bf16 ulp of the oracle (the kernel's exp differs from numpy's)
-    assert bf16_ulp_diff(bits16(act), act_ref).max() <= 1
-    # q and the scales are exact given the kernel's own act
-    q_given, qs_given = O.quant_rows(O.bf16_to_f32(bits16(act)), KINDS[kind])
-    np.testing.assert_array_equal(qs.cpu().numpy(), qs_given)
-    np.testing.assert_array_equal(qbits(q, kind), q_given)
+    q_ref, qs_ref, act_ref = O.swiglu_quant_per_token(y[:, :F], y[:, F:], KINDS[kind])
+    np.testing.assert_array_equal(bits16(act), act_ref)
+    np.testing.assert_array_equal(qs.cpu().numpy(), qs_ref)
+    np.testing.assert_array_equal(qbits(q, kind), q_ref)
 
 
-def test_swiglu_every_finite_bf16_gate(ops):
-    """act for every finite bf16 gate value (subnormals, the window g < -87.3 where
-    1 / (1 + e^-g) is subnormal, g < -88.7 where e^-g overflows, and the largest
-    magnitudes) times four up values, within one bf16 ulp of the oracle; q exact given act."""
+def test_swiglu_every_bf16_gate(ops):
+    """act for every bf16 gate value -- subnormals, the window -88.7 < g < -87.3 where the
+    sigmoid is subnormal, g < -88.7 where exp(-g) overflows, the table's edges at
+    |g| = 2^-25 and 128, the largest magnitudes, infinities and NaNs -- times four up
+    values, bit for bit against the oracle (NaN for NaN); the codes too."""
     bits = np.arange(65536, dtype=np.uint32).astype(np.uint16)
-    finite = bits[(bits & 0x7F80) != 0x7F80]
     F = 2048
-    g = np.zeros(-(-finite.size // F) * F, np.uint16)
-    g[: finite.size] = finite
-    g = g.reshape(-1, F)
+    g = bits.reshape(-1, F)
     ups = np.array([0.5, -1.0, 1e-3, -0.75], np.float32)
     gate = np.concatenate([g] * len(ups))
     up = np.repeat(ups, g.shape[0])[:, None] * np.ones((1, F), np.float32)
     y = np.concatenate([gate, O.f32_to_bf16(up)], axis=1)
-    q, qs, act = ops.swiglu_quant_fc1(bf16_dev(y), kind="int8", return_act=True)
-    _, _, act_ref = O.swiglu_quant_per_token(O.bf16_to_f32(gate), O.round_bf16(up), O.QUANT_INT8)
-    assert bf16_ulp_diff(bits16(act), act_ref).max() <= 1
-    q_given, qs_given = O.quant_rows(O.bf16_to_f32(bits16(act)), O.QUANT_INT8)
-    np.testing.assert_array_equal(qs.cpu().numpy(), qs_given)
-    np.testing.assert_array_equal(qbits(q, "int8"), q_given)
+    _, _, act = ops.swiglu_quant_fc1(bf16_dev(y), kind="int8", return_act=True)
+    act_ref = O.f32_to_bf16(O.silu_mul(O.bf16_to_f32(gate), O.round_bf16(up)))
+    got = bits16(act)
+    nan_ref = np.isnan(O.bf16_to_f32(act_ref))
+    np.testing.assert_array_equal(np.isnan(O.bf16_to_f32(got)), nan_ref)
+    np.testing.assert_array_equal(got[~nan_ref], act_ref[~nan_ref])
+    # the quantiser end to end on the finite gates
+    fin = (bits & 0x7F80) != 0x7F80
+    gf = np.zeros(-(-int(fin.sum()) // F) * F, np.uint16)
+    gf[: fin.sum()] = bits[fin]
+    gf = gf.reshape(-1, F)
+    yf = np.concatenate([np.concatenate([gf] * 2), O.f32_to_bf16(np.repeat(ups[:2], gf.shape[0])[:, None]
+                                                                   * np.ones((1, F), np.float32))], axis=1)
+    q, qs, _ = ops.swiglu_quant_fc1(bf16_dev(yf), kind="int8", return_act=True)
+    q_ref, qs_ref, _ = O.swiglu_quant_per_token(O.bf16_to_f32(yf[:, :F]), O.bf16_to_f32(yf[:, F:]), O.QUANT_INT8)
+    np.testing.assert_array_equal(qs.cpu().numpy(), qs_ref)
+    np.testing.assert_array_equal(qbits(q, "int8"), q_ref)
 
 
 def test_swiglu_quant_config2_shape(ops):
-    """[32768, 24576] fc1 output -> SwiGLU + per-token int8 [32768, 12288], read in place."""
+    """[32768, 24576] fc1 output -> SwiGLU + per-token int8 [32768, 12288], read in place:
+    act, scales and codes of 256 sampled rows (tile and tail edges included) bit for bit
+    against the oracle -- zero mismatches -- and every row's codes exact given its act."""
     M, F = 32768, 12288
     g = torch.Generator().manual_seed(7)
     y = torch.randn(M, 2 * F, generator=g).to(torch.bfloat16)
     q, qs, act = ops.swiglu_quant_fc1(y.cuda(), kind="int8", return_act=True)
-    rows = np.array([0, 1, 4097, M - 1])
+    rng = np.random.default_rng(8)
+    rows = np.unique(np.concatenate([[0, 1, 127, 128, 4097, M - 2, M - 1], rng.integers(0, M, 249)]))
     yr = y[torch.from_numpy(rows)].float().numpy()
-    _, _, act_ref = O.swiglu_quant_per_token(yr[:, :F], yr[:, F:], O.QUANT_INT8)
-    act_r = bits16(act[torch.from_numpy(rows).cuda()])
-    assert bf16_ulp_diff(act_r, act_ref).max() <= 1
+    q_ref, qs_ref, act_ref = O.swiglu_quant_per_token(yr[:, :F], yr[:, F:], O.QUANT_INT8)
+    sel = torch.from_numpy(rows).cuda()
+    act_r = bits16(act[sel])
+    assert int((act_r != act_ref).sum()) == 0, f"{int((act_r != act_ref).sum())} act mismatches"
+    np.testing.assert_array_equal(qs[sel].cpu().numpy(), qs_ref)
+    np.testing.assert_array_equal(qbits(q[sel], "int8"), q_ref)
     act_all, qh, qsh = bits16(act), qbits(q, "int8"), qs.cpu().numpy()
     for r0 in range(0, M, 4096):
         q_given, qs_given = O.quant_rows(O.bf16_to_f32(act_all[r0:r0 + 4096]), O.QUANT_INT8)
@@ -283,14 +319,28 @@ def test_swiglu_quant_config2_shape(ops):
 
 @pytest.mark.parametrize("i", range(int(FUSED["n_swiglu"])))
 def test_fused_swiglu_quant_vs_reference_golden(ops, i):
+    """The reference-signature fused_swiglu_quant against the reference's own outputs:
+    act, the one scale and every fp8 code bit for bit."""
     from thor_int8_gemm_b200.fused import fused_swiglu_quant
     p = f"s{i}_"
     q, scale, act = fused_swiglu_quant(bf16_dev(FUSED[p + "gate"]), bf16_dev(FUSED[p + "up"]))
-    assert bf16_ulp_diff(bits16(act), FUSED[p + "act"]).max() <= 1
-    ref_scale = FUSED[p + "scale"][0]
-    assert abs(scale.item() - float(ref_scale)) <= 4 * np.spacing(np.float32(ref_scale))
-    q_own = O.quantize_with_scale(O.bf16_to_f32(bits16(act)), np.float32(scale.item()), O.QUANT_FP8)
-    np.testing.assert_array_equal(qbits(q, "fp8_e4m3"), q_own)
+    np.testing.assert_array_equal(bits16(act), FUSED[p + "act"])
+    assert np.float32(scale.item()) == FUSED[p + "scale"][0]
+    np.testing.assert_array_equal(qbits(q, "fp8_e4m3"), FUSED[p + "q"])
+
+
+def test_swiglu_tensorwise_long_rows_vs_oracle(ops):
+    """The tensorwise SwiGLU over rows that take the generic kernel and two row groups per
+    CTA, against the oracle: act, the float32 amax behind the scale, every code."""
+    rng = np.random.default_rng(21)
+    for M, F in ((50, 12288), (7, 24576), (300, 1536)):
+        gate = O.round_bf16((rng.standard_normal((M, F)) * 3).astype(np.float32))
+        up = O.round_bf16(rng.standard_normal((M, F)).astype(np.float32))
+        q, qs, act = ops.swiglu_quant_tensorwise(bf16_dev(to_bf16_bits(gate)), bf16_dev(to_bf16_bits(up)))
+        q_ref, s_ref, act_ref, _ = O.swiglu_tensorwise(gate, up)
+        np.testing.assert_array_equal(bits16(act), act_ref)
+        assert np.float32(qs.item()) == s_ref
+        np.testing.assert_array_equal(qbits(q, "fp8_e4m3"), q_ref)
 
 
 def test_row_kernels_reject_bad_shapes(ops):

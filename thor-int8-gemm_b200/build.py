@@ -21,8 +21,12 @@ CSRC = os.path.join(HERE, "csrc")
 LIB_NAME = "libthor_int8_gemm_b200.so"
 LIB_PATH = os.path.join(HERE, LIB_NAME)
 SOURCES = [os.path.join(CSRC, "t8g.cu")]
+# generated at build time: the SwiGLU kernels' sigmoid table (csrc/sigmoid_table.c)
+GEN_DIR = os.path.join(HERE, "_build")
+SIGMOID_GEN_SOURCE = os.path.join(CSRC, "sigmoid_table.c")
+SIGMOID_TABLE = os.path.join(GEN_DIR, "sigmoid_table.inc")
 DEPENDS = SOURCES + [os.path.join(CSRC, f) for f in sorted(os.listdir(CSRC)) if f.endswith(".cuh")] + [
-    os.path.join(ROOT, "include", "thor_int8_gemm_b200.h")]
+    os.path.join(ROOT, "include", "thor_int8_gemm_b200.h"), SIGMOID_GEN_SOURCE]
 
 EXT_SOURCE = os.path.join(CSRC, "capsule.c")
 EXT_PATH = os.path.join(HERE, "_t8g_capsule" + sysconfig.get_config_var("EXT_SUFFIX"))
@@ -43,6 +47,28 @@ def nvcc_path() -> str:
     raise RuntimeError("nvcc not found (set NVCC or put CUDA's bin on PATH)")
 
 
+def c_compiler() -> str:
+    return os.environ.get("CC") or shutil.which("gcc") or "cc"
+
+
+def generate_sigmoid_table(path: str = SIGMOID_TABLE) -> str:
+    """Compile and run csrc/sigmoid_table.c, writing the table's initialiser list to `path`."""
+    os.makedirs(os.path.dirname(path), exist_ok=True)
+    exe = os.path.join(os.path.dirname(path), "sigmoid_table_gen")
+    cmd = [c_compiler(), "-O2", "-std=c11", "-o", exe, SIGMOID_GEN_SOURCE, "-lm"]
+    proc = subprocess.run(cmd, capture_output=True, text=True)
+    if proc.returncode != 0:
+        sys.stderr.write(proc.stdout + proc.stderr)
+        raise RuntimeError(f"compiling {os.path.basename(SIGMOID_GEN_SOURCE)} failed ({proc.returncode})")
+    tmp = path + ".tmp"
+    proc = subprocess.run([exe, tmp], capture_output=True, text=True)
+    if proc.returncode != 0:
+        sys.stderr.write(proc.stdout + proc.stderr)
+        raise RuntimeError(f"sigmoid table generator failed ({proc.returncode})")
+    os.replace(tmp, path)
+    return path
+
+
 def up_to_date() -> bool:
     if not os.path.exists(LIB_PATH):
         return False
@@ -55,7 +81,7 @@ def build_ext(force: bool = False) -> str:
     deps = [EXT_SOURCE, LIB_PATH, os.path.join(ROOT, "include", "thor_int8_gemm_b200.h")]
     if not force and os.path.exists(EXT_PATH) and all(os.path.getmtime(p) <= os.path.getmtime(EXT_PATH) for p in deps):
         return EXT_PATH
-    cc = os.environ.get("CC") or shutil.which("gcc") or "cc"
+    cc = c_compiler()
     tmp = EXT_PATH + ".tmp"
     cmd = [cc, "-O2", "-shared", "-fPIC", "-std=c11", "-I" + sysconfig.get_paths()["include"], "-o", tmp, EXT_SOURCE,
            "-L" + HERE, "-lthor_int8_gemm_b200", "-Wl,-rpath,$ORIGIN"]
@@ -73,8 +99,9 @@ def build(force: bool = False, verbose: bool = False) -> str:
     if not force and up_to_date():
         build_ext()
         return LIB_PATH
+    generate_sigmoid_table()
     tmp = LIB_PATH + ".tmp"
-    cmd = [nvcc_path(), *NVCC_FLAGS, "-o", tmp, *SOURCES]
+    cmd = [nvcc_path(), *NVCC_FLAGS, "-I" + GEN_DIR, "-o", tmp, *SOURCES]
     proc = subprocess.run(cmd, capture_output=True, text=True)
     log_path = os.path.join(HERE, "build.log")
     with open(log_path, "w") as f:

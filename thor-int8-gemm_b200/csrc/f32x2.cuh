@@ -1,5 +1,5 @@
-// Packed fp32 / bf16 helpers and the SiLU shared by the row kernels and the GEMM's
-// SwiGLU epilogue (the same operations in the same order, so both give the same bits).
+// Packed fp32 / bf16 helpers shared by the row kernels and the GEMM epilogues (the same
+// operations in the same order, so both give the same bits).
 #pragma once
 
 #include <cuda_bf16.h>
@@ -54,39 +54,6 @@ __device__ __forceinline__ float2 add_f32_f16x2(float2 p, uint32_t b) {
       : "=f"(x), "=f"(y)
       : "r"(b), "f"(p.x), "f"(p.y));
   return make_float2(x, y);
-}
-
-// act = (g * sigmoid(g)) * u with sigmoid(g) = 1 / (1 + e^-g), in fp32 with the fast
-// hardware exponential and reciprocal (act is compared with the oracle within one bf16
-// ulp):
-//   e   = 2^(-g * log2(e))              ex2.approx.ftz (the change-of-base identity)
-//   d4  = (1 + e) / 4                   one fma: RN(1 + e) scaled exactly by 1/4
-//   r4  = approx(1 / d4) = 4 / (1 + e)  rcp.approx.ftz
-//   act = ((g / 4) * r4) * u            g / 4 is exact for every bf16 g
-// The quarter scaling keeps the reciprocal normal where 1 / (1 + e) itself would be
-// subnormal (g < -87.3: 2^-126 < 4 / (1 + e)), so flushing subnormal reciprocals cannot
-// change act; (g / 4) * r4 is the same real product as g * (1 / (1 + e)).  For e = inf
-// (g < -88.7) r4 = 0 and act is a signed zero, as in fp32 with an IEEE reciprocal.
-__device__ __forceinline__ float ex2_approx(float x) {
-  float r;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
-  return r;
-}
-__device__ __forceinline__ float rcp_approx_ftz(float x) {
-  float r;
-  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
-  return r;
-}
-
-constexpr float kLog2E = 1.44269504088896340736f;
-
-// g4 = g / 4 (exact), u: one packed pair of gate / up values.
-__device__ __forceinline__ float2 silu_mul2(float2 g4, float2 u) {
-  const float2 t = mul2_rn(g4, make_float2(-4.0f * kLog2E, -4.0f * kLog2E));   // = -g * log2(e), same rounding
-  const float2 e = make_float2(ex2_approx(t.x), ex2_approx(t.y));
-  const float2 d4 = fma2_rn(e, make_float2(0.25f, 0.25f), make_float2(0.25f, 0.25f));
-  const float2 r4 = make_float2(rcp_approx_ftz(d4.x), rcp_approx_ftz(d4.y));
-  return mul2_rn(mul2_rn(g4, r4), u);
 }
 
 }  // namespace t8g

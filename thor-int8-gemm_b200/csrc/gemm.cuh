@@ -25,6 +25,7 @@
 
 #include "f32x2.cuh"
 #include "ptx.cuh"
+#include "sigmoid.cuh"
 
 namespace t8g {
 namespace gemm {
@@ -723,16 +724,16 @@ __device__ __forceinline__ void epilogue_tile_staged64(const Args& args, const C
 
 // SwiGLU epilogue of one 32-row slice: tile columns [0, 128) are gate and [128, 256) the
 // matching up columns.  Each value is dequantised and rounded to bf16 exactly as the plain
-// epilogue stores it, then act = silu(gate) * up with the row kernels' SiLU (f32x2.cuh),
-// rounded to bf16 and stored at act columns [n_tile0 / 2, n_tile0 / 2 + 128).
+// epilogue stores it, then act = (g * sigmoid(g)) * u with the row kernel's exact sigmoid
+// (sigmoid.cuh, table `sig` in shared memory), rounded to bf16 and stored at act columns
+// [n_tile0 / 2, n_tile0 / 2 + 128).
 template <int IN, int EPB>
 __device__ __forceinline__ void epilogue_tile_swiglu(const Args& args, const CUtensorMap* tm_out,
                                                      uint8_t (*bufs)[EPB], int& ebuf, uint32_t t_row, int row0,
                                                      int n_tile0, int lane, uint64_t pol_out, float xs_r,
-                                                     const TileParams& tp) {
+                                                     const TileParams& tp, const uint32_t* sig) {
   const bool has_bias = args.bias != nullptr;
   const float2 xs2 = make_float2(xs_r, xs_r);
-  const float2 quarter = make_float2(0.25f, 0.25f);
   constexpr int kChunks = BN / 2 / EPI_COLS;
   uint32_t rg[32], ru[32];
   tmem_ld_32x32b_x32(t_row, rg);
@@ -770,8 +771,7 @@ __device__ __forceinline__ void epilogue_tile_swiglu(const Args& args, const CUt
         g = add_f32_bf16x2(g, bg[p]);
         u = add_f32_bf16x2(u, bu[p]);
       }
-      // g / 4 is exact for a bf16 g
-      act[p] = f2_to_bf2(silu_mul2(mul2_rn(bf2_to_f2(f2_to_bf2(g)), quarter), bf2_to_f2(f2_to_bf2(u))));
+      act[p] = f2_to_bf2(silu_mul2(f2_to_bf2(g), bf2_to_f2(f2_to_bf2(u)), sig));
     }
     if (lane == 0) bulk_wait_group_read<1>();
     __syncwarp();
@@ -835,15 +835,17 @@ struct PairCfg {
   // instead of the staging buffers, and keeps four stages to make room for them
   static constexpr int kStages = OUT == kOutGated ? 4 : 5;
   static constexpr int kResBytes = OUT == kOutGated ? 4 * 32 * 128 : 16;
+  static constexpr int kSigEntries = OUT == kOutSwiglu ? kSigmoidEntries : 4;
 };
 
-template <int STAGES, int EPB, int RESB, int BBYTES = P_B_BYTES>
+template <int STAGES, int EPB, int RESB, int BBYTES = P_B_BYTES, int SIGN = 4>
 struct SmemPair {
   uint8_t a[STAGES][P_A_BYTES];
   uint8_t b[STAGES][BBYTES];
   alignas(1024) uint8_t epi[EPI_WARPS][2][EPB];
   alignas(1024) uint8_t res[EPI_WARPS][RESB];        // kOutGated: residual / output chunks
   uint8_t gate[EPI_WARPS][RESB > 16 ? 512 : 16];     // kOutGated: a shared gate row
+  alignas(16) uint32_t sig[SIGN];                    // kOutSwiglu: the sigmoid table
   TileParams params[2];   // channel parameters of the tile in each accumulator
   uint64_t full[STAGES];
   uint64_t empty[STAGES];
@@ -854,11 +856,11 @@ struct SmemPair {
 };
 template <int OUT, int TBN = BN>
 using SmemPairOf = SmemPair<PairCfg<OUT, TBN>::kStages, PairCfg<OUT, TBN>::kEpiBytes, PairCfg<OUT, TBN>::kResBytes,
-                            PairCfg<OUT, TBN>::kBBytes>;
+                            PairCfg<OUT, TBN>::kBBytes, PairCfg<OUT, TBN>::kSigEntries>;
 template <int OUT, int TBN = BN>
 constexpr size_t pair_smem_bytes() { return sizeof(SmemPairOf<OUT, TBN>) + 1024; }   // + slack to align to 1024 B
 static_assert(pair_smem_bytes<kOutBF16>() <= 227 * 1024 && pair_smem_bytes<kOutF32>() <= 227 * 1024 &&
-                  pair_smem_bytes<kOutGated>() <= 227 * 1024,
+                  pair_smem_bytes<kOutGated>() <= 227 * 1024 && pair_smem_bytes<kOutSwiglu>() <= 227 * 1024,
               "pair kernel shared memory exceeds the per-CTA limit");
 
 template <int IN, int OUT, int TBN = BN>
@@ -1013,6 +1015,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     tempty_bar[1] = mapa_shared(smem_u32(&s.tmem_empty[1]), 0);
     int local = 0;
     int ebuf = 0;
+    // the sigmoid table; the first tile's named barrier orders these writes before any read
+    if constexpr (OUT == kOutSwiglu) load_sigmoid_table(s.sig, e, 128);
     for (int tile = pair; tile < num_tiles; tile += npairs, ++local) {
       const int tm = tile / tiles_n;
       const int tn = tile - tm * tiles_n;
@@ -1038,7 +1042,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
                                   s.params[acc]);
         else if constexpr (OUT == kOutSwiglu)
           epilogue_tile_swiglu<IN, Cfg::kEpiBytes>(args, &tm_out, s.epi[ew], ebuf, t_row, row0, tn * TBN, lane, pol_out,
-                                                   xs_r, s.params[acc]);
+                                                   xs_r, s.params[acc], s.sig);
         else if constexpr (Cfg::kEpiCols == 64)
           epilogue_tile_staged64<IN, OUT, Cfg::kEpiBytes, TBN>(args, &tm_out, s.epi[ew], ebuf, t_row, row0, tn * TBN,
                                                                lane, pol_out, xs_r, s.params[acc]);

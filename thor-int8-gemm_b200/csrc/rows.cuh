@@ -31,6 +31,7 @@
 
 #include "f32x2.cuh"
 #include "ptx.cuh"
+#include "sigmoid.cuh"
 
 namespace t8g {
 namespace rows {
@@ -149,32 +150,54 @@ __device__ __forceinline__ void unpack_pairs(const uint4& u, float2 (&v)[4]) {
 }
 
 
+// ---------------------------------------------------------------- row groups
+// A CTA-per-row kernel runs `count` independent row groups of T threads each (a multiple of
+// 32); each group has its own ring and synchronises on its own named barrier (1 + index),
+// so two rows are in flight per CTA without a CTA-wide barrier (the SwiGLU kernel shares
+// one sigmoid table between its groups this way).
+struct RowGroup {
+  int index;   // group within the CTA
+  int count;   // groups per CTA
+  int T;       // threads of the group
+  int t;       // this thread's index within the group
+};
+
+__device__ __forceinline__ RowGroup row_group(int T) {
+  RowGroup g;
+  g.T = T;
+  g.index = static_cast<int>(threadIdx.x) / T;
+  g.count = static_cast<int>(blockDim.x) / T;
+  g.t = static_cast<int>(threadIdx.x) - g.index * T;
+  return g;
+}
+__device__ __forceinline__ void group_sync(const RowGroup& g) { named_bar_sync(1 + g.index, g.T); }
+__device__ __forceinline__ bool group_any(const RowGroup& g, bool v) { return named_bar_any(1 + g.index, g.T, v); }
+
 // ---------------------------------------------------------------- block reductions
-// The CTA is one row group of blockDim.x (a multiple of 32) threads; `red` holds one
-// float per warp.  Canonical order: butterfly within each warp, then the warp
-// partials added (or maxed) left to right.
-__device__ __forceinline__ float block_sum(float v, float* red) {
+// A row group of T threads; `red` holds one float per warp of the group.  Canonical order:
+// butterfly within each warp, then the warp partials added (or maxed) left to right.
+__device__ __forceinline__ float block_sum(const RowGroup& grp, float v, float* red) {
 #pragma unroll
   for (int off = 16; off >= 1; off >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xFFFFFFFFu, v, off));
-  const int nw = blockDim.x >> 5;
+  const int nw = grp.T >> 5;
   if (nw == 1) return v;
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
-  __syncthreads();
+  if ((grp.t & 31) == 0) red[grp.t >> 5] = v;
+  group_sync(grp);
   float t = red[0];
   for (int i = 1; i < nw; ++i) t = __fadd_rn(t, red[i]);
   return t;
 }
 
-// Max of non-negative values over the CTA (order-free: every lane of every warp
+// Max of non-negative values over the row group (order-free: every lane of every warp
 // folds the warp partials with one more butterfly).
-__device__ __forceinline__ float block_max(float v, float* red) {
+__device__ __forceinline__ float block_max(const RowGroup& grp, float v, float* red) {
 #pragma unroll
   for (int off = 16; off >= 1; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xFFFFFFFFu, v, off));
-  const int nw = blockDim.x >> 5;
+  const int nw = grp.T >> 5;
   if (nw == 1) return v;
-  const int lane = threadIdx.x & 31;
-  if (lane == 0) red[threadIdx.x >> 5] = v;
-  __syncthreads();
+  const int lane = grp.t & 31;
+  if (lane == 0) red[grp.t >> 5] = v;
+  group_sync(grp);
   float t = lane < nw ? red[lane] : 0.f;
 #pragma unroll
   for (int off = 16; off >= 1; off >>= 1) t = fmaxf(t, __shfl_xor_sync(0xFFFFFFFFu, t, off));
@@ -195,16 +218,32 @@ __device__ __forceinline__ void flush_amax(float* amax, float m) {
 }
 
 // ---------------------------------------------------------------- row ring
-// Shared-memory layout of every row kernel: mbarriers, reduction scratch, then
-// `stages` slots of `slot_bytes` (1024-byte aligned).
+// Shared-memory layout of a row group: mbarriers, reduction scratch, then `stages` slots of
+// `slot_bytes` (1024-byte aligned).
 struct RingGeom {
   int stages;          // slots in the ring (>= 2)
   uint32_t slot_bytes; // bytes of one slot (one row, or gate row + up row)
-  uint32_t part_bytes; // bytes of one bulk copy (a row of one operand)
-  int parts;           // bulk copies per slot (1, or 2 for gate + up)
+  uint32_t part_bytes; // bytes of one operand row
+  int parts;           // operand rows per slot (1, or 2 for gate + up)
+  int padded;          // rows copied in 256-byte pieces at kPiecePitch (see below)
 };
 constexpr int kRingHeader = 1024;   // barriers (<= 16 x 8 B), reductions (2 x 32 floats)
 constexpr int kMaxStages = 16;
+
+// Padded row layout: the row is copied in 256-byte pieces (128 bf16 values) placed
+// kPiecePitch bytes apart, so that reads of the same offset in 16 consecutive pieces (the
+// reference-order reduction's leaf-major pass) fall in distinct banks, while reads of
+// consecutive 16-byte vectors (every other pass) stay conflict-free.
+constexpr uint32_t kPieceBytes = 256;
+constexpr uint32_t kPiecePitch = 272;
+
+__host__ __device__ constexpr uint32_t padded_row_bytes(uint32_t row_bytes) {
+  return ((row_bytes + kPieceBytes - 1) / kPieceBytes) * kPiecePitch;
+}
+// Shared-memory byte offset of 16-byte vector c of a padded row.
+__device__ __forceinline__ uint32_t padded_vec(int c) {
+  return static_cast<uint32_t>(c >> 4) * kPiecePitch + static_cast<uint32_t>(c & 15) * 16u;
+}
 
 struct RingState {
   uint64_t* full;
@@ -222,13 +261,31 @@ __device__ __forceinline__ RingState ring_state(uint8_t* smem) {
   return r;
 }
 
-// Issue the bulk copies of row `row` into slot `st` (one thread).
+// Issue the copies of one operand row of `bytes` into `dst` (all lanes of one warp; the
+// mbarrier's expected bytes are registered separately): one bulk copy from lane 0, or the
+// row's 256-byte pieces spread over the lanes in the padded layout.
+__device__ __forceinline__ void issue_row_copies(uint8_t* dst, const void* src, uint32_t bytes, bool padded,
+                                                 uint64_t* bar, int lane, uint64_t policy) {
+  if (!padded) {
+    if (lane == 0) bulk_load(dst, src, bytes, bar, policy);
+    return;
+  }
+  const uint32_t pieces = (bytes + kPieceBytes - 1) / kPieceBytes;
+  for (uint32_t p = static_cast<uint32_t>(lane); p < pieces; p += 32) {
+    const uint32_t off = p * kPieceBytes;
+    const uint32_t n = bytes - off < kPieceBytes ? bytes - off : kPieceBytes;
+    bulk_load(dst + p * kPiecePitch, static_cast<const uint8_t*>(src) + off, n, bar, policy);
+  }
+}
+
+// Issue the copies of row `row` into slot `st` (every lane of the group's first warp).
 __device__ __forceinline__ void ring_issue(const RingState& rs, const RingGeom& g, int st, const void* src0,
-                                           const void* src1, uint64_t policy) {
+                                           const void* src1, uint64_t policy, int lane) {
   uint8_t* dst = rs.slots + static_cast<size_t>(st) * g.slot_bytes;
-  mbar_arrive_expect_tx(&rs.full[st], g.part_bytes * static_cast<uint32_t>(g.parts));
-  bulk_load(dst, src0, g.part_bytes, &rs.full[st], policy);
-  if (g.parts == 2) bulk_load(dst + g.part_bytes, src1, g.part_bytes, &rs.full[st], policy);
+  if (lane == 0) mbar_arrive_expect_tx(&rs.full[st], g.part_bytes * static_cast<uint32_t>(g.parts));
+  const uint32_t stride = g.padded ? padded_row_bytes(g.part_bytes) : g.part_bytes;
+  issue_row_copies(dst, src0, g.part_bytes, g.padded, &rs.full[st], lane, policy);
+  if (g.parts == 2) issue_row_copies(dst + stride, src1, g.part_bytes, g.padded, &rs.full[st], lane, policy);
 }
 
 // ---------------------------------------------------------------- kernel arguments
@@ -280,25 +337,31 @@ struct SwigluArgs {
 };
 
 // ---------------------------------------------------------------- common loop
-// Runs `body(row, slot_ptr, ring)` for rows blockIdx.x, blockIdx.x + gridDim.x, ...
-// with the ring kept `stages - 1` rows ahead.  `src(row, part)` gives the
-// global address of a row operand.  Returns after draining in-flight copies.
+// Runs `body(row, slot_ptr, ring)` for the rows of row group `grp`: rows
+// blockIdx.x * count + index, then every gridDim.x * count rows, with the ring kept
+// `stages - 1` rows ahead.  `src(row, part)` gives the global address of a row operand.
+// `smem` is the group's own region (header + slots).  Returns after draining in-flight
+// copies.
 template <typename Src, typename Body>
-__device__ __forceinline__ void row_loop(uint8_t* smem, const RingGeom& g, int64_t nrows, Src src, Body body) {
+__device__ __forceinline__ void row_loop(uint8_t* smem, const RingGeom& g, const RowGroup& grp, int64_t nrows,
+                                         Src src, Body body) {
   RingState rs = ring_state(smem);
   const uint64_t policy = policy_evict_first();
-  const int64_t G = gridDim.x;
-  if (threadIdx.x == 0) {
+  const int64_t G = static_cast<int64_t>(gridDim.x) * grp.count;
+  const int64_t first = static_cast<int64_t>(blockIdx.x) * grp.count + grp.index;
+  const bool issuer = grp.t < 32;   // the group's first warp issues the copies
+  const int lane = grp.t & 31;
+  if (grp.t == 0) {
     for (int i = 0; i < g.stages; ++i) mbar_init(&rs.full[i], 1);
     fence_mbarrier_init();
   }
-  __syncthreads();
-  int64_t issued = 0;   // meaningful in thread 0 only
-  if (threadIdx.x == 0) {
+  group_sync(grp);
+  int64_t issued = 0;   // meaningful in the first warp only
+  if (issuer) {
     for (int i = 0; i < g.stages; ++i) {
-      const int64_t r = blockIdx.x + i * G;
+      const int64_t r = first + i * G;
       if (r >= nrows) break;
-      ring_issue(rs, g, i, src(r, 0), src(r, 1), policy);
+      ring_issue(rs, g, i, src(r, 0), src(r, 1), policy, lane);
       ++issued;
     }
   }
@@ -307,14 +370,14 @@ __device__ __forceinline__ void row_loop(uint8_t* smem, const RingGeom& g, int64
   int st = 0, prev = g.stages - 1;
   uint32_t ph = 0;
   const int64_t ahead = static_cast<int64_t>(g.stages - 1) * G;   // row k-1+stages = row + ahead
-  for (int64_t row = blockIdx.x; row < nrows; row += G, ++k) {
+  for (int64_t row = first; row < nrows; row += G, ++k) {
     const bool ok = mbar_wait(&rs.full[st], ph, kStatusTimeoutProducer);
-    if (__syncthreads_or(!ok)) break;
-    // every thread is past row k-1: refill its slot with row k-1+stages
-    if (threadIdx.x == 0 && k > 0) {
+    if (group_any(grp, !ok)) break;
+    // every thread of the group is past row k-1: refill its slot with row k-1+stages
+    if (issuer && k > 0) {
       const int64_t r = row + ahead;
       if (r < nrows) {
-        ring_issue(rs, g, prev, src(r, 0), src(r, 1), policy);
+        ring_issue(rs, g, prev, src(r, 0), src(r, 1), policy, lane);
         ++issued;
       }
     }
@@ -326,7 +389,7 @@ __device__ __forceinline__ void row_loop(uint8_t* smem, const RingGeom& g, int64
     }
   }
   // teardown: copies still in flight (only after an abort) must land before exit
-  if (threadIdx.x == 0) {
+  if (grp.t == 0) {
     for (int64_t n = k; n < issued; ++n) {
       if (!mbar_wait(&rs.full[st], ph, kStatusTimeoutDrain)) break;
       if (++st == g.stages) {
@@ -368,9 +431,10 @@ template <int V, int QK>
 __global__ void __launch_bounds__(512) quant_rows_kernel(const QuantRowsArgs a, const RingGeom g) {
   extern __shared__ __align__(1024) uint8_t smem[];
   const int T = blockDim.x;
+  const RowGroup grp = row_group(T);
   const int nvec = a.D >> 3;
   auto src = [&](int64_t r, int) -> const void* { return a.x + r * a.ld_x; };
-  row_loop(smem, g, a.S, src, [&](int64_t row, const uint8_t* slot, const RingState& rs) {
+  row_loop(smem, g, grp, a.S, src, [&](int64_t row, const uint8_t* slot, const RingState& rs) {
     uint8_t* qrow = static_cast<uint8_t*>(a.q) + row * a.ld_q;
     uint32_t m2 = 0;
     if constexpr (V > 0) {
@@ -381,7 +445,7 @@ __global__ void __launch_bounds__(512) quant_rows_kernel(const QuantRowsArgs a, 
         xv[i] = c < nvec ? lds_v4(slot + 16 * c) : make_uint4(0, 0, 0, 0);
         m2 = absmax4(m2, xv[i]);
       }
-      const QuantRow qr = quant_row<QK>(block_max(pair_max(m2), rs.red_max));
+      const QuantRow qr = quant_row<QK>(block_max(grp, pair_max(m2), rs.red_max));
       if (threadIdx.x == 0) a.q_scale[row] = qr.scale;
 #pragma unroll
       for (int i = 0; i < V; ++i) {
@@ -390,7 +454,7 @@ __global__ void __launch_bounds__(512) quant_rows_kernel(const QuantRowsArgs a, 
       }
     } else {
       for (int c = threadIdx.x; c < nvec; c += T) m2 = absmax4(m2, lds_v4(slot + 16 * c));
-      const QuantRow qr = quant_row<QK>(block_max(pair_max(m2), rs.red_max));
+      const QuantRow qr = quant_row<QK>(block_max(grp, pair_max(m2), rs.red_max));
       if (threadIdx.x == 0) a.q_scale[row] = qr.scale;
       for (int c = threadIdx.x; c < nvec; c += T) store_q<QK>(qrow, c, lds_v4(slot + 16 * c), qr);
     }
@@ -410,11 +474,20 @@ constexpr int kWarpRingHeader = kWarpMaxWarps * kWarpMaxStages * 8;   // mbarrie
 
 struct WarpRingGeom {
   int stages;           // slots per warp (2..kWarpMaxStages)
-  uint32_t slot_bytes;  // one row rounded up to 128 bytes
-  uint32_t row_bytes;   // bytes of the row's bulk copy
+  uint32_t slot_bytes;  // one row (padded layout: its pieces at kPiecePitch) rounded up to 128 bytes
+  uint32_t row_bytes;   // bytes of the row
   int64_t cta_rows;     // > 0: CTA b owns rows [b * cta_rows, (b + 1) * cta_rows), its warps
                         // interleaved; 0: rows are dealt round robin over all warps of the grid
+  int padded;           // rows copied in 256-byte pieces at kPiecePitch (all lanes issue)
 };
+
+// Issue the copies of one row into `slot` (every lane of the warp): lane 0 registers the
+// row's bytes on the slot's mbarrier.
+__device__ __forceinline__ void warp_ring_issue(uint64_t* bar, uint8_t* slot, const void* src, const WarpRingGeom& g,
+                                                int lane, uint64_t policy) {
+  if (lane == 0) mbar_arrive_expect_tx(bar, g.row_bytes);
+  issue_row_copies(slot, src, g.row_bytes, g.padded != 0, bar, lane, policy);
+}
 
 // Runs `body(row, slot)` for the rows of this warp: blockIdx.x * W + warp, then every
 // gridDim.x * W rows (W warps per CTA), each warp `stages - 1` rows ahead.
@@ -429,19 +502,18 @@ __device__ __forceinline__ void warp_row_loop(uint8_t* smem, const WarpRingGeom&
   const int64_t GW = static_cast<int64_t>(gridDim.x) * W;
   const int64_t first = static_cast<int64_t>(blockIdx.x) * W + warp;
   const uint64_t policy = policy_evict_first();
-  int64_t issued = 0;   // lane 0 only
   if (lane == 0) {
     for (int i = 0; i < g.stages; ++i) mbar_init(&full[i], 1);
     fence_mbarrier_init();
-    for (int i = 0; i < g.stages; ++i) {
-      const int64_t r = first + i * GW;
-      if (r >= nrows) break;
-      mbar_arrive_expect_tx(&full[i], g.row_bytes);
-      bulk_load(slots + static_cast<size_t>(i) * g.slot_bytes, src(r), g.row_bytes, &full[i], policy);
-      ++issued;
-    }
   }
   __syncwarp();
+  int64_t issued = 0;   // the same in every lane
+  for (int i = 0; i < g.stages; ++i) {
+    const int64_t r = first + i * GW;
+    if (r >= nrows) break;
+    warp_ring_issue(&full[i], slots + static_cast<size_t>(i) * g.slot_bytes, src(r), g, lane, policy);
+    ++issued;
+  }
   int st = 0;
   uint32_t ph = 0;
   int64_t k = 0;
@@ -452,14 +524,11 @@ __device__ __forceinline__ void warp_row_loop(uint8_t* smem, const WarpRingGeom&
     uint8_t* slot = slots + static_cast<size_t>(st) * g.slot_bytes;
     body(row, slot);
     __syncwarp();
-    if (lane == 0) {
-      const int64_t r = row + ahead;
-      if (r < nrows) {
-        fence_proxy_async_smem();   // the warp's reads of the slot precede the copy that refills it
-        mbar_arrive_expect_tx(&full[st], g.row_bytes);
-        bulk_load(slot, src(r), g.row_bytes, &full[st], policy);
-        ++issued;
-      }
+    const int64_t r = row + ahead;
+    if (r < nrows) {
+      fence_proxy_async_smem();   // the warp's reads of the slot precede the copies that refill it
+      warp_ring_issue(&full[st], slot, src(r), g, lane, policy);
+      ++issued;
     }
     if (++st == g.stages) {
       st = 0;
@@ -562,20 +631,21 @@ __device__ __forceinline__ float absmax_f2x4(float m, const float2 (&h)[4]) {
   return m;
 }
 
-// The modulation vectors are re-read (from L1/L2) for every row: caching them in
-// registers across the rows of one batch element raised register use enough to cost
-// more occupancy than the loads it saved (measured at D=3072).
-template <int V, int MODE>
+// RMSNorm + modulation + per-token quantisation, one CTA (row group) per row, for rows
+// longer than a warp ring holds.  The modulation vectors are re-read (from L1/L2) for
+// every row: caching them in registers across the rows of one batch element raised
+// register use enough to cost more occupancy than the loads it saved (measured at D=3072).
+template <int V, int QK>
 __global__ void __launch_bounds__(512) rms_mod_kernel(const RmsArgs a, const RingGeom g) {
   extern __shared__ __align__(1024) uint8_t smem[];
   const int T = blockDim.x;
+  const RowGroup grp = row_group(T);
   const int nvec = a.D >> 3;
   const float fD = static_cast<float>(a.D);
   int64_t cur_m = -1;
   int64_t seg_end = -1;          // first row past the current batch element (rows_per_mod layout)
   auto src = [&](int64_t r, int) -> const void* { return a.x + r * a.ld_x; };
-  float tw_max = 0.f;   // tensorwise: running max of |h| over this thread's rows
-  row_loop(smem, g, a.S, src, [&](int64_t row, uint8_t* slot, const RingState& rs) {
+  row_loop(smem, g, grp, a.S, src, [&](int64_t row, uint8_t* slot, const RingState& rs) {
     // pass 1: sum of squares in the canonical order
     float2 acc = make_float2(0.f, 0.f);
     if constexpr (V > 0) {
@@ -587,7 +657,7 @@ __global__ void __launch_bounds__(512) rms_mod_kernel(const RmsArgs a, const Rin
     } else {
       for (int c = threadIdx.x; c < nvec; c += T) acc = row_sumsq_vec(acc, lds_v4(slot + 16 * c));
     }
-    const float ss = block_sum(__fadd_rn(acc.x, acc.y), rs.red_sum);
+    const float ss = block_sum(grp, __fadd_rn(acc.x, acc.y), rs.red_sum);
     const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, fD), a.eps)));
     const float2 inv2 = make_float2(inv, inv);
     // each CTA visits rows in increasing order: divide only when a batch element ends
@@ -602,8 +672,6 @@ __global__ void __launch_bounds__(512) rms_mod_kernel(const RmsArgs a, const Rin
     }
     uint8_t* qrow = static_cast<uint8_t*>(a.q) + row * a.ld_q;
     uint32_t m2 = 0;
-    float amax32 = 0.f;
-
     cur_m = m;
     if constexpr (V > 0) {
       uint4 hv[V];
@@ -615,52 +683,42 @@ __global__ void __launch_bounds__(512) rms_mod_kernel(const RmsArgs a, const Rin
           float2 x[4], h[4], sm[4], bm[4];
           load_mod8(a, m, c, sm, bm);
           rms_h8(lds_v4(slot + 16 * c), inv2, sm, bm, a.w, c, x, h);
-          if constexpr (MODE == kModeTensorwise) amax32 = absmax_f2x4(amax32, h);
           hv[i] = rms_store8(a, row, c, x, h);
           m2 = absmax4(m2, hv[i]);
         }
       }
-      if constexpr (MODE != kModeTensorwise) {
-        constexpr int QK = MODE;
-        const QuantRow qr = quant_row<QK>(block_max(pair_max(m2), rs.red_max));
-        if (threadIdx.x == 0) a.q_scale[row] = qr.scale;
+      const QuantRow qr = quant_row<QK>(block_max(grp, pair_max(m2), rs.red_max));
+      if (threadIdx.x == 0) a.q_scale[row] = qr.scale;
 #pragma unroll
-        for (int i = 0; i < V; ++i) {
-          const int c = threadIdx.x + T * i;
-          if (c < nvec) store_q<QK>(qrow, c, hv[i], qr);
-        }
+      for (int i = 0; i < V; ++i) {
+        const int c = threadIdx.x + T * i;
+        if (c < nvec) store_q<QK>(qrow, c, hv[i], qr);
       }
     } else {
       for (int c = threadIdx.x; c < nvec; c += T) {
         float2 s[4], b[4], x[4], h[4];
         load_mod8(a, m, c, s, b);
         rms_h8(lds_v4(slot + 16 * c), inv2, s, b, a.w, c, x, h);
-        if constexpr (MODE == kModeTensorwise) amax32 = absmax_f2x4(amax32, h);
         const uint4 hu = rms_store8(a, row, c, x, h);
         m2 = absmax4(m2, hu);
         *reinterpret_cast<uint4*>(slot + 16 * c) = hu;   // h replaces x in the slot
       }
       slot_written();
-      if constexpr (MODE != kModeTensorwise) {
-        constexpr int QK = MODE;
-        const QuantRow qr = quant_row<QK>(block_max(pair_max(m2), rs.red_max));   // barrier: h complete
-        if (threadIdx.x == 0) a.q_scale[row] = qr.scale;
-        for (int c = threadIdx.x; c < nvec; c += T) store_q<QK>(qrow, c, lds_v4(slot + 16 * c), qr);
-      }
+      const QuantRow qr = quant_row<QK>(block_max(grp, pair_max(m2), rs.red_max));   // barrier: h complete
+      if (threadIdx.x == 0) a.q_scale[row] = qr.scale;
+      for (int c = threadIdx.x; c < nvec; c += T) store_q<QK>(qrow, c, lds_v4(slot + 16 * c), qr);
     }
-    if constexpr (MODE == kModeTensorwise) tw_max = fmaxf(tw_max, amax32);
   });
-  if constexpr (MODE == kModeTensorwise) flush_amax(a.amax, tw_max);
 }
 
-// RMSNorm + modulation + quantisation, one row per warp (rows of at most
+// RMSNorm + modulation + per-token quantisation, one row per warp (rows of at most
 // kWarpRowMaxBytes).  The sum of squares is the canonical row-group tree of
 // rms_mod_kernel for a group of T threads: lane l plays thread 32 j + l of every warp
 // j < T / 32, so each of those warps' accumulation, butterfly and the left-to-right
 // sum of their partials are the same operations in the same order.  h (and the
 // optional res) is stored per vector, and bf16(h) replaces x in the slot for the
 // quantisation pass.
-template <int MODE>
+template <int QK>
 __global__ void __launch_bounds__(1024) rms_mod_warp_kernel(const RmsArgs a, const WarpRingGeom g, const int T) {
   extern __shared__ __align__(1024) uint8_t smem[];
   const int lane = threadIdx.x & 31;
@@ -670,7 +728,6 @@ __global__ void __launch_bounds__(1024) rms_mod_warp_kernel(const RmsArgs a, con
   int64_t cur_m = -1;
   int64_t seg_end = -1;   // first row past the current batch element (rows_per_mod layout)
   auto src = [&](int64_t r) -> const void* { return a.x + r * a.ld_x; };
-  float tw_max = 0.f;   // tensorwise: running max of |h| over this thread's rows
   warp_row_loop(smem, g, a.S, src, [&](int64_t row, uint8_t* slot) {
     // pass 1: sum of squares, virtual warp by virtual warp
     float ss = 0.f;
@@ -696,32 +753,24 @@ __global__ void __launch_bounds__(1024) rms_mod_warp_kernel(const RmsArgs a, con
     cur_m = m;
     // pass 2: h, its stores, the row max; bf16(h) back into the slot
     uint32_t m2 = 0;
-    float amax32 = 0.f;
 #pragma unroll 2
     for (int c = lane; c < nvec; c += 32) {
       float2 s[4], b[4], x[4], h[4];
       load_mod8(a, m, c, s, b);
       rms_h8(lds_v4(slot + 16 * c), inv2, s, b, a.w, c, x, h);
-      if constexpr (MODE == kModeTensorwise) amax32 = absmax_f2x4(amax32, h);
       const uint4 hu = rms_store8(a, row, c, x, h);
       m2 = absmax4(m2, hu);
-      if constexpr (MODE != kModeTensorwise) *reinterpret_cast<uint4*>(slot + 16 * c) = hu;
+      *reinterpret_cast<uint4*>(slot + 16 * c) = hu;
     }
-    if constexpr (MODE != kModeTensorwise) {
-      constexpr int QK = MODE;
-      float mx = pair_max(m2);
+    float mx = pair_max(m2);
 #pragma unroll
-      for (int off = 16; off >= 1; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, off));
-      const QuantRow qr = quant_row<QK>(mx);
-      if (lane == 0) a.q_scale[row] = qr.scale;
-      uint8_t* qrow = static_cast<uint8_t*>(a.q) + row * a.ld_q;
+    for (int off = 16; off >= 1; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, off));
+    const QuantRow qr = quant_row<QK>(mx);
+    if (lane == 0) a.q_scale[row] = qr.scale;
+    uint8_t* qrow = static_cast<uint8_t*>(a.q) + row * a.ld_q;
 #pragma unroll 4
-      for (int c = lane; c < nvec; c += 32) store_q<QK>(qrow, c, lds_v4(slot + 16 * c), qr);
-    } else {
-      tw_max = fmaxf(tw_max, amax32);
-    }
+    for (int c = lane; c < nvec; c += 32) store_q<QK>(qrow, c, lds_v4(slot + 16 * c), qr);
   });
-  if constexpr (MODE == kModeTensorwise) flush_amax(a.amax, tw_max);
 }
 
 // ---------------------------------------------------------------- register-resident warp rows
@@ -1002,17 +1051,16 @@ __global__ void __launch_bounds__(512, 1) rms_mod_simple_kernel(const RmsArgs a,
       });
 }
 
-// RMSNorm + modulation + quantisation (every option of the entry point: norm weight,
-// mod_index, scale as multiplier, h / res outputs, tensorwise phase A) for rows of 256 NV
-// elements held in registers.
-template <int NV, int MODE>
+// RMSNorm + modulation + per-token quantisation (every option of the entry point: norm
+// weight, mod_index, scale as multiplier, h / res outputs) for rows of 256 NV elements held
+// in registers.
+template <int NV, int QK>
 __global__ void __launch_bounds__(512, 1) rms_mod_warp_reg_kernel(const RmsArgs a, const WarpRingGeom g) {
   extern __shared__ __align__(1024) uint8_t smem[];
   const int lane = threadIdx.x & 31;
   int64_t cur_m = -1;
   int64_t seg_end = -1;
   auto src = [&](int64_t r) -> const void* { return a.x + r * a.ld_x; };
-  float tw_max = 0.f;   // tensorwise: running max of |h| over this thread's rows
   warp_row_loop_reg(
       smem, g, a.S, src, [&](const uint8_t* slot) { return load_row_regs<NV>(slot, lane); },
       [&](int64_t row, RowRegs<NV>& r) {
@@ -1031,7 +1079,6 @@ __global__ void __launch_bounds__(512, 1) rms_mod_warp_reg_kernel(const RmsArgs 
         const __nv_bfloat16* srow = a.scale + m * a.ld_mod;
         const __nv_bfloat16* brow = a.shift + m * a.ld_mod;
         uint32_t m2 = 0;
-        float amax32 = 0.f;
 #pragma unroll
         for (int k = 0; k < NV; ++k) {
           const int c = 32 * k + lane;
@@ -1055,7 +1102,6 @@ __global__ void __launch_bounds__(512, 1) rms_mod_warp_reg_kernel(const RmsArgs 
             t = mul2_rn(t, bf2_to_f2(sw[p]));
             h[p] = add_f32_bf16x2(t, bw[p]);
           }
-          if constexpr (MODE == kModeTensorwise) amax32 = absmax_f2x4(amax32, h);
           const uint4 hu = make_uint4(f2_to_bf2(h[0]), f2_to_bf2(h[1]), f2_to_bf2(h[2]), f2_to_bf2(h[3]));
           {
             if (a.res) {
@@ -1073,55 +1119,177 @@ __global__ void __launch_bounds__(512, 1) rms_mod_warp_reg_kernel(const RmsArgs 
           // keep the modulation loads of at most four vectors in flight (register budget)
           if ((k & 3) == 3) asm volatile("" ::: "memory");
         }
-        if constexpr (MODE != kModeTensorwise) {
-          constexpr int QK = MODE;
-          float mx = pair_max(m2);
+        float mx = pair_max(m2);
 #pragma unroll
-          for (int off = 16; off >= 1; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, off));
-          const QuantRow qr = quant_row<QK>(mx);
-          if (lane == 0) a.q_scale[row] = qr.scale;
-          uint8_t* qrow = static_cast<uint8_t*>(a.q) + row * a.ld_q;
+        for (int off = 16; off >= 1; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, off));
+        const QuantRow qr = quant_row<QK>(mx);
+        if (lane == 0) a.q_scale[row] = qr.scale;
+        uint8_t* qrow = static_cast<uint8_t*>(a.q) + row * a.ld_q;
 #pragma unroll
-          for (int k = 0; k < NV; ++k) store_q<QK>(qrow, 32 * k + lane, r.v[k], qr);
-        } else {
-          tw_max = fmaxf(tw_max, amax32);
-        }
+        for (int k = 0; k < NV; ++k) store_q<QK>(qrow, 32 * k + lane, r.v[k], qr);
       });
-  if constexpr (MODE == kModeTensorwise) flush_amax(a.amax, tw_max);
+}
+
+// ---------------------------------------------------------------- tensorwise (reference) norm
+// The reference's fused_rms_mod_quant and its per-segment driver (src/ck_fused_mod_norm_quant.py:
+// 23-55, src/ck_fused_patch.py:105-136) derive one scale for the whole tensor from the
+// float32 max of |h|, so h must be the reference's to the last bit: these kernels sum the
+// squares in the reference's own order.  Its kernel accumulates x^2 into a 2048-lane float32
+// vector chunk by chunk (lane i += x[2048 c + i]^2; BLOCK_K = 2048 in both callers) and
+// reduces the vector with tl.sum, which Triton evaluates (CPU interpreter: numpy's pairwise
+// summation) as a balanced binary tree over 16 leaves of 128 lanes, each leaf summed by 8
+// interleaved accumulators r_j (lanes 8 t + j, t = 0..15, in order) and combined as
+// ((r0 + r1) + (r2 + r3)) + ((r4 + r5) + (r6 + r7)).
+//
+// One warp computes it from a row in the padded layout: lane 2 b + e owns leaf b's
+// accumulators 4 e .. 4 e + 3 and folds their chunks in order with a mixed-precision fma
+// (x^2 of a bf16 value is exact, so fma(x, x, acc) = RN(acc + x^2)); the eight accumulators
+// of a leaf combine as above (the two halves across the lane pair), and the leaves by a
+// butterfly (xor 2, 4, 8, 16), which is the pairwise tree.  At a given (t, chunk) the 32
+// lanes read 8 bytes at the same offset of 16 consecutive pieces: with the 272-byte piece
+// pitch each half-warp covers all 32 banks once.
+constexpr int kRefBlock = 2048;
+
+__device__ __forceinline__ float ref_sumsq_warp(const uint8_t* row, int D, int lane) {
+  const int b = lane >> 1;
+  const int e = lane & 1;
+  const int nch = (D + kRefBlock - 1) / kRefBlock;
+  float2 r01 = make_float2(0.f, 0.f), r23 = make_float2(0.f, 0.f);
+#pragma unroll
+  for (int t = 0; t < 16; ++t) {
+    float2 e01 = make_float2(0.f, 0.f), e23 = make_float2(0.f, 0.f);
+    for (int c = 0; c < nch; ++c) {
+      const int el = c * kRefBlock + b * 128 + t * 8 + e * 4;   // this lane's 4 elements (all in or all out)
+      if (el < D) {
+        const uint2 v = *reinterpret_cast<const uint2*>(row + (el >> 7) * kPiecePitch + (el & 127) * 2);
+        e01 = sumsq_bf16x2(e01, v.x);
+        e23 = sumsq_bf16x2(e23, v.y);
+      }
+    }
+    if (t == 0) {
+      r01 = e01;
+      r23 = e23;
+    } else {
+      r01 = make_float2(__fadd_rn(r01.x, e01.x), __fadd_rn(r01.y, e01.y));
+      r23 = make_float2(__fadd_rn(r23.x, e23.x), __fadd_rn(r23.y, e23.y));
+    }
+  }
+  float v = __fadd_rn(__fadd_rn(r01.x, r01.y), __fadd_rn(r23.x, r23.y));
+#pragma unroll
+  for (int off = 1; off <= 16; off <<= 1) v = __fadd_rn(v, __shfl_xor_sync(0xFFFFFFFFu, v, off));
+  return v;
+}
+
+__device__ __forceinline__ float rms_inv_of(float ss, float D, float eps) {
+  return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, D), eps)));
+}
+
+// The modulation row of `row` (mod_index, or batch-major rows_per_mod with the division done
+// only when a batch element ends; rows are visited in increasing order).
+__device__ __forceinline__ int64_t mod_row_of(const RmsArgs& a, int64_t row, int64_t& cur_m, int64_t& seg_end) {
+  if (a.mod_index) return static_cast<int64_t>(__ldg(a.mod_index + row));
+  if (row >= seg_end || cur_m < 0) {
+    cur_m = row / a.rows_per_mod;
+    seg_end = (cur_m + 1) * a.rows_per_mod;
+  }
+  return cur_m;
+}
+
+// Phase A of the tensorwise norm, one row per warp (rows of at most kWarpRowMaxBytes, padded
+// layout): h and res stored, each lane's running max of the float32 |h|, folded into the
+// tensor's amax word at the end.
+__global__ void __launch_bounds__(1024) rms_mod_tw_warp_kernel(const RmsArgs a, const WarpRingGeom g) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const int lane = threadIdx.x & 31;
+  const int nvec = a.D >> 3;
+  const float fD = static_cast<float>(a.D);
+  int64_t cur_m = -1, seg_end = -1;
+  float tw_max = 0.f;
+  auto src = [&](int64_t r) -> const void* { return a.x + r * a.ld_x; };
+  warp_row_loop(smem, g, a.S, src, [&](int64_t row, uint8_t* slot) {
+    const float inv = rms_inv_of(ref_sumsq_warp(slot, a.D, lane), fD, a.eps);
+    const float2 inv2 = make_float2(inv, inv);
+    const int64_t m = mod_row_of(a, row, cur_m, seg_end);
+#pragma unroll 2
+    for (int c = lane; c < nvec; c += 32) {
+      float2 s[4], b[4], x[4], h[4];
+      load_mod8(a, m, c, s, b);
+      rms_h8(lds_v4(slot + padded_vec(c)), inv2, s, b, a.w, c, x, h);
+      tw_max = absmax_f2x4(tw_max, h);
+      rms_store8(a, row, c, x, h);
+    }
+  });
+  flush_amax(a.amax, tw_max);
+}
+
+// The same for longer rows, one CTA (row group of T threads) per row: its first warp sums
+// the squares in the reference's order while the others wait, then every thread takes the
+// vectors t, t + T, ... of the h pass.
+__global__ void __launch_bounds__(512) rms_mod_tw_cta_kernel(const RmsArgs a, const RingGeom g) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const int T = blockDim.x;
+  const RowGroup grp = row_group(T);
+  const int nvec = a.D >> 3;
+  const float fD = static_cast<float>(a.D);
+  int64_t cur_m = -1, seg_end = -1;
+  float tw_max = 0.f;
+  auto src = [&](int64_t r, int) -> const void* { return a.x + r * a.ld_x; };
+  row_loop(smem, g, grp, a.S, src, [&](int64_t row, uint8_t* slot, const RingState& rs) {
+    if (grp.t < 32) {
+      const float ss = ref_sumsq_warp(slot, a.D, grp.t);
+      if (grp.t == 0) rs.red_sum[0] = ss;
+    }
+    group_sync(grp);
+    const float inv = rms_inv_of(rs.red_sum[0], fD, a.eps);
+    const float2 inv2 = make_float2(inv, inv);
+    const int64_t m = mod_row_of(a, row, cur_m, seg_end);
+    for (int c = grp.t; c < nvec; c += T) {
+      float2 s[4], b[4], x[4], h[4];
+      load_mod8(a, m, c, s, b);
+      rms_h8(lds_v4(slot + padded_vec(c)), inv2, s, b, a.w, c, x, h);
+      tw_max = absmax_f2x4(tw_max, h);
+      rms_store8(a, row, c, x, h);
+    }
+    // rs.red_sum[0] is rewritten only after the next row's group barrier in row_loop
+  });
+  flush_amax(a.amax, tw_max);
 }
 
 // ---------------------------------------------------------------- SwiGLU
-// (lo(g) / 4, hi(g) / 4) straight from a packed bf16 pair: one mixed-precision fma per
-// value, g * 0.25 + (-0), exact (the sign of a zero product is kept).
-__device__ __forceinline__ float2 quarter_bf16x2(uint32_t g) {
-  float x, y;
-  asm("{ .reg .b16 lo, hi, q; mov.b32 {lo, hi}, %2; mov.b16 q, 0x3E80;"
-      " fma.rn.f32.bf16 %0, lo, q, 0f80000000; fma.rn.f32.bf16 %1, hi, q, 0f80000000; }"
-      : "=f"(x), "=f"(y)
-      : "r"(g));
-  return make_float2(x, y);
-}
-
-// act for one vector from the gate and up rows in the slot; returns bf16(act).
-__device__ __forceinline__ uint4 swiglu8(const uint8_t* slot, const uint8_t* up, int c, float& amax32, bool tensorwise) {
+// act for one vector from the gate and up rows in the slot (sigmoid table `sig` in shared
+// memory); returns bf16(act) and folds the float32 |act| into amax32 when asked.
+__device__ __forceinline__ uint4 swiglu8(const uint8_t* gate, const uint8_t* up, int c, const uint32_t* sig,
+                                         float& amax32, bool tensorwise) {
   float2 uv[4], act[4];
-  const uint4 gu = lds_v4(slot + 16 * c);
+  const uint4 gu = lds_v4(gate + 16 * c);
   const uint32_t gw[4] = {gu.x, gu.y, gu.z, gu.w};
   unpack_pairs(lds_v4(up + 16 * c), uv);
 #pragma unroll
-  for (int p = 0; p < 4; ++p) act[p] = silu_mul2(quarter_bf16x2(gw[p]), uv[p]);
+  for (int p = 0; p < 4; ++p) act[p] = silu_mul2(gw[p], uv[p], sig);
   if (tensorwise) amax32 = absmax_f2x4(amax32, act);
   return make_uint4(f2_to_bf2(act[0]), f2_to_bf2(act[1]), f2_to_bf2(act[2]), f2_to_bf2(act[3]));
 }
 
+// Shared-memory bytes of one row group's ring.
+__host__ __device__ inline size_t ring_bytes(const RingGeom& g) {
+  return static_cast<size_t>(kRingHeader) + static_cast<size_t>(g.stages) * g.slot_bytes;
+}
+
+// SwiGLU + quantisation, CTA-per-row form: blockDim.x / T row groups of T threads, each with
+// its own ring; the sigmoid table (32 KB) sits in front of the rings and is shared by the
+// groups.  Thread t of a group owns the vectors t, t + T, ... of a row.
 template <int V, int MODE>
-__global__ void __launch_bounds__(1024) swiglu_kernel(const SwigluArgs a, const RingGeom g) {
+__global__ void __launch_bounds__(1024) swiglu_kernel(const SwigluArgs a, const RingGeom g, const int T) {
   extern __shared__ __align__(1024) uint8_t smem[];
-  const int T = blockDim.x;
+  uint32_t* sig = reinterpret_cast<uint32_t*>(smem);
+  load_sigmoid_table(sig, threadIdx.x, blockDim.x);
+  __syncthreads();
+  const RowGroup grp = row_group(T);
+  uint8_t* ring = smem + kSigmoidBytes + static_cast<size_t>(grp.index) * ring_bytes(g);
   const int nvec = a.F >> 3;
   auto src = [&](int64_t r, int part) -> const void* { return (part ? a.up : a.gate) + r * a.ld_in; };
-  float tw_max = 0.f;   // tensorwise: running max of |h| over this thread's rows
-  row_loop(smem, g, a.M, src, [&](int64_t row, uint8_t* slot, const RingState& rs) {
+  float tw_max = 0.f;   // tensorwise: running max of |act| over this thread's rows
+  row_loop(ring, g, grp, a.M, src, [&](int64_t row, uint8_t* slot, const RingState& rs) {
     const uint8_t* up = slot + g.part_bytes;
     uint8_t* qrow = static_cast<uint8_t*>(a.q) + row * a.ld_q;
     uint32_t m2 = 0;
@@ -1131,37 +1299,37 @@ __global__ void __launch_bounds__(1024) swiglu_kernel(const SwigluArgs a, const 
       uint4 av[V];
 #pragma unroll
       for (int i = 0; i < V; ++i) {
-        const int c = threadIdx.x + T * i;
+        const int c = grp.t + T * i;
         av[i] = make_uint4(0, 0, 0, 0);
         if (c < nvec) {
-          av[i] = swiglu8(slot, up, c, amax32, kTw);
+          av[i] = swiglu8(slot, up, c, sig, amax32, kTw);
           m2 = absmax4(m2, av[i]);
           if (a.act) *reinterpret_cast<uint4*>(a.act + row * a.ld_act + 8 * c) = av[i];
         }
       }
       if constexpr (!kTw) {
         constexpr int QK = MODE;
-        const QuantRow qr = quant_row<QK>(block_max(pair_max(m2), rs.red_max));
-        if (threadIdx.x == 0) a.q_scale[row] = qr.scale;
+        const QuantRow qr = quant_row<QK>(block_max(grp, pair_max(m2), rs.red_max));
+        if (grp.t == 0) a.q_scale[row] = qr.scale;
 #pragma unroll
         for (int i = 0; i < V; ++i) {
-          const int c = threadIdx.x + T * i;
+          const int c = grp.t + T * i;
           if (c < nvec) store_q<QK>(qrow, c, av[i], qr);
         }
       }
     } else {
-      for (int c = threadIdx.x; c < nvec; c += T) {
-        const uint4 au = swiglu8(slot, up, c, amax32, kTw);
+      for (int c = grp.t; c < nvec; c += T) {
+        const uint4 au = swiglu8(slot, up, c, sig, amax32, kTw);
         m2 = absmax4(m2, au);
-        *reinterpret_cast<uint4*>(slot + 16 * c) = au;   // act replaces the gate row
+        if constexpr (!kTw) *reinterpret_cast<uint4*>(slot + 16 * c) = au;   // act replaces the gate row
         if (a.act) *reinterpret_cast<uint4*>(a.act + row * a.ld_act + 8 * c) = au;
       }
-      slot_written();
       if constexpr (!kTw) {
         constexpr int QK = MODE;
-        const QuantRow qr = quant_row<QK>(block_max(pair_max(m2), rs.red_max));   // barrier: act complete
-        if (threadIdx.x == 0) a.q_scale[row] = qr.scale;
-        for (int c = threadIdx.x; c < nvec; c += T) store_q<QK>(qrow, c, lds_v4(slot + 16 * c), qr);
+        slot_written();
+        const QuantRow qr = quant_row<QK>(block_max(grp, pair_max(m2), rs.red_max));   // barrier: act complete
+        if (grp.t == 0) a.q_scale[row] = qr.scale;
+        for (int c = grp.t; c < nvec; c += T) store_q<QK>(qrow, c, lds_v4(slot + 16 * c), qr);
       }
     }
     if constexpr (kTw) tw_max = fmaxf(tw_max, amax32);

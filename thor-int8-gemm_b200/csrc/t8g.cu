@@ -226,14 +226,32 @@ int gemm_entry(int in_kind, const void* x, const void* w, const float* x_scale, 
   // kernel.
   const char* sm_env = getenv("T8G_GEMM_SM");
   const bool force_1sm = sm_env && sm_env[0] == '1';
-  // Tile width of the 2-SM kernel: 256 columns, or 128 / 64 for 2-byte outputs when 256-wide
-  // tiles would leave more than half of the CTA pairs idle (small M): narrower tiles put more
-  // SMs on the problem, each with a shorter tile.
+  // Tile width of the 2-SM kernel (2-byte outputs): 256, 128 or 64 columns, whichever keeps
+  // the CTA pairs busiest.  The persistent kernel deals tiles round robin, so with T tiles
+  // on P pairs the last wave is partly idle: busy fraction = T / (ceil(T / P) * P).  A
+  // narrower tile re-reads its activation panel for fewer output columns, which costs a
+  // little per tile (kNarrowCost), so it has to win by more than that.  Examples on 74
+  // pairs: M = 8192, N = 3072 -> 384 tiles of 256 (86.5 % busy) or 768 of 128 (94.3 %):
+  // 128; M = 256, N = 3072 -> 12, 24 or 48 tiles: 64.  T8G_GEMM_TBN=256|128|64 forces one.
   const int64_t pairs_avail = info.sms / 2;
   const int64_t tiles_m = (M + P_BM - 1) / P_BM;
   int tbn = BN;
   if (esz == 2) {
-    while (tbn > 64 && tiles_m * ((N + tbn - 1) / tbn) * 2 < pairs_avail) tbn /= 2;
+    constexpr double kNarrowCost[3] = {1.0, 0.96, 0.88};   // 256, 128, 64 columns
+    double best = -1.0;
+    for (int i = 0, w = BN; i < 3; ++i, w /= 2) {
+      const int64_t tiles = tiles_m * ((N + w - 1) / w);
+      const int64_t waves = (tiles + pairs_avail - 1) / pairs_avail;
+      const double score = kNarrowCost[i] * static_cast<double>(tiles) / static_cast<double>(waves * pairs_avail);
+      if (score > best + 1e-9) {
+        best = score;
+        tbn = w;
+      }
+    }
+    if (const char* force = getenv("T8G_GEMM_TBN")) {
+      const int f = atoi(force);
+      if (f == 256 || f == 128 || f == 64) tbn = f;
+    }
   }
   const bool pair = (M > BM || tbn < BN) && !force_1sm;
   const CUtensorMapDataType in_dt = CU_TENSOR_MAP_DATA_TYPE_UINT8;
@@ -470,20 +488,20 @@ RowShape swiglu_shape(int64_t F) {
 
 // Ring geometry of a row kernel: `parts` operand rows of D bf16 per slot (the depth
 // is set at launch).
-t8g::rows::RingGeom ring_geom(int64_t D, int parts) {
+t8g::rows::RingGeom ring_geom(int64_t D, int parts, bool padded = false) {
   t8g::rows::RingGeom g;
   g.parts = parts;
   g.part_bytes = static_cast<uint32_t>(D * 2);
-  g.slot_bytes = (static_cast<uint32_t>(parts) * g.part_bytes + 127u) & ~127u;
+  g.padded = padded ? 1 : 0;
+  const uint32_t part_slot = padded ? t8g::rows::padded_row_bytes(g.part_bytes) : g.part_bytes;
+  g.slot_bytes = (static_cast<uint32_t>(parts) * part_slot + 127u) & ~127u;
   g.stages = 2;
   return g;
 }
 
-size_t ring_smem(const t8g::rows::RingGeom& g) {
-  return t8g::rows::kRingHeader + static_cast<size_t>(g.stages) * g.slot_bytes;
-}
+size_t ring_smem(const t8g::rows::RingGeom& g) { return t8g::rows::ring_bytes(g); }
 
-constexpr size_t kRowSmemLimit = 200 * 1024;
+constexpr size_t kRowSmemLimit = 226 * 1024;
 
 int check_row_shape(const char* what, int64_t S, int64_t D, int quant_kind, int parts) {
   if (S < 0 || D < 0) return fail(T8G_ERR_INVALID_ARGUMENT, "%s: negative size", what);
@@ -514,9 +532,9 @@ int check_q(const void* q, int64_t ld_q, int64_t D) {
 // kernel gets: at most 16 CTAs per SM share ~216 KB of shared memory, each taking as
 // many slots as fit (2..16), so 150-200 KB of rows are in flight per SM.  Grid =
 // min(rows, SMs x resident CTAs).
-// Raise a row kernel's dynamic shared-memory limit to kRowAttrBytes, once per kernel
-// and device.
-constexpr size_t kRowAttrBytes = 220 * 1024;
+// Raise a row kernel's dynamic shared-memory limit to kRowAttrBytes (the per-CTA maximum),
+// once per kernel and device.
+constexpr size_t kRowAttrBytes = 227 * 1024;
 
 template <typename K>
 int ensure_row_attr(K kern, int dev) {
@@ -547,7 +565,7 @@ int launch_rows(K kern, int T, const A& args, t8g::rows::RingGeom g, int64_t row
   const size_t per_cta = (216 * 1024) / n;
   int stages = static_cast<int>((per_cta > kRingHeader ? per_cta - kRingHeader : 0) / g.slot_bytes);
   stages = stages < 2 ? 2 : stages > kMaxStages ? kMaxStages : stages;
-  while (stages > 2 && ring_smem(t8g::rows::RingGeom{stages, g.slot_bytes, g.part_bytes, g.parts}) > kRowSmemLimit)
+  while (stages > 2 && ring_smem(t8g::rows::RingGeom{stages, g.slot_bytes, g.part_bytes, g.parts, g.padded}) > kRowSmemLimit)
     --stages;
   g.stages = stages;
   const size_t smem = ring_smem(g);
@@ -571,6 +589,7 @@ struct WarpLaunch {
   int max_warps = t8g::rows::kWarpMaxWarps;
   size_t tail_bytes = 0;
   bool contiguous = false;
+  bool padded = false;   // rows in 256-byte pieces at the padded pitch (reference-order reduction)
 };
 
 template <typename K, typename A, typename... Extra>
@@ -581,7 +600,8 @@ int launch_warp_rows(K kern, const A& args, uint32_t row_bytes, int64_t rows, in
   if (rc) return rc;
   WarpRingGeom g;
   g.row_bytes = row_bytes;
-  g.slot_bytes = (row_bytes + 127u) & ~127u;
+  g.padded = opt.padded ? 1 : 0;
+  g.slot_bytes = ((opt.padded ? padded_row_bytes(row_bytes) : row_bytes) + 127u) & ~127u;
   g.stages = kWarpStages;
   const int64_t budget = static_cast<int64_t>(216 * 1024 - kWarpRingHeader) - static_cast<int64_t>(opt.tail_bytes);
   int64_t warps = budget / (static_cast<int64_t>(g.stages) * g.slot_bytes);
@@ -592,6 +612,40 @@ int launch_warp_rows(K kern, const A& args, uint32_t row_bytes, int64_t rows, in
   g.cta_rows = opt.contiguous ? (rows + grid - 1) / grid : 0;
   const size_t smem = kWarpRingHeader + static_cast<size_t>(warps) * g.stages * g.slot_bytes + opt.tail_bytes;
   kern<<<static_cast<unsigned>(grid), static_cast<unsigned>(32 * warps), smem, st>>>(args, g, extra...);
+  T8G_CHECK_CUDA(cudaGetLastError(), what);
+  return T8G_OK;
+}
+
+// Launch the SwiGLU kernel: one CTA per SM holding the 32 KB sigmoid table and up to eight
+// row groups of T threads (at most 1024 threads), each with a ring of as many slots (>= 2)
+// as the rest of the CTA's shared memory holds.
+template <typename K>
+int launch_swiglu(K kern, int T, const t8g::rows::SwigluArgs& args, t8g::rows::RingGeom g, int64_t rows, int dev,
+                  int sms, cudaStream_t st, const char* what) {
+  using namespace t8g::rows;
+  int rc = ensure_row_attr(kern, dev);
+  if (rc) return rc;
+  const size_t avail = kRowAttrBytes - t8g::kSigmoidBytes;
+  int groups = 1024 / T;
+  if (groups > 8) groups = 8;
+  if (groups < 1) groups = 1;
+  auto group_fits = [&](int n, int stages) {
+    return static_cast<size_t>(n) * (kRingHeader + static_cast<size_t>(stages) * g.slot_bytes) <= avail;
+  };
+  while (groups > 1 && !group_fits(groups, 2)) --groups;
+  if (!group_fits(groups, 2)) return fail(T8G_ERR_UNSUPPORTED, "%s: row too long for the shared-memory ring", what);
+  int stages = 2;
+  while (stages < kMaxStages && group_fits(groups, stages + 1)) ++stages;
+  g.stages = stages;
+  const size_t smem = t8g::kSigmoidBytes + static_cast<size_t>(groups) * ring_bytes(g);
+  const int threads = groups * T;
+  int occ = 0;
+  T8G_CHECK_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, threads, smem), "occupancy query");
+  if (occ < 1) occ = 1;
+  const int64_t want = (rows + groups - 1) / groups;
+  const int64_t cap = static_cast<int64_t>(sms) * occ;
+  const unsigned grid = static_cast<unsigned>(want < cap ? want : cap);
+  kern<<<grid, threads, smem, st>>>(args, g, T);
   T8G_CHECK_CUDA(cudaGetLastError(), what);
   return T8G_OK;
 }
@@ -702,15 +756,16 @@ int rms_common(bool tensorwise, const void* x, int64_t ld_x, const void* w, cons
   WarpLaunch reg_launch;
   reg_launch.max_warps = kRegWarps;
   if (tensorwise) {
+    // phase A sums the squares in the reference's order (rows in the padded layout)
     T8G_CHECK_CUDA(cudaMemsetAsync(amax, 0, sizeof(float), st), "cudaMemsetAsync(amax)");
-    if (nv) {
-      T8G_DISPATCH_NV(nv, rc = launch_warp_rows(rms_mod_warp_reg_kernel<NV, kModeTensorwise>, a, row_bytes, S,
-                                                dev, info.sms, st, reg_launch, "rms_mod phase A"));
-    } else if (warp_rows)
-      rc = launch_warp_rows(rms_mod_warp_kernel<kModeTensorwise>, a, row_bytes, S, dev, info.sms, st,
-                            WarpLaunch{}, "rms_mod phase A", rsh.T);
-    else
-      T8G_DISPATCH_V(rsh.V, rc = launch_rows(rms_mod_kernel<V, kModeTensorwise>, rsh.T, a, g, S, dev, info.sms, st, "rms_mod phase A"));
+    if (warp_rows) {
+      WarpLaunch o;
+      o.padded = true;
+      rc = launch_warp_rows(rms_mod_tw_warp_kernel, a, row_bytes, S, dev, info.sms, st, o, "rms_mod phase A");
+    } else {
+      rc = launch_rows(rms_mod_tw_cta_kernel, rsh.T, a, ring_geom(D, 1, true), S, dev, info.sms, st,
+                       "rms_mod phase A");
+    }
     if (rc) return rc;
     QuantGivenArgs b;
     b.h = a.h;
@@ -737,23 +792,23 @@ int rms_common(bool tensorwise, const void* x, int64_t ld_x, const void* w, cons
                                                   info.sms, st, o, "rms_mod_quant"));
       }
     } else if (fp8) {
-      T8G_DISPATCH_NV(nv, rc = launch_warp_rows(rms_mod_warp_reg_kernel<NV, kModeFp8>, a, row_bytes, S, dev,
+      T8G_DISPATCH_NV(nv, rc = launch_warp_rows(rms_mod_warp_reg_kernel<NV, kQuantFp8>, a, row_bytes, S, dev,
                                                 info.sms, st, reg_launch, "rms_mod_quant"));
     } else {
-      T8G_DISPATCH_NV(nv, rc = launch_warp_rows(rms_mod_warp_reg_kernel<NV, kModeInt8>, a, row_bytes, S, dev,
+      T8G_DISPATCH_NV(nv, rc = launch_warp_rows(rms_mod_warp_reg_kernel<NV, kQuantInt8>, a, row_bytes, S, dev,
                                                 info.sms, st, reg_launch, "rms_mod_quant"));
     }
     return rc;
   }
   if (warp_rows) {
     if (quant_kind == T8G_QUANT_FP8_E4M3)
-      return launch_warp_rows(rms_mod_warp_kernel<kModeFp8>, a, row_bytes, S, dev, info.sms, st, WarpLaunch{}, "rms_mod_quant", rsh.T);
-    return launch_warp_rows(rms_mod_warp_kernel<kModeInt8>, a, row_bytes, S, dev, info.sms, st, WarpLaunch{}, "rms_mod_quant", rsh.T);
+      return launch_warp_rows(rms_mod_warp_kernel<kQuantFp8>, a, row_bytes, S, dev, info.sms, st, WarpLaunch{}, "rms_mod_quant", rsh.T);
+    return launch_warp_rows(rms_mod_warp_kernel<kQuantInt8>, a, row_bytes, S, dev, info.sms, st, WarpLaunch{}, "rms_mod_quant", rsh.T);
   }
   if (quant_kind == T8G_QUANT_FP8_E4M3) {
-    T8G_DISPATCH_V(rsh.V, rc = launch_rows(rms_mod_kernel<V, kModeFp8>, rsh.T, a, g, S, dev, info.sms, st, "rms_mod_quant"));
+    T8G_DISPATCH_V(rsh.V, rc = launch_rows(rms_mod_kernel<V, kQuantFp8>, rsh.T, a, g, S, dev, info.sms, st, "rms_mod_quant"));
   } else {
-    T8G_DISPATCH_V(rsh.V, rc = launch_rows(rms_mod_kernel<V, kModeInt8>, rsh.T, a, g, S, dev, info.sms, st, "rms_mod_quant"));
+    T8G_DISPATCH_V(rsh.V, rc = launch_rows(rms_mod_kernel<V, kQuantInt8>, rsh.T, a, g, S, dev, info.sms, st, "rms_mod_quant"));
   }
   return rc;
 }
@@ -792,7 +847,7 @@ int swiglu_common(bool tensorwise, const void* gate, const void* up, int64_t ld_
   const RingGeom g = ring_geom(F, 2);
   if (tensorwise) {
     T8G_CHECK_CUDA(cudaMemsetAsync(amax, 0, sizeof(float), st), "cudaMemsetAsync(amax)");
-    T8G_DISPATCH_SW(rsh.V, rc = launch_rows(swiglu_kernel<V, kModeTensorwise>, rsh.T, a, g, M, dev, info.sms, st, "swiglu phase A"));
+    T8G_DISPATCH_SW(rsh.V, rc = launch_swiglu(swiglu_kernel<V, kModeTensorwise>, rsh.T, a, g, M, dev, info.sms, st, "swiglu phase A"));
     if (rc) return rc;
     QuantGivenArgs b;
     b.h = a.act;
@@ -806,9 +861,9 @@ int swiglu_common(bool tensorwise, const void* gate, const void* up, int64_t ld_
     return launch_quant_given(b, quant_kind, info.sms, st);
   }
   if (quant_kind == T8G_QUANT_FP8_E4M3) {
-    T8G_DISPATCH_SW(rsh.V, rc = launch_rows(swiglu_kernel<V, kModeFp8>, rsh.T, a, g, M, dev, info.sms, st, "swiglu_quant"));
+    T8G_DISPATCH_SW(rsh.V, rc = launch_swiglu(swiglu_kernel<V, kModeFp8>, rsh.T, a, g, M, dev, info.sms, st, "swiglu_quant"));
   } else {
-    T8G_DISPATCH_SW(rsh.V, rc = launch_rows(swiglu_kernel<V, kModeInt8>, rsh.T, a, g, M, dev, info.sms, st, "swiglu_quant"));
+    T8G_DISPATCH_SW(rsh.V, rc = launch_swiglu(swiglu_kernel<V, kModeInt8>, rsh.T, a, g, M, dev, info.sms, st, "swiglu_quant"));
   }
   return rc;
 }

@@ -17,18 +17,24 @@ What the fused forward runs (the block's call order is the stock one, :153-172):
     (t8g_rms_mod_quant_tensorwise) for all segments through a per-token modulation-row map
     -- handed to qkv_proj / fc1 as comfy's fp8 QuantizedTensor, so they skip their own
     quantisation;
-  cluster 2 (on / c2): fc1's bf16 output -> SwiGLU + tensorwise fp8 (gate and up read in
-    place, t8g_swiglu_quant_tensorwise) -> QuantizedTensor -> fc2.
+  cluster 2 (on / c2): when fc1 and fc2 hold comfy fp8 QuantizedTensor weights (e4m3 codes
+    with one scale, or one per output channel), the whole MLP and the block's gated residual
+    run on this library's fp8 GEMMs: fc1 with the SwiGLU in its epilogue
+    (t8g_gemm_fp8_swiglu; its weight, scale and bias interleaved in 128-row gate / up blocks
+    once per weight and cached), per-token fp8 quantisation of act (t8g_quant_rows), and fc2
+    with x + gate_mlp * y in its epilogue (t8g_gemm_fp8_gated) -- neither fc1's [S, 2F]
+    output nor fc2's output reaches memory, and comfy's own fp8 matmul is not called.
+    Otherwise (another weight format) fc1 runs as comfy's linear and its bf16 output takes
+    the reference's route: SwiGLU + tensorwise fp8 (gate and up read in place,
+    t8g_swiglu_quant_tensorwise) -> QuantizedTensor -> fc2.
 Unlike the reference (:97-101), a segment whose row is a tensor of per-token rows (inpaint
 masks) is accepted: it maps straight into the kernel's row map.
 """
 from __future__ import annotations
 
-import importlib.abc
-import importlib.machinery
-import os
-import sys
 import traceback
+
+from . import _agent
 
 MODE_FILE = "/etc/ck-fused.mode"
 ENV = "CK_FUSED"
@@ -37,29 +43,20 @@ VALIDATED_KITCHEN = ("0.2.40",)
 TAG = "[ck-fused-patch]"
 MODES = ("on", "c1", "c2")
 
+# meta-path finders of the agents are instances of this class
+_Finder = _agent.ImportHook
+
 
 def _read_mode() -> str:
-    env = os.environ.get(ENV)
-    if env:
-        env = env.strip().lower()
-        return "on" if env == "1" else env
-    try:
-        with open(MODE_FILE) as f:
-            return f.read().strip().lower() or "off"
-    except OSError:
-        return "off"
+    return _agent.read_mode(ENV, MODE_FILE, aliases={"1": "on"})
 
 
 def _kitchen_version():
-    try:
-        from importlib.metadata import version
-        return version("comfy-kitchen")
-    except Exception:
-        return None
+    return _agent.kitchen_version()
 
 
 def _say(msg: str) -> None:
-    print(f"{TAG} {msg}", file=sys.stderr, flush=True)
+    _agent.say(TAG, msg)
 
 
 class _Runtime:
@@ -77,6 +74,7 @@ class _Runtime:
         self.c2 = mode in ("on", "c2")
         self.broken = False
         self.warned = False
+        self._weights = {}   # (id(linear), interleaved) -> (stamp, (codes, scale, bias))
 
     # ------------------------------------------------------------------ eligibility
     def eligible(self, block, x, mod_segments) -> bool:
@@ -134,12 +132,73 @@ class _Runtime:
         params = self.Layout.Params(scale=qscale, orig_dtype=y.dtype, orig_shape=(y.shape[0], F))
         return mlp.fc2(self.QT(q, "TensorCoreFP8E4M3Layout", params))
 
+    def fp8_weights(self, linear, interleave: bool):
+        """(e4m3 codes [N, K], float32 scale [1] or [N], bf16 bias [N] or None) of a linear whose
+        weight is a comfy fp8 QuantizedTensor -- gate / up interleaved for the SwiGLU epilogue
+        when asked -- or None for any other form.  Built once per weight and cached (keyed by
+        the weight's storage and version, so a reloaded weight is rebuilt)."""
+        torch = self.torch
+        w = getattr(linear, "weight", None)
+        if not isinstance(w, self.QT):
+            return None
+        codes, params = getattr(w, "qdata", None), getattr(w, "params", None)
+        scale = getattr(params, "scale", None)
+        if not (isinstance(codes, torch.Tensor) and isinstance(scale, torch.Tensor)):
+            return None
+        if codes.dtype != torch.float8_e4m3fn or codes.dim() != 2 or not codes.is_cuda or codes.shape[1] % 16:
+            return None
+        N = codes.shape[0]
+        if scale.numel() not in (1, N) or (interleave and N % 256):
+            return None
+        bias = getattr(linear, "bias", None)
+        if bias is not None and (not isinstance(bias, torch.Tensor) or bias.numel() != N):
+            return None
+        stamp = (codes.data_ptr(), codes._version, scale.data_ptr(), None if bias is None else bias.data_ptr())
+        key = (id(linear), interleave)
+        hit = self._weights.get(key)
+        if hit is not None and hit[0] == stamp:
+            return hit[1]
+        scale = scale.to(device=codes.device, dtype=torch.float32).reshape(-1).contiguous()
+        if bias is not None:
+            bias = self.mm.cast_to(bias, device=codes.device, dtype=torch.bfloat16).reshape(-1).contiguous()
+        codes = codes.contiguous()
+        if interleave:
+            il = self.ops.interleave_gate_up
+            codes = il(codes)
+            scale = il(scale) if scale.numel() > 1 else scale
+            bias = None if bias is None else il(bias)
+        value = (codes, scale, bias)
+        self._weights[key] = (stamp, value)
+        return value
+
+    def mlp_and_gate(self, mlp, h, x, gate, rows):
+        """x + gate[row] * fc2(SwiGLU(fc1(h))) on the library's fp8 GEMMs (cluster 2 with fp8
+        weights), or None when the linears are not in that form.  h is cluster 1's fp8
+        QuantizedTensor (its one scale given per row) or a bf16 tensor (quantised per token)."""
+        torch = self.torch
+        fc1 = self.fp8_weights(mlp.fc1, interleave=True)
+        fc2 = self.fp8_weights(mlp.fc2, interleave=False)
+        if fc1 is None or fc2 is None:
+            return None
+        (w1, s1, b1), (w2, s2, b2) = fc1, fc2
+        S = x.shape[0]
+        if isinstance(h, self.QT):
+            a = h.qdata
+            a_scale = h.params.scale.to(torch.float32).reshape(1).expand(S).contiguous()
+        else:
+            a, a_scale = self.ops.quant_rows(h.contiguous(), "fp8_e4m3")
+        if a.dtype != torch.float8_e4m3fn or tuple(a.shape) != (S, w1.shape[1]) or w2.shape[1] != w1.shape[0] // 2:
+            return None
+        act = self.ops.gemm_swiglu(a.contiguous(), w1, a_scale, s1, b1)
+        q, q_scale = self.ops.quant_rows(act, "fp8_e4m3")
+        return self.ops.gemm_gated(q, w2, q_scale, s2, b2, x, gate.to(torch.bfloat16).contiguous(), gate_index=rows)
+
     # ------------------------------------------------------------------ block
     def forward(self, block, x, t_emb, mod_segments, rope_freqs, transformer_options, attention):
         model = self.model
         shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp = block.adaln_proj(t_emb)
         attn = block.attn if attention is None else attention
-        rows = self.row_map(mod_segments, x.shape[0], x.device) if self.c1 else None
+        rows = self.row_map(mod_segments, x.shape[0], x.device)
         if self.c1:
             h1 = self.norm_quant(block.norm1, x, shift_msa, scale_msa, rows)
         else:
@@ -150,7 +209,13 @@ class _Runtime:
             h2 = self.norm_quant(block.norm2, x, shift_mlp, scale_mlp, rows)
         else:
             h2 = model._mod_scale_shift(block.norm2(x), shift_mlp, scale_mlp, mod_segments)
-        out = self.mlp(block.mlp, h2) if self.c2 else block.mlp(h2)
+        if self.c2:
+            done = self.mlp_and_gate(block.mlp, h2, x, gate_mlp, rows)
+            if done is not None:
+                return done
+            out = self.mlp(block.mlp, h2)
+        else:
+            out = block.mlp(h2)
         return model._mod_gate(x, gate_mlp, out, mod_segments)
 
     def fail(self, exc) -> None:
@@ -191,29 +256,6 @@ def _apply(mod, mode: str) -> None:
         _say(f"NOT applied ({exc!r:.200}); running stock")
 
 
-class _Finder(importlib.abc.MetaPathFinder):
-    """Patches the target module right after it executes."""
-
-    def __init__(self, mode: str):
-        self.mode = mode
-
-    def find_spec(self, name, path, target=None):
-        if name != TARGET:
-            return None
-        spec = importlib.machinery.PathFinder.find_spec(name, path)
-        if spec is None or spec.loader is None:
-            return None
-        loader, mode = spec.loader, self.mode
-        run = loader.exec_module
-
-        def exec_module(module):
-            run(module)
-            _apply(module, mode)
-
-        loader.exec_module = exec_module
-        return spec
-
-
 def install() -> None:
     mode = _read_mode()
     if mode not in MODES:
@@ -224,10 +266,7 @@ def install() -> None:
     if ver not in VALIDATED_KITCHEN:
         _say(f"NOT applied: comfy-kitchen {ver} is not validated ({', '.join(VALIDATED_KITCHEN)}); running stock")
         return
-    if TARGET in sys.modules:
-        _apply(sys.modules[TARGET], mode)
-    elif not any(isinstance(f, _Finder) for f in sys.meta_path):
-        sys.meta_path.insert(0, _Finder(mode))
+    _agent.when_imported(__name__, {TARGET: lambda module: _apply(module, mode)})
 
 
 def install_safely() -> None:

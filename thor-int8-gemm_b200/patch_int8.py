@@ -1,53 +1,52 @@
-"""comfy-kitchen INT8 GEMM override that routes `_C.cutlass_int8_dequant` to this
-library's sm_100a kernel.  Drop-in for the reference agent
-src/ck_int8_patch_thor.py (same modes, mode file, environment variable, version
-guard, eligibility rules, fallback latch and stderr tag), loaded the same way:
-from a `.pth` file in site-packages (see `write_pth`), so every interpreter in the
-venv gets it without code changes.
+"""comfy-kitchen INT8 GEMM override: `_C.cutlass_int8_dequant` served by this library's
+sm_100a kernel.
 
-Modes (env CK_INT8_MODE, else /etc/comfy-kitchen-int8.mode, else "off"):
+A drop-in for the reference agent src/ck_int8_patch_thor.py: the same modes, mode file,
+environment variable, comfy-kitchen version guard, eligibility rules, fall-back latch and
+stderr tag, loaded the same way -- from a `.pth` file in site-packages (`write_pth`), so
+every interpreter of the environment gets it without code changes.
+
+Modes (environment CK_INT8_MODE, else /etc/comfy-kitchen-int8.mode, else "off"):
   off     stock comfy-kitchen
-  cublas  comfy-kitchen's own cuBLAS route (sets `_DISABLE_CUTLASS_INT8`)
+  cublas  comfy-kitchen's own cuBLAS route (sets its `_DISABLE_CUTLASS_INT8`)
   b200    `_C.cutlass_int8_dequant` runs on this library's tcgen05 GEMM
-  triton  accepted as a synonym of b200, so an existing mode file keeps working
+  triton  the reference's name for the kernel mode, accepted so an existing mode file works
 
-Nothing here imports torch or loads the CUDA library until a call needs it;
-installing never raises.
+Nothing here imports torch or loads the CUDA library until a call needs it; installing
+never raises.
 """
 from __future__ import annotations
 
-import importlib.abc
-import importlib.machinery
 import os
-import sys
 
-MODE_FILE = "/etc/comfy-kitchen-int8.mode"          # src/ck_int8_patch_thor.py:26
-TARGET = "comfy_kitchen.backends.cuda"               # :27
-TOP = "comfy_kitchen"                                # :28
-VALIDATED_KITCHEN = ("0.2.37", "0.2.40")             # :29
-MIN_M = 128                                          # :30
-KERNEL_MODES = ("b200", "triton")
+from . import _agent
+
+# The deployment contract of the reference agent (src/ck_int8_patch_thor.py:26-30).
+MODE_FILE = "/etc/comfy-kitchen-int8.mode"
+ENV = "CK_INT8_MODE"
+TARGET = "comfy_kitchen.backends.cuda"
+TOP = "comfy_kitchen"
+VALIDATED_KITCHEN = ("0.2.37", "0.2.40")
+MIN_M = 128
 TAG = "[ck-int8-patch]"
+KERNEL_MODES = ("b200", "triton")
+ACTIVE_MODES = ("cublas",) + KERNEL_MODES
+KNOWN_MODES = ("off",) + ACTIVE_MODES
+
+# meta-path finders of the agents are instances of this class
+_Finder = _agent.ImportHook
+
+
+def _say(message: str) -> None:
+    _agent.say(TAG, message)
 
 
 def _read_mode() -> str:
-    """src/ck_int8_patch_thor.py:34-42."""
-    m = os.environ.get("CK_INT8_MODE")
-    if m:
-        return m.strip().lower()
-    try:
-        with open(MODE_FILE) as f:
-            return f.read().strip().lower() or "off"
-    except OSError:
-        return "off"
+    return _agent.read_mode(ENV, MODE_FILE)
 
 
 def _kitchen_version():
-    try:
-        from importlib.metadata import version
-        return version("comfy-kitchen")
-    except Exception:
-        return None
+    return _agent.kitchen_version()
 
 
 def _b200_gemm(x8, w8, x_scale, w_scale, bias, out, stream=None):
@@ -62,7 +61,7 @@ _capsule_tried = False
 
 def _capsule_entry():
     """The compiled capsule fast path (`_t8g_capsule.cutlass_int8_dequant`), or None when the
-    module is not built (the general path below then serves every call)."""
+    module is not built (the general path then serves every call)."""
     global _capsule_fn, _capsule_tried
     if not _capsule_tried:
         _capsule_tried = True
@@ -82,9 +81,37 @@ def _stream_arg(stream):
         return None
 
 
+def _decline_reason(tx, tw, txs, tws, tb, tout):
+    """Why this call stays on the stock kernel, or None when this library takes it.
+
+    The rules are the stock CUTLASS kernel's own eligibility, as the reference agent
+    mirrors it (src/ck_int8_patch_thor.py:148-156), so that whatever CUTLASS would decline
+    (and comfy-kitchen would then route to cuBLAS) keeps its stock route."""
+    import torch
+    if tx.dim() != 2 or tw.dim() != 2:
+        return "x or w is not a matrix"
+    (M, K), N = tx.shape, tw.shape[0]
+    rules = (
+        (M >= MIN_M, f"M={M} below {MIN_M}"),
+        (K % 16 == 0, f"K={K} not a multiple of 16"),
+        (tx.dtype == torch.int8 and tw.dtype == torch.int8, "x and w must both be int8"),
+        (tw.shape[1] == K, "w is not [N, K]"),
+        (tx.is_contiguous() and tw.is_contiguous() and tout.is_contiguous(), "x, w and out must be contiguous"),
+        (tout.dtype in (torch.bfloat16, torch.float16, torch.float32), f"output dtype {tout.dtype}"),
+        (tuple(tout.shape) == (M, N), "out is not [M, N]"),
+        (txs.dtype == torch.float32 and txs.numel() == M, "x_scale is not float32 with M elements"),
+        (tws.dtype == torch.float32 and tws.numel() in (1, N), "w_scale is not float32 with 1 or N elements"),
+        (tb.numel() in (0, N), "bias has neither 0 nor N elements"),
+        (tb.numel() == 0 or tb.dtype == tout.dtype, "bias dtype differs from the output dtype"),
+    )
+    return next((why for ok, why in rules if not ok), None)
+
+
 class _CProxy:
-    """Stands in for comfy_kitchen.backends.cuda._C and takes over cutlass_int8_dequant
-    (src/ck_int8_patch_thor.py:130-168)."""
+    """Stands in for comfy_kitchen.backends.cuda._C (src/ck_int8_patch_thor.py:130-168):
+    `cutlass_int8_dequant` goes to the B200 GEMM when the call is eligible, every other
+    attribute to the real module.  The first failure of the B200 path (an exception from
+    the launch) prints a traceback and sends this and every later call to stock."""
 
     def __init__(self, real, gemm=_b200_gemm):
         self._real = real
@@ -96,147 +123,108 @@ class _CProxy:
             raise AttributeError(name)
         return getattr(self._real, name)
 
+    def _give_up(self, exc) -> None:
+        import traceback
+        self._broken = True
+        _say(f"B200 GEMM failed ({exc!r:.200}); stock CUTLASS for the rest of this process\n"
+             + traceback.format_exc())
+
     def _stock(self, tensors, dtype_code, stream):
         return self._real.cutlass_int8_dequant(*(t.__dlpack__(stream=-1) for t in tensors), dtype_code, stream)
 
     def cutlass_int8_dequant(self, x, w, x_scale, w_scale, bias, out, dtype_code, stream):
-        fast = _capsule_entry() if (self._gemm is _b200_gemm and not self._broken) else None
+        if self._broken:
+            return self._real.cutlass_int8_dequant(x, w, x_scale, w_scale, bias, out, dtype_code, stream)
+        fast = _capsule_entry() if self._gemm is _b200_gemm else None
         if fast is not None:
-            # capsules read in place (not consumed): eligible calls launch here, the rest
-            # take the general path below
+            # the capsules are read in place, not consumed: an eligible call launches here,
+            # anything else continues below with the same capsules
             try:
                 if fast(x, w, x_scale, w_scale, bias, out, stream) is True:
                     return True
-            except Exception as exc:  # a rejected launch: stock for the rest of the process
-                import traceback
-                self._broken = True
-                print(f"{TAG} B200 GEMM failed ({exc!r:.200}); stock CUTLASS for the rest of this process\n"
-                      + traceback.format_exc(), file=sys.stderr, flush=True)
+            except Exception as exc:
+                self._give_up(exc)
                 return self._real.cutlass_int8_dequant(x, w, x_scale, w_scale, bias, out, dtype_code, stream)
         import torch
-        tensors = tuple(torch.from_dlpack(t) for t in (x, w, x_scale, w_scale, bias, out))
-        tx, tw, txs, tws, tb, tout = tensors
-        M, K = tx.shape if tx.dim() == 2 else (0, 0)
-        N = tw.shape[0] if tw.dim() == 2 else 0
-        # the CUTLASS eligibility the reference mirrors (:148-156); declined calls stay stock
-        if (self._broken or M < MIN_M or K % 16
-                or not (tx.is_contiguous() and tw.is_contiguous() and tout.is_contiguous())
-                or tx.dtype != torch.int8 or tw.dtype != torch.int8
-                or tw.dim() != 2 or tw.shape[1] != K or tuple(tout.shape) != (M, N)
-                or tout.dtype not in (torch.bfloat16, torch.float16, torch.float32)
-                or txs.dtype != torch.float32 or txs.numel() != M
-                or tws.dtype != torch.float32 or tws.numel() not in (1, N)
-                or tb.numel() not in (0, N) or (tb.numel() and tb.dtype != tout.dtype)):
+        tensors = tuple(torch.from_dlpack(c) for c in (x, w, x_scale, w_scale, bias, out))
+        if _decline_reason(*tensors) is not None:
             return self._stock(tensors, dtype_code, stream)
         try:
-            self._gemm(tx, tw, txs, tws, tb, tout, _stream_arg(stream))
-        except Exception as exc:  # stay numerically safe: stock for the rest of the process
-            import traceback
-            self._broken = True
-            print(f"{TAG} B200 GEMM failed ({exc!r:.200}); stock CUTLASS for the rest of this process\n"
-                  + traceback.format_exc(), file=sys.stderr, flush=True)
+            self._gemm(*tensors, _stream_arg(stream))
+        except Exception as exc:
+            self._give_up(exc)
             return self._stock(tensors, dtype_code, stream)
         return True
 
 
-def _apply(mod, mode):
+def _apply(cuda_backend, mode: str) -> None:
+    """Version guard, then the mode's change to comfy_kitchen.backends.cuda; never raises."""
     try:
-        _apply_unguarded(mod, mode)
+        ver = _kitchen_version()
+        if ver not in VALIDATED_KITCHEN:
+            _say(f"NOT applied: comfy-kitchen {ver} is not validated ({', '.join(VALIDATED_KITCHEN)}); running stock")
+            return
+        if mode == "cublas":
+            cuda_backend._DISABLE_CUTLASS_INT8 = True
+        elif mode in KERNEL_MODES and not isinstance(cuda_backend._C, _CProxy):
+            cuda_backend._C = _CProxy(cuda_backend._C)
+        _say(f"comfy_kitchen {ver} int8 mode={mode}")
     except Exception as exc:
-        print(f"{TAG} NOT applied ({exc!r:.200}); running stock", file=sys.stderr, flush=True)
+        _say(f"NOT applied ({exc!r:.200}); running stock")
 
 
-def _apply_unguarded(mod, mode):
-    """Version guard, then swap `_C` (src/ck_int8_patch_thor.py:178-188)."""
-    ver = _kitchen_version()
-    if ver not in VALIDATED_KITCHEN:
-        print(f"{TAG} NOT applied: comfy-kitchen {ver} is not validated "
-              f"({', '.join(VALIDATED_KITCHEN)}); running stock", file=sys.stderr, flush=True)
+def _compile_safe_int8_linear(top) -> None:
+    """Make comfy_kitchen.int8_linear traceable by torch.compile (src/ck_int8_patch_thor.py:
+    191-216): its eager body exports DLPack capsules, which FakeTensors cannot, so while
+    dynamo traces, calls go to comfy-kitchen's registered custom op comfy_kitchen::int8_linear
+    (which has a fake kernel) with the output dtype given as comfy's dtype code.  Eager calls
+    reach the original function unchanged."""
+    if not hasattr(top, "int8_linear"):
         return
-    if mode == "cublas":
-        mod._DISABLE_CUTLASS_INT8 = True
-    elif mode in KERNEL_MODES:
-        if not isinstance(mod._C, _CProxy):
-            mod._C = _CProxy(mod._C)
-    print(f"{TAG} comfy_kitchen {ver} int8 mode={mode}", file=sys.stderr, flush=True)
-
-
-def _compile_safe_int8_linear(top):
-    """While torch.compile traces, route comfy_kitchen.int8_linear through its
-    registered custom op (src/ck_int8_patch_thor.py:191-216); eager calls are untouched."""
     try:
+        import functools
+        import inspect
+
         import torch
         from comfy_kitchen.backends.eager.quantization import DTYPE_CODE_TO_DTYPE
-        if _kitchen_version() not in VALIDATED_KITCHEN or getattr(top.int8_linear, "_ck_compile_safe", False):
-            return
-        code_of = {dt: code for code, dt in DTYPE_CODE_TO_DTYPE.items()}
         eager = top.int8_linear
+        if _kitchen_version() not in VALIDATED_KITCHEN or getattr(eager, "_ck_compile_safe", False):
+            return
+        signature = inspect.signature(eager)
+        order = list(signature.parameters)
+        code_of = {dtype: code for code, dtype in DTYPE_CODE_TO_DTYPE.items()}
 
-        def int8_linear(x, weight, weight_scale, bias=None, out_dtype=None, convrot=False,
-                        convrot_groupsize=256, input_act=None, input_act_weight=None,
-                        input_act_eps=0.0, residual=None, residual_scale=None):
-            if torch.compiler.is_compiling():
-                return torch.ops.comfy_kitchen.int8_linear(
-                    x, weight, weight_scale, bias, code_of[out_dtype or torch.bfloat16],
-                    convrot, convrot_groupsize, input_act, input_act_weight, input_act_eps,
-                    residual, residual_scale)
-            return eager(x, weight, weight_scale, bias, out_dtype, convrot, convrot_groupsize,
-                         input_act, input_act_weight, input_act_eps, residual, residual_scale)
+        @functools.wraps(eager)
+        def int8_linear(*args, **kwargs):
+            if not torch.compiler.is_compiling():
+                return eager(*args, **kwargs)
+            call = signature.bind(*args, **kwargs)
+            call.apply_defaults()
+            values = dict(call.arguments)
+            values["out_dtype"] = code_of[values["out_dtype"] or torch.bfloat16]
+            return torch.ops.comfy_kitchen.int8_linear(*(values[name] for name in order))
 
         int8_linear._ck_compile_safe = True
-        int8_linear.__wrapped__ = eager
         top.int8_linear = int8_linear
     except Exception as exc:
-        print(f"{TAG} compile-safe int8_linear NOT applied ({exc!r:.200})", file=sys.stderr, flush=True)
+        _say(f"compile-safe int8_linear NOT applied ({exc!r:.200})")
 
 
-class _Finder(importlib.abc.MetaPathFinder):
-    """Applies the patch when comfy-kitchen is imported (src/ck_int8_patch_thor.py:219-240)."""
-
-    def __init__(self, mode):
-        self.mode = mode
-
-    def find_spec(self, name, path, target=None):
-        if name not in (TARGET, TOP):
-            return None
-        spec = importlib.machinery.PathFinder.find_spec(name, path)
-        if spec is None or spec.loader is None:
-            return None
-        loader, mode = spec.loader, self.mode
-        orig_exec = loader.exec_module
-
-        def exec_module(module):
-            orig_exec(module)
-            if name == TARGET:
-                _apply(module, mode)
-            else:
-                _compile_safe_int8_linear(module)
-
-        loader.exec_module = exec_module
-        return spec
-
-
-def install():
-    """src/ck_int8_patch_thor.py:243-254."""
+def install() -> None:
+    """Read the mode and hook comfy-kitchen (now, or when it is imported)."""
     mode = _read_mode()
-    if mode not in ("off", "cublas") + KERNEL_MODES:
-        print(f"{TAG} unknown mode {mode!r} in {MODE_FILE}; running stock", file=sys.stderr, flush=True)
-    if mode not in ("cublas",) + KERNEL_MODES:
+    if mode not in KNOWN_MODES:
+        _say(f"unknown mode {mode!r} in {MODE_FILE}; running stock")
+    if mode not in ACTIVE_MODES:
         return
-    if TARGET in sys.modules:
-        _apply(sys.modules[TARGET], mode)
-    if TOP in sys.modules and hasattr(sys.modules[TOP], "int8_linear"):
-        _compile_safe_int8_linear(sys.modules[TOP])
-    if TARGET not in sys.modules or TOP not in sys.modules:
-        if not any(isinstance(f, _Finder) for f in sys.meta_path):
-            sys.meta_path.insert(0, _Finder(mode))
+    _agent.when_imported(__name__, {TARGET: lambda module: _apply(module, mode), TOP: _compile_safe_int8_linear})
 
 
-def install_safely():
+def install_safely() -> None:
     try:
         install()
-    except Exception as exc:  # never break interpreter start-up
-        print(f"{TAG} disabled: {exc!r}", file=sys.stderr)
+    except Exception as exc:  # interpreter start-up must not break
+        _say(f"disabled: {exc!r}")
 
 
 PTH_NAME = "zz_thor_int8_gemm_b200.pth"
