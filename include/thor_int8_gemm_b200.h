@@ -52,6 +52,15 @@ const char* t8g_last_error(void);
  * in which case that kernel's output is incomplete. */
 int t8g_device_status(void* stream, int* status);
 
+/* A host-visible mirror of the status word: *host_word receives the address of a mapped,
+ * pinned host int that every kernel of this library also writes (with a system-visible
+ * store) when one of its bounded waits runs out, on every device this was called for.  A
+ * caller can poll it without synchronising or calling CUDA -- the comfy-kitchen proxy checks
+ * it on every call and stops using the library after a wait ran out -- and clears it by
+ * writing 0.  Set-up (once per device, with that device current) copies the address to the
+ * device, so make the first call before any stream capture. */
+int t8g_status_mirror(int** host_word);
+
 /* The calling thread's current CUDA device, and setting it (cudaGetDevice /
  * cudaSetDevice of the runtime this library uses), for callers without their own. */
 int t8g_get_device(int* device);

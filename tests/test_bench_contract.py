@@ -2,6 +2,7 @@
 and under torchrun with two ranks (rank 0 alone prints; the other rank exits 0)."""
 import json
 import os
+import socket
 import subprocess
 import sys
 
@@ -23,6 +24,8 @@ def _check(d, n_gpus):
     cb = d["cpu_baseline"]
     assert cb["kind"] in ("port", "reference") and cb["cores"] >= 1 and cb["sample"] and cb["value"] == d["value"]
     assert d["e2e"] == {"value": d["value"], "unit": d["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+    # the step time is extrapolated from measured M-slices, and says so
+    assert d["extrapolated"] is True and d["measured_slice"]["ms_per_slice_gemm"] > 0
 
 
 def test_reference_arm_one_rank():
@@ -34,9 +37,16 @@ def test_reference_arm_one_rank():
     _check(lines[0], 1)
 
 
+def _free_port() -> int:
+    with socket.socket(socket.AF_INET, socket.SOCK_STREAM) as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
 def test_reference_arm_two_ranks_prints_once():
     r = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
-                        "--master-addr", "127.0.0.1", "--master-port", "29547", "bench.py", "--impl", "reference",
+                        "--master-addr", "127.0.0.1", "--master-port", str(_free_port()), "bench.py", "--impl",
+                        "reference",
                         "--gpus", "2", "--steps", "1", "--warmup", "0"],
                        cwd=ROOT, capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stderr[-2000:]

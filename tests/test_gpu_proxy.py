@@ -131,3 +131,25 @@ def test_capsule_module_takes_dlpack_1_capsules(ops):
     assert C.cutlass_int8_dequant(*caps, torch.cuda.current_stream().cuda_stream) is True
     torch.cuda.synchronize()
     assert torch.equal(out, ops.gemm_dequant(xq, wq, xs, ws, b))
+
+
+def test_wait_that_ran_out_stops_the_proxy(ops, fast_counter, capsys):
+    """A kernel whose bounded wait runs out (the self-test kernel, which waits on a barrier
+    nothing completes) shows on the host-visible status mirror without a synchronisation; the
+    proxy reads it on its next call, reports it and serves that call and every later one from
+    stock.  The device status word tells the same story and is cleared after."""
+    stock = Stock()
+    proxy = P._CProxy(stock)
+    xq, wq, xs, ws, b, out = problem(ops, 256, 512, 256, seed=12)
+    assert call(proxy, (xq, wq, xs, ws, b, out)) is True          # sets the mirror up for this device
+    word = ops.status_mirror()
+    assert word[0] == 0
+    assert ops.wait_selftest(limit_ns=5_000_000) == 1
+    assert word[0] == 0x1FF
+    assert call(proxy, (xq, wq, xs, ws, b, out)) == "stock"
+    err = capsys.readouterr().err
+    assert "bounded device wait" in err and "0x1ff" in err
+    assert proxy._broken and stock.calls == 1 and word[0] == 0
+    assert call(proxy, (xq, wq, xs, ws, b, out)) == "stock" and stock.calls == 2
+    assert ops.device_status() == 0x1FF
+    assert ops.device_status() == 0

@@ -29,6 +29,7 @@ SIGNATURES = {
     "t8g_version": (ctypes.c_char_p, []),
     "t8g_last_error": (ctypes.c_char_p, []),
     "t8g_device_status": (_i32, [_vp, ctypes.POINTER(_i32)]),
+    "t8g_status_mirror": (_i32, [ctypes.POINTER(ctypes.POINTER(_i32))]),
     "t8g_get_device": (_i32, [ctypes.POINTER(_i32)]),
     "t8g_set_device": (_i32, [_i32]),
     "t8g_gemm_i8_dequant": (_i32, [_vp, _vp, _vp, _vp, _i64, _vp, _i64, _vp, _i32,

@@ -731,7 +731,7 @@ template <int IN, int EPB>
 __device__ __forceinline__ void epilogue_tile_swiglu(const Args& args, const CUtensorMap* tm_out,
                                                      uint8_t (*bufs)[EPB], int& ebuf, uint32_t t_row, int row0,
                                                      int n_tile0, int lane, uint64_t pol_out, float xs_r,
-                                                     const TileParams& tp, const uint32_t* sig) {
+                                                     const TileParams& tp, uint32_t sig) {
   const bool has_bias = args.bias != nullptr;
   const float2 xs2 = make_float2(xs_r, xs_r);
   constexpr int kChunks = BN / 2 / EPI_COLS;
@@ -823,7 +823,7 @@ constexpr int P_STAGE_BYTES = P_A_BYTES + P_B_BYTES;   // per CTA
 // TBN / 2 rows of W per CTA.
 template <int OUT, int TBN = BN>
 struct PairCfg {
-  static_assert(TBN == BN || ((TBN == 128 || TBN == 64) && (OUT == kOutBF16 || OUT == kOutF16)),
+  static_assert(TBN == BN || ((TBN == 192 || TBN == 128 || TBN == 64) && (OUT == kOutBF16 || OUT == kOutF16)),
                 "narrow tiles serve the plain 2-byte outputs");
   static constexpr int kBRows = TBN / 2;             // rows of W per CTA
   static constexpr int kBBytes = kBRows * BK;
@@ -871,7 +871,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
   using Cfg = PairCfg<OUT, TBN>;
   constexpr int P_STAGES = Cfg::kStages;
-  constexpr uint32_t kTmemCols = 2 * TBN;   // double-buffered accumulator
+  // double-buffered accumulator; TMEM is allocated in powers of two (192-wide tiles: 512)
+  constexpr uint32_t kTmemCols = 2 * TBN <= 128 ? 2 * TBN : (2 * TBN <= 256 ? 256 : 512);
   SmemPairOf<OUT, TBN>& s = *reinterpret_cast<SmemPairOf<OUT, TBN>*>(smem_raw + pad);
 
   const int warp = threadIdx.x >> 5;
@@ -1042,7 +1043,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
                                   s.params[acc]);
         else if constexpr (OUT == kOutSwiglu)
           epilogue_tile_swiglu<IN, Cfg::kEpiBytes>(args, &tm_out, s.epi[ew], ebuf, t_row, row0, tn * TBN, lane, pol_out,
-                                                   xs_r, s.params[acc], s.sig);
+                                                   xs_r, s.params[acc], smem_u32(s.sig));
         else if constexpr (Cfg::kEpiCols == 64)
           epilogue_tile_staged64<IN, OUT, Cfg::kEpiBytes, TBN>(args, &tm_out, s.epi[ew], ebuf, t_row, row0, tn * TBN,
                                                                lane, pol_out, xs_r, s.params[acc]);

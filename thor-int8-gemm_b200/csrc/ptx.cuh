@@ -31,8 +31,18 @@ enum DeviceStatus : int {
 // Limit of one wait, in nanoseconds of %globaltimer.
 constexpr uint64_t kWaitLimitNs = 1000ull * 1000ull * 1000ull;
 
+// Optional host-visible copy of the status: a mapped pinned host int that a caller asked for
+// (t8g_status_mirror); null until then.  Written with a plain system-visible store, so a host
+// thread sees a wait that ran out without synchronising or calling into CUDA.
+__device__ int* g_status_mirror;
+
 __device__ __forceinline__ void record_status(int code) {
   atomicCAS(&g_device_status, 0, code);
+  int* mirror = g_status_mirror;
+  if (mirror != nullptr) {
+    *reinterpret_cast<volatile int*>(mirror) = code;
+    __threadfence_system();
+  }
 }
 
 __device__ __forceinline__ uint64_t globaltimer_ns() {

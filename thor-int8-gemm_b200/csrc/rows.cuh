@@ -802,19 +802,18 @@ __device__ __forceinline__ void warp_row_loop_reg(uint8_t* smem, const WarpRingG
     end = nrows;
   }
   const uint64_t policy = policy_evict_first();
-  int64_t issued = 0;   // lane 0 only
   if (lane == 0) {
     for (int i = 0; i < g.stages; ++i) mbar_init(&full[i], 1);
     fence_mbarrier_init();
-    for (int i = 0; i < g.stages; ++i) {
-      const int64_t r = first + i * GW;
-      if (r >= end) break;
-      mbar_arrive_expect_tx(&full[i], g.row_bytes);
-      bulk_load(slots + static_cast<size_t>(i) * g.slot_bytes, src(r), g.row_bytes, &full[i], policy);
-      ++issued;
-    }
   }
   __syncwarp();
+  int64_t issued = 0;   // the same in every lane
+  for (int i = 0; i < g.stages; ++i) {
+    const int64_t r = first + i * GW;
+    if (r >= end) break;
+    warp_ring_issue(&full[i], slots + static_cast<size_t>(i) * g.slot_bytes, src(r), g, lane, policy);
+    ++issued;
+  }
   int st = 0;
   uint32_t ph = 0;
   int64_t k = 0;
@@ -825,12 +824,11 @@ __device__ __forceinline__ void warp_row_loop_reg(uint8_t* smem, const WarpRingG
     uint8_t* slot = slots + static_cast<size_t>(st) * g.slot_bytes;
     auto regs = load(slot);
     __syncwarp();
-    if (lane == 0) {
+    {
       const int64_t r = row + ahead;
       if (r < end) {
-        fence_proxy_async_smem();   // the warp's reads of the slot precede the copy that refills it
-        mbar_arrive_expect_tx(&full[st], g.row_bytes);
-        bulk_load(slot, src(r), g.row_bytes, &full[st], policy);
+        fence_proxy_async_smem();   // the warp's reads of the slot precede the copies that refill it
+        warp_ring_issue(&full[st], slot, src(r), g, lane, policy);
         ++issued;
       }
     }
@@ -1150,14 +1148,18 @@ __global__ void __launch_bounds__(512, 1) rms_mod_warp_reg_kernel(const RmsArgs 
 // pitch each half-warp covers all 32 banks once.
 constexpr int kRefBlock = 2048;
 
+// NCH > 0: the row's chunk count as a compile-time constant (loops unrolled); 0: D / 2048
+// rounded up, at run time.
+template <int NCH = 0>
 __device__ __forceinline__ float ref_sumsq_warp(const uint8_t* row, int D, int lane) {
   const int b = lane >> 1;
   const int e = lane & 1;
-  const int nch = (D + kRefBlock - 1) / kRefBlock;
+  const int nch = NCH > 0 ? NCH : (D + kRefBlock - 1) / kRefBlock;
   float2 r01 = make_float2(0.f, 0.f), r23 = make_float2(0.f, 0.f);
 #pragma unroll
   for (int t = 0; t < 16; ++t) {
     float2 e01 = make_float2(0.f, 0.f), e23 = make_float2(0.f, 0.f);
+#pragma unroll
     for (int c = 0; c < nch; ++c) {
       const int el = c * kRefBlock + b * 128 + t * 8 + e * 4;   // this lane's 4 elements (all in or all out)
       if (el < D) {
@@ -1196,8 +1198,9 @@ __device__ __forceinline__ int64_t mod_row_of(const RmsArgs& a, int64_t row, int
 }
 
 // Phase A of the tensorwise norm, one row per warp (rows of at most kWarpRowMaxBytes, padded
-// layout): h and res stored, each lane's running max of the float32 |h|, folded into the
-// tensor's amax word at the end.
+// layout, NCH = the row's 2048-element chunks): h and res stored, each lane's running max of
+// the float32 |h|, folded into the tensor's amax word at the end.
+template <int NCH>
 __global__ void __launch_bounds__(1024) rms_mod_tw_warp_kernel(const RmsArgs a, const WarpRingGeom g) {
   extern __shared__ __align__(1024) uint8_t smem[];
   const int lane = threadIdx.x & 31;
@@ -1207,7 +1210,7 @@ __global__ void __launch_bounds__(1024) rms_mod_tw_warp_kernel(const RmsArgs a, 
   float tw_max = 0.f;
   auto src = [&](int64_t r) -> const void* { return a.x + r * a.ld_x; };
   warp_row_loop(smem, g, a.S, src, [&](int64_t row, uint8_t* slot) {
-    const float inv = rms_inv_of(ref_sumsq_warp(slot, a.D, lane), fD, a.eps);
+    const float inv = rms_inv_of(ref_sumsq_warp<NCH>(slot, a.D, lane), fD, a.eps);
     const float2 inv2 = make_float2(inv, inv);
     const int64_t m = mod_row_of(a, row, cur_m, seg_end);
 #pragma unroll 2
@@ -1219,6 +1222,81 @@ __global__ void __launch_bounds__(1024) rms_mod_tw_warp_kernel(const RmsArgs a, 
       rms_store8(a, row, c, x, h);
     }
   });
+  flush_amax(a.amax, tw_max);
+}
+
+// Phase A of the tensorwise norm for rows of 256 NV elements (every option of the entry
+// point: norm weight, mod_index, scale as multiplier, res): the warp sums the squares in the
+// reference's order from the padded slot, copies the row into registers (lane l holding
+// vectors 32 k + l) and refills the slot at once, then computes h from the registers.
+template <int NV>
+struct RowRegsSS {
+  uint4 v[NV];
+  float ss;
+};
+
+template <int NV>
+__global__ void __launch_bounds__(512, 1) rms_mod_tw_reg_kernel(const RmsArgs a, const WarpRingGeom g) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  constexpr int D = 256 * NV;
+  constexpr int NCH = (D + kRefBlock - 1) / kRefBlock;
+  const int lane = threadIdx.x & 31;
+  int64_t cur_m = -1, seg_end = -1;
+  float tw_max = 0.f;
+  auto src = [&](int64_t r) -> const void* { return a.x + r * a.ld_x; };
+  warp_row_loop_reg(
+      smem, g, a.S, src,
+      [&](const uint8_t* slot) {
+        RowRegsSS<NV> r;
+        r.ss = ref_sumsq_warp<NCH>(slot, D, lane);
+#pragma unroll
+        for (int k = 0; k < NV; ++k) r.v[k] = lds_v4(slot + padded_vec(32 * k + lane));
+        return r;
+      },
+      [&](int64_t row, RowRegsSS<NV>& r) {
+        const float inv = rms_inv_of(r.ss, static_cast<float>(D), a.eps);
+        const float2 inv2 = make_float2(inv, inv);
+        const int64_t m = mod_row_of(a, row, cur_m, seg_end);
+        const __nv_bfloat16* srow = a.scale + m * a.ld_mod;
+        const __nv_bfloat16* brow = a.shift + m * a.ld_mod;
+#pragma unroll
+        for (int k = 0; k < NV; ++k) {
+          const int c = 32 * k + lane;
+          uint4 su = ld_v4(srow + 8 * c);
+          const uint4 bu = ld_v4(brow + 8 * c);
+          if (!a.scale_is_multiplier)
+            su = make_uint4(one_plus_bf16x2(su.x), one_plus_bf16x2(su.y), one_plus_bf16x2(su.z),
+                            one_plus_bf16x2(su.w));
+          const uint32_t xw[4] = {r.v[k].x, r.v[k].y, r.v[k].z, r.v[k].w};
+          const uint32_t sw[4] = {su.x, su.y, su.z, su.w};
+          const uint32_t bw[4] = {bu.x, bu.y, bu.z, bu.w};
+          uint4 wu = make_uint4(0, 0, 0, 0);
+          if (a.w) wu = ld_v4(a.w + 8 * c);
+          const uint32_t ww[4] = {wu.x, wu.y, wu.z, wu.w};
+          float2 h[4], x[4];
+#pragma unroll
+          for (int p = 0; p < 4; ++p) {
+            x[p] = bf2_to_f2(xw[p]);
+            float2 t = mul2_rn(x[p], inv2);
+            if (a.w) t = mul2_rn(t, bf2_to_f2(ww[p]));
+            t = mul2_rn(t, bf2_to_f2(sw[p]));
+            h[p] = add_f32_bf16x2(t, bw[p]);
+          }
+          tw_max = absmax_f2x4(tw_max, h);
+          if (a.res) {
+            uint4 ru;
+            ru.x = f2_to_bf2(add2_rn(h[0], x[0]));
+            ru.y = f2_to_bf2(add2_rn(h[1], x[1]));
+            ru.z = f2_to_bf2(add2_rn(h[2], x[2]));
+            ru.w = f2_to_bf2(add2_rn(h[3], x[3]));
+            *reinterpret_cast<uint4*>(a.res + row * a.ld_res + 8 * c) = ru;
+          }
+          *reinterpret_cast<uint4*>(a.h + row * a.ld_h + 8 * c) =
+              make_uint4(f2_to_bf2(h[0]), f2_to_bf2(h[1]), f2_to_bf2(h[2]), f2_to_bf2(h[3]));
+          // keep the modulation loads of at most four vectors in flight (register budget)
+          if ((k & 3) == 3) asm volatile("" ::: "memory");
+        }
+      });
   flush_amax(a.amax, tw_max);
 }
 
@@ -1257,8 +1335,9 @@ __global__ void __launch_bounds__(512) rms_mod_tw_cta_kernel(const RmsArgs a, co
 
 // ---------------------------------------------------------------- SwiGLU
 // act for one vector from the gate and up rows in the slot (sigmoid table `sig` in shared
-// memory); returns bf16(act) and folds the float32 |act| into amax32 when asked.
-__device__ __forceinline__ uint4 swiglu8(const uint8_t* gate, const uint8_t* up, int c, const uint32_t* sig,
+// memory, its shared-memory address); returns bf16(act) and folds the float32 |act| into
+// amax32 when asked.
+__device__ __forceinline__ uint4 swiglu8(const uint8_t* gate, const uint8_t* up, int c, uint32_t sig,
                                          float& amax32, bool tensorwise) {
   float2 uv[4], act[4];
   const uint4 gu = lds_v4(gate + 16 * c);
@@ -1281,8 +1360,8 @@ __host__ __device__ inline size_t ring_bytes(const RingGeom& g) {
 template <int V, int MODE>
 __global__ void __launch_bounds__(1024) swiglu_kernel(const SwigluArgs a, const RingGeom g, const int T) {
   extern __shared__ __align__(1024) uint8_t smem[];
-  uint32_t* sig = reinterpret_cast<uint32_t*>(smem);
-  load_sigmoid_table(sig, threadIdx.x, blockDim.x);
+  load_sigmoid_table(reinterpret_cast<uint32_t*>(smem), threadIdx.x, blockDim.x);
+  const uint32_t sig = smem_u32(smem);
   __syncthreads();
   const RowGroup grp = row_group(T);
   uint8_t* ring = smem + kSigmoidBytes + static_cast<size_t>(grp.index) * ring_bytes(g);

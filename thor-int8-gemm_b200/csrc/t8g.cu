@@ -226,31 +226,30 @@ int gemm_entry(int in_kind, const void* x, const void* w, const float* x_scale, 
   // kernel.
   const char* sm_env = getenv("T8G_GEMM_SM");
   const bool force_1sm = sm_env && sm_env[0] == '1';
-  // Tile width of the 2-SM kernel (2-byte outputs): 256, 128 or 64 columns, whichever keeps
-  // the CTA pairs busiest.  The persistent kernel deals tiles round robin, so with T tiles
-  // on P pairs the last wave is partly idle: busy fraction = T / (ceil(T / P) * P).  A
-  // narrower tile re-reads its activation panel for fewer output columns, which costs a
-  // little per tile (kNarrowCost), so it has to win by more than that.  Examples on 74
-  // pairs: M = 8192, N = 3072 -> 384 tiles of 256 (86.5 % busy) or 768 of 128 (94.3 %):
-  // 128; M = 256, N = 3072 -> 12, 24 or 48 tiles: 64.  T8G_GEMM_TBN=256|128|64 forces one.
+  // Tile width of the 2-SM kernel (2-byte outputs).  256 columns by default.  The persistent
+  // kernel deals tiles round robin, so with T tiles on P pairs the last wave is partly idle
+  // (busy fraction T / (ceil(T / P) * P)):
+  //  * few tiles (less than half the pairs busy, small M): 128 or 64 columns put more pairs on
+  //    the problem, each with a shorter tile;
+  //  * otherwise 192-column tiles when they fill the last wave much better (M = 8192,
+  //    N = 3072 on 74 pairs: 384 tiles of 256, 86.5 % busy; 512 of 192, 98.8 %).  A narrower
+  //    tile streams its activation panel for fewer output columns, which costs per tile
+  //    (128-column tiles measured 0.6x the 256-column rate at M = 8192), so only a clear
+  //    gain in the last wave switches.
+  // T8G_GEMM_TBN=256|192|128|64 forces a width (tuning).
   const int64_t pairs_avail = info.sms / 2;
   const int64_t tiles_m = (M + P_BM - 1) / P_BM;
+  auto busy = [&](int w) {
+    const int64_t t = tiles_m * ((N + w - 1) / w);
+    return static_cast<double>(t) / static_cast<double>(((t + pairs_avail - 1) / pairs_avail) * pairs_avail);
+  };
   int tbn = BN;
   if (esz == 2) {
-    constexpr double kNarrowCost[3] = {1.0, 0.96, 0.88};   // 256, 128, 64 columns
-    double best = -1.0;
-    for (int i = 0, w = BN; i < 3; ++i, w /= 2) {
-      const int64_t tiles = tiles_m * ((N + w - 1) / w);
-      const int64_t waves = (tiles + pairs_avail - 1) / pairs_avail;
-      const double score = kNarrowCost[i] * static_cast<double>(tiles) / static_cast<double>(waves * pairs_avail);
-      if (score > best + 1e-9) {
-        best = score;
-        tbn = w;
-      }
-    }
+    while (tbn > 64 && tiles_m * ((N + tbn - 1) / tbn) * 2 < pairs_avail) tbn /= 2;
+    if (tbn == BN && busy(BN) < 0.92 && busy(192) >= busy(BN) + 0.08) tbn = 192;
     if (const char* force = getenv("T8G_GEMM_TBN")) {
       const int f = atoi(force);
-      if (f == 256 || f == 128 || f == 64) tbn = f;
+      if (f == 256 || f == 192 || f == 128 || f == 64) tbn = f;
     }
   }
   const bool pair = (M > BM || tbn < BN) && !force_1sm;
@@ -284,12 +283,18 @@ int gemm_entry(int in_kind, const void* x, const void* w, const float* x_scale, 
     // narrow tiles (2-byte outputs only)
     const bool f16 = out_dtype == T8G_OUT_F16;
     if (in_kind == kInI8) {
+      if (tbn == 192)
+        return f16 ? launch_gemm_pair<kInI8, kOutF16, 192>(ta, tb, to, args, dev, info.sms, st)
+                   : launch_gemm_pair<kInI8, kOutBF16, 192>(ta, tb, to, args, dev, info.sms, st);
       if (tbn == 128)
         return f16 ? launch_gemm_pair<kInI8, kOutF16, 128>(ta, tb, to, args, dev, info.sms, st)
                    : launch_gemm_pair<kInI8, kOutBF16, 128>(ta, tb, to, args, dev, info.sms, st);
       return f16 ? launch_gemm_pair<kInI8, kOutF16, 64>(ta, tb, to, args, dev, info.sms, st)
                  : launch_gemm_pair<kInI8, kOutBF16, 64>(ta, tb, to, args, dev, info.sms, st);
     }
+    if (tbn == 192)
+      return f16 ? launch_gemm_pair<kInE4M3, kOutF16, 192>(ta, tb, to, args, dev, info.sms, st)
+                 : launch_gemm_pair<kInE4M3, kOutBF16, 192>(ta, tb, to, args, dev, info.sms, st);
     if (tbn == 128)
       return f16 ? launch_gemm_pair<kInE4M3, kOutF16, 128>(ta, tb, to, args, dev, info.sms, st)
                  : launch_gemm_pair<kInE4M3, kOutBF16, 128>(ta, tb, to, args, dev, info.sms, st);
@@ -758,10 +763,21 @@ int rms_common(bool tensorwise, const void* x, int64_t ld_x, const void* w, cons
   if (tensorwise) {
     // phase A sums the squares in the reference's order (rows in the padded layout)
     T8G_CHECK_CUDA(cudaMemsetAsync(amax, 0, sizeof(float), st), "cudaMemsetAsync(amax)");
-    if (warp_rows) {
+    if (nv) {
+      WarpLaunch o = reg_launch;
+      o.padded = true;
+      T8G_DISPATCH_NV(nv, rc = launch_warp_rows(rms_mod_tw_reg_kernel<NV>, a, row_bytes, S, dev, info.sms, st, o,
+                                                "rms_mod phase A"));
+    } else if (warp_rows) {
       WarpLaunch o;
       o.padded = true;
-      rc = launch_warp_rows(rms_mod_tw_warp_kernel, a, row_bytes, S, dev, info.sms, st, o, "rms_mod phase A");
+      const int64_t nch = (D + kRefBlock - 1) / kRefBlock;   // 1..4 for rows of at most 16 KB
+      switch (nch) {
+        case 1: rc = launch_warp_rows(rms_mod_tw_warp_kernel<1>, a, row_bytes, S, dev, info.sms, st, o, "rms_mod phase A"); break;
+        case 2: rc = launch_warp_rows(rms_mod_tw_warp_kernel<2>, a, row_bytes, S, dev, info.sms, st, o, "rms_mod phase A"); break;
+        case 3: rc = launch_warp_rows(rms_mod_tw_warp_kernel<3>, a, row_bytes, S, dev, info.sms, st, o, "rms_mod phase A"); break;
+        default: rc = launch_warp_rows(rms_mod_tw_warp_kernel<4>, a, row_bytes, S, dev, info.sms, st, o, "rms_mod phase A"); break;
+      }
     } else {
       rc = launch_rows(rms_mod_tw_cta_kernel, rsh.T, a, ring_geom(D, 1, true), S, dev, info.sms, st,
                        "rms_mod phase A");
@@ -879,6 +895,12 @@ constexpr uint64_t kNoAllocHOffset = 256;
 void* g_noalloc_addr[kMaxDevices] = {};
 std::mutex g_noalloc_mu;
 
+// The host-visible status mirror (t8g_status_mirror): one mapped pinned int for the process,
+// its device address stored once per device.
+int* g_mirror_host = nullptr;
+bool g_mirror_set[kMaxDevices] = {};
+std::mutex g_mirror_mu;
+
 // Device address of g_noalloc_scratch on device `dev` (which must be current); looked up
 // on the first use per device and cached.
 int noalloc_scratch(int dev, unsigned char** out) {
@@ -925,6 +947,31 @@ int t8g_device_status(void* stream, int* status) {
     T8G_CHECK_CUDA(cudaMemcpyToSymbol(t8g::g_device_status, &zero, sizeof(int)), "cudaMemcpyToSymbol");
   }
   *status = v;
+  return T8G_OK;
+}
+
+int t8g_status_mirror(int** host_word) {
+  g_last_error[0] = '\0';
+  if (!host_word) return fail(T8G_ERR_INVALID_ARGUMENT, "host_word is null");
+  int dev;
+  DeviceInfo info;
+  int rc = current_device(&dev, &info);
+  if (rc) return rc;
+  std::lock_guard<std::mutex> lk(g_mirror_mu);
+  if (!g_mirror_host) {
+    void* p = nullptr;
+    T8G_CHECK_CUDA(cudaHostAlloc(&p, sizeof(int), cudaHostAllocMapped | cudaHostAllocPortable),
+                   "cudaHostAlloc(status mirror)");
+    g_mirror_host = static_cast<int*>(p);
+    *g_mirror_host = 0;
+  }
+  if (!g_mirror_set[dev]) {
+    void* dptr = nullptr;
+    T8G_CHECK_CUDA(cudaHostGetDevicePointer(&dptr, g_mirror_host, 0), "cudaHostGetDevicePointer(status mirror)");
+    T8G_CHECK_CUDA(cudaMemcpyToSymbol(t8g::g_status_mirror, &dptr, sizeof(dptr)), "cudaMemcpyToSymbol(status mirror)");
+    g_mirror_set[dev] = true;
+  }
+  *host_word = g_mirror_host;
   return T8G_OK;
 }
 

@@ -434,6 +434,24 @@ def device_status(device=None, stream=None) -> int:
     return st.value
 
 
+_status_words = {}
+
+
+def status_mirror(device=None):
+    """The host-visible mirror of the device status word (a ctypes pointer to one int, shared by
+    every device), set up for `device` on first use: nonzero once any kernel's bounded wait ran
+    out.  Read it with `[0]`, clear it by assigning 0; no synchronisation or CUDA call involved."""
+    device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    word = _status_words.get(device.index)
+    if word is None:
+        word = ctypes.POINTER(ctypes.c_int)()
+        with _on(device):
+            rc = _lib.load().t8g_status_mirror(ctypes.byref(word))
+        _lib.check(rc)
+        _status_words[device.index] = word
+    return word
+
+
 def wait_selftest(limit_ns: int = 20_000_000, device=None) -> int:
     """Run the bounded-wait self-test kernel; returns 1 if the wait gave up."""
     device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)

@@ -117,6 +117,30 @@ class _CProxy:
         self._real = real
         self._gemm = gemm
         self._broken = False
+        self._watched = {}   # device index -> the library's host-visible status word
+
+    def _wait_ran_out(self) -> int:
+        """The status a kernel of this library recorded when one of its bounded waits ran out
+        (0: none), read from the host-visible mirror without synchronising.  A launch whose
+        wait gave up has left its output incomplete; comfy has consumed it already, so all
+        the proxy can do is stop using the library from the next call on."""
+        try:
+            import torch
+            if not torch.cuda.is_available():
+                return 0
+            dev = torch.cuda.current_device()
+            word = self._watched.get(dev)
+            if word is None:
+                if torch.cuda.is_current_stream_capturing():
+                    return 0                           # set up on a later, uncaptured call
+                from . import ops
+                word = self._watched[dev] = ops.status_mirror(dev)
+            code = word[0]
+            if code:
+                word[0] = 0
+            return code
+        except Exception:
+            return 0
 
     def __getattr__(self, name):
         if name.startswith("_"):
@@ -124,15 +148,21 @@ class _CProxy:
         return getattr(self._real, name)
 
     def _give_up(self, exc) -> None:
+        import sys
         import traceback
         self._broken = True
-        _say(f"B200 GEMM failed ({exc!r:.200}); stock CUTLASS for the rest of this process\n"
-             + traceback.format_exc())
+        trace = traceback.format_exc() if sys.exc_info()[0] is not None else ""
+        _say(f"B200 GEMM failed ({exc!r:.200}); stock CUTLASS for the rest of this process\n" + trace)
 
     def _stock(self, tensors, dtype_code, stream):
         return self._real.cutlass_int8_dequant(*(t.__dlpack__(stream=-1) for t in tensors), dtype_code, stream)
 
     def cutlass_int8_dequant(self, x, w, x_scale, w_scale, bias, out, dtype_code, stream):
+        if not self._broken and self._gemm is _b200_gemm:
+            code = self._wait_ran_out()
+            if code:
+                self._give_up(RuntimeError(f"a bounded device wait of the B200 kernels ran out (status {code:#x}); "
+                                           "an earlier output of this library may be incomplete"))
         if self._broken:
             return self._real.cutlass_int8_dequant(x, w, x_scale, w_scale, bias, out, dtype_code, stream)
         fast = _capsule_entry() if self._gemm is _b200_gemm else None
