@@ -546,7 +546,9 @@ def _graph_ms(torch, stream, fn, calls, replays):
 
 def time_mlp_chain(torch, ops, dev, steps, warmup, stream, seed):
     """DiT SwiGLU MLP, hidden 3072 / FFN 12288 on 32768 tokens: int8 up-GEMM (N 24576, bf16
-    out) -> SwiGLU + per-token int8 quant -> int8 down-GEMM (K 12288, N 3072)."""
+    out) -> SwiGLU + per-token int8 quant -> int8 down-GEMM (K 12288, N 3072); and the fused
+    chain: up-GEMM with the SwiGLU in its epilogue (which also reports every row's max |act|)
+    -> streaming per-token quant of act -> down-GEMM."""
     M, H, F = 32768, 3072, 12288
     gen = torch.Generator(device=dev)
     gen.manual_seed(seed)
@@ -585,15 +587,20 @@ def time_mlp_chain(torch, ops, dev, steps, warmup, stream, seed):
     def up_fused():
         ops.gemm_swiglu(xq, wu_il, xs, wus_il, bu_il, out=a_buf, stream=stream)
 
+    def up_fused_quant():
+        return ops.gemm_swiglu_quant(xq, wu_il, xs, wus_il, bu_il, kind="int8", act=a_buf, stream=stream)
+
     def chain_fused():
-        up_fused()
-        a, s_ = ops.quant_rows(a_buf, "int8", stream=stream)
+        a, s_, _ = up_fused_quant()
         ops.gemm_dequant(a, wd, s_, wds, bd, out=out, stream=stream)
 
     ms_fused = _event_ms(torch, stream, chain_fused, steps, warmup)
-    parts_fused = {"up_gemm_swiglu": round(_event_ms(torch, stream, up_fused, steps, 1), 4),
-                   "quant_act": round(_event_ms(torch, stream, lambda: ops.quant_rows(a_buf, "int8", stream=stream),
-                                                steps, 1), 4)}
+    up_ms = _event_ms(torch, stream, up_fused, steps, 1)
+    parts_fused = {"up_gemm_swiglu": round(up_ms, 4),
+                   "up_gemm_swiglu_with_row_max_and_quant": round(_event_ms(torch, stream, up_fused_quant, steps, 1), 4),
+                   "quant_rows_act_alone": round(_event_ms(torch, stream,
+                                                           lambda: ops.quant_rows(a_buf, "int8", stream=stream),
+                                                           steps, 1), 4)}
     ops_chain = 2.0 * M * H * 2 * F + 2.0 * M * F * H
     return {"ms": round(ms, 4), "tops": round(ops_chain / (ms / 1e3) / 1e12, 1), "parts_ms": parts,
             "fused_ms": round(ms_fused, 4), "fused_tops": round(ops_chain / (ms_fused / 1e3) / 1e12, 1),

@@ -119,6 +119,29 @@ int t8g_gemm_fp8_swiglu(const void* x, const void* w, const float* x_scale, cons
                         int64_t K, int64_t ld_x, int64_t ld_w, int64_t ld_act, void* stream);
 
 /*
+ * fc1 + SwiGLU + per-token quantisation of act for the next linear (the reference's
+ * swiglu_linear up to fc2's input, src/ck_fused_patch.py:139-149): t8g_gemm_i8_swiglu, whose
+ * epilogue also reports act_amax[m] = max_j |act[m, j]| (bf16 values; an atomic max per row and
+ * tile into the caller's float32 [M] buffer, zeroed by this call), then a streaming pass
+ *   q_scale[m] = max(act_amax[m] / qmax, 1e-12),  q[m, j] = cvt(clamp(act[m, j] / q_scale[m]))
+ * equal bit for bit to t8g_quant_rows(act).  A row's scale needs the whole row, which spans
+ * many GEMM tiles, so q cannot be written by the epilogue itself; with the row maxima known the
+ * quantiser reads act once as a plain stream (no row held in shared memory, no reduction).
+ *   act [M, F] bf16 (ld_act, also returned), act_amax float32 [M] scratch, q [M, F] of
+ *   quant_kind (ld_q), q_scale float32 [M]; the rest as t8g_gemm_i8_swiglu.
+ */
+int t8g_gemm_i8_swiglu_quant(const void* x, const void* w, const float* x_scale, const float* w_scale,
+                             int64_t w_scale_numel, const void* bias, int64_t bias_numel, void* act, int64_t ld_act,
+                             float* act_amax, void* q, int64_t ld_q, float* q_scale, int64_t M, int64_t F, int64_t K,
+                             int64_t ld_x, int64_t ld_w, int quant_kind, void* stream);
+
+/* float8_e4m3fn twin of t8g_gemm_i8_swiglu_quant (quant_kind selects act's codes). */
+int t8g_gemm_fp8_swiglu_quant(const void* x, const void* w, const float* x_scale, const float* w_scale,
+                              int64_t w_scale_numel, const void* bias, int64_t bias_numel, void* act, int64_t ld_act,
+                              float* act_amax, void* q, int64_t ld_q, float* q_scale, int64_t M, int64_t F, int64_t K,
+                              int64_t ld_x, int64_t ld_w, int quant_kind, void* stream);
+
+/*
  * Fused-dequant GEMM whose epilogue applies the DiT block's gated residual, the stock
  * `x = _mod_gate(x, gate, proj(h), mod_segments)` after the attention and MLP projections
  * (the block's call order, src/ck_fused_patch.py:153-172), in torch's bf16 operation order:

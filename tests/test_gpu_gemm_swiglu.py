@@ -85,3 +85,19 @@ def test_fused_swiglu_rejects(ops):
         ops.gemm_swiglu(xq, wq[:192], xs, ws[:192])           # 2F not a multiple of 256
     with pytest.raises(TypeError):
         ops.gemm_swiglu(xq, wq, xs, ws, b.float())            # bias must be bf16
+
+
+@pytest.mark.parametrize("kind,in_kind", [("int8", "int8"), ("fp8_e4m3", "int8"), ("fp8_e4m3", "fp8_e4m3")])
+@pytest.mark.parametrize("M,K,F", [(300, 1024, 384), (129, 256, 128), (2048, 3072, 12288)])
+def test_swiglu_quant_entry_equals_quant_of_fused_act(ops, kind, in_kind, M, K, F):
+    """fc1 + SwiGLU + per-token quant in one call (the epilogue's row maxima, then a streaming
+    quantiser) gives act, the scales and the codes of gemm_swiglu followed by quant_rows,
+    bit for bit -- including rows past the last full 128-row block."""
+    xq, xs, wq, ws, b = _problem(ops, M, K, F, in_kind, True, M * 3 + F)
+    il = ops.interleave_gate_up
+    act_ref = ops.gemm_swiglu(xq, il(wq), xs, il(ws), il(b))
+    q_ref, qs_ref = ops.quant_rows(act_ref, kind)
+    q, qs, act = ops.gemm_swiglu_quant(xq, il(wq), xs, il(ws), il(b), kind=kind)
+    assert torch.equal(act, act_ref)
+    assert torch.equal(qs, qs_ref)
+    assert torch.equal(q.view(torch.uint8), q_ref.view(torch.uint8))

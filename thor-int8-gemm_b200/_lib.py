@@ -38,6 +38,10 @@ SIGNATURES = {
                                     _i64, _i64, _i64, _i64, _i64, _i64, _vp]),
     "t8g_gemm_i8_swiglu": (_i32, [_vp, _vp, _vp, _vp, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _vp]),
     "t8g_gemm_fp8_swiglu": (_i32, [_vp, _vp, _vp, _vp, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _vp]),
+    "t8g_gemm_i8_swiglu_quant": (_i32, [_vp, _vp, _vp, _vp, _i64, _vp, _i64, _vp, _i64, _vp, _vp, _i64, _vp,
+                                        _i64, _i64, _i64, _i64, _i64, _i32, _vp]),
+    "t8g_gemm_fp8_swiglu_quant": (_i32, [_vp, _vp, _vp, _vp, _i64, _vp, _i64, _vp, _i64, _vp, _vp, _i64, _vp,
+                                         _i64, _i64, _i64, _i64, _i64, _i32, _vp]),
     "t8g_gemm_i8_gated": (_i32, [_vp, _vp, _vp, _vp, _i64, _vp, _i64, _vp, _i64, _vp, _i64, _vp, _i64, _vp,
                                  _i64, _i64, _i64, _i64, _i64, _i64, _vp]),
     "t8g_gemm_fp8_gated": (_i32, [_vp, _vp, _vp, _vp, _i64, _vp, _i64, _vp, _i64, _vp, _i64, _vp, _i64, _vp,

@@ -48,6 +48,14 @@ __device__ __forceinline__ float2 mul_bf16x2_exact(uint32_t a, uint32_t b) {
       : "r"(a), "r"(b));
   return make_float2(x, y);
 }
+// max(|a|, |b|) lane by lane on packed bf16 pairs (exact; a NaN loses to a number).
+__device__ __forceinline__ uint32_t absmax_bf16x2(uint32_t a, uint32_t b) {
+  __nv_bfloat162 x = *reinterpret_cast<__nv_bfloat162*>(&a);
+  __nv_bfloat162 y = *reinterpret_cast<__nv_bfloat162*>(&b);
+  __nv_bfloat162 r = __hmax2(x, __habs2(y));
+  return *reinterpret_cast<uint32_t*>(&r);
+}
+
 __device__ __forceinline__ float2 add_f32_f16x2(float2 p, uint32_t b) {
   float x, y;
   asm("{ .reg .b16 lo, hi; mov.b32 {lo, hi}, %2; add.rn.f32.f16 %0, lo, %3; add.rn.f32.f16 %1, hi, %4; }"

@@ -78,6 +78,9 @@ struct Args {
   const void* gate;
   const int32_t* gate_index;
   int64_t ld_res, ld_gate, rows_per_gate;
+  // kOutSwiglu only, optional: float32 [M], zeroed by the host; receives max |bf16(act)| of
+  // every row (an atomic max per row and tile), so a per-token quantiser can stream act
+  float* row_amax;
 };
 
 template <int OUT>
@@ -735,6 +738,7 @@ __device__ __forceinline__ void epilogue_tile_swiglu(const Args& args, const CUt
   const bool has_bias = args.bias != nullptr;
   const float2 xs2 = make_float2(xs_r, xs_r);
   constexpr int kChunks = BN / 2 / EPI_COLS;
+  uint32_t m2 = 0;   // max |act| of this lane's row over the tile (packed bf16 pair)
   uint32_t rg[32], ru[32];
   tmem_ld_32x32b_x32(t_row, rg);
   tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(BN / 2), ru);
@@ -772,6 +776,7 @@ __device__ __forceinline__ void epilogue_tile_swiglu(const Args& args, const CUt
         u = add_f32_bf16x2(u, bu[p]);
       }
       act[p] = f2_to_bf2(silu_mul2(f2_to_bf2(g), bf2_to_f2(f2_to_bf2(u)), sig));
+      m2 = absmax_bf16x2(m2, act[p]);
     }
     if (lane == 0) bulk_wait_group_read<1>();
     __syncwarp();
@@ -789,6 +794,11 @@ __device__ __forceinline__ void epilogue_tile_swiglu(const Args& args, const CUt
       bulk_commit_group();
     }
     ebuf ^= 1;
+  }
+  if (args.row_amax != nullptr && row0 + lane < args.M) {
+    // rows of the 32-row slice past M hold garbage accumulators: only valid rows report
+    const float m = fmaxf(__uint_as_float(m2 << 16), __uint_as_float(m2 & 0xFFFF0000u));
+    if (m > 0.f) atomicMax(reinterpret_cast<int*>(args.row_amax + row0 + lane), __float_as_int(m));
   }
 }
 
@@ -823,7 +833,7 @@ constexpr int P_STAGE_BYTES = P_A_BYTES + P_B_BYTES;   // per CTA
 // TBN / 2 rows of W per CTA.
 template <int OUT, int TBN = BN>
 struct PairCfg {
-  static_assert(TBN == BN || ((TBN == 192 || TBN == 128 || TBN == 64) && (OUT == kOutBF16 || OUT == kOutF16)),
+  static_assert(TBN == BN || ((TBN == 128 || TBN == 64) && (OUT == kOutBF16 || OUT == kOutF16)),
                 "narrow tiles serve the plain 2-byte outputs");
   static constexpr int kBRows = TBN / 2;             // rows of W per CTA
   static constexpr int kBBytes = kBRows * BK;
@@ -871,8 +881,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
   using Cfg = PairCfg<OUT, TBN>;
   constexpr int P_STAGES = Cfg::kStages;
-  // double-buffered accumulator; TMEM is allocated in powers of two (192-wide tiles: 512)
-  constexpr uint32_t kTmemCols = 2 * TBN <= 128 ? 2 * TBN : (2 * TBN <= 256 ? 256 : 512);
+  constexpr uint32_t kTmemCols = 2 * TBN;   // double-buffered accumulator
   SmemPairOf<OUT, TBN>& s = *reinterpret_cast<SmemPairOf<OUT, TBN>*>(smem_raw + pad);
 
   const int warp = threadIdx.x >> 5;

@@ -63,13 +63,6 @@ __device__ __forceinline__ void unpack8(const uint4& v, float (&f)[8]) {
 __device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
   return make_uint4(pack_bf16(f[0], f[1]), pack_bf16(f[2], f[3]), pack_bf16(f[4], f[5]), pack_bf16(f[6], f[7]));
 }
-// |a| max |b| on packed bf16 pairs (exact).
-__device__ __forceinline__ uint32_t absmax_bf16x2(uint32_t a, uint32_t b) {
-  __nv_bfloat162 x = *reinterpret_cast<__nv_bfloat162*>(&a);
-  __nv_bfloat162 y = *reinterpret_cast<__nv_bfloat162*>(&b);
-  __nv_bfloat162 r = __hmax2(x, __habs2(y));
-  return *reinterpret_cast<uint32_t*>(&r);
-}
 // bf16(1 + s) for a packed pair: a correctly rounded bf16 add, equal to the
 // reference's fp32 add then bf16 rounding (src/ck_fused_patch.py:120).
 __device__ __forceinline__ uint32_t one_plus_bf16x2(uint32_t s) {
@@ -125,12 +118,14 @@ __device__ __forceinline__ QuantRow quant_row(float amax) {
 // conversion is then the IEEE one (int8: round half to even through the fp32 adder,
 // never needing the +-127 clamp since |v/s| <= 127; e4m3: RNE with saturation).
 template <int QK>
-__device__ __forceinline__ uint2 quant8(const float2 (&v)[4], const QuantRow& qr) {
+__device__ __forceinline__ uint2 quant8(const uint4& packed, const QuantRow& qr) {
+  const uint32_t w[4] = {packed.x, packed.y, packed.z, packed.w};
   uint32_t c[4];
 #pragma unroll
   for (int p = 0; p < 4; ++p) {
-    const float2 q = mul2_rn(v[p], qr.rcp);
-    const float2 n = fma2_rn(q, qr.scale2, make_float2(-v[p].x, -v[p].y));
+    const float2 v = bf2_to_f2(w[p]);
+    const float2 q = mul2_rn(v, qr.rcp);
+    const float2 n = fma2_rn(q, qr.scale2, make_float2(-v.x, -v.y));
     const float2 qq = fma2_rn(n, qr.nrcp, q);
     if constexpr (QK == kQuantInt8) {
       const float2 rq = add2_rn(qq, make_float2(kRoundMagic, kRoundMagic));
@@ -421,9 +416,7 @@ __device__ __forceinline__ float pair_max(uint32_t m2) { return fmaxf(bf_lo(m2),
 
 template <int QK>
 __device__ __forceinline__ void store_q(uint8_t* qrow, int c, const uint4& u, const QuantRow& qr) {
-  float2 v[4];
-  unpack_pairs(u, v);
-  *reinterpret_cast<uint2*>(qrow + 8 * c) = quant8<QK>(v, qr);
+  *reinterpret_cast<uint2*>(qrow + 8 * c) = quant8<QK>(u, qr);
 }
 
 // ---------------------------------------------------------------- per-token quant
@@ -900,6 +893,55 @@ __host__ __device__ constexpr int row_group_threads(int nvec) {
                (32 * ((nvec + 511) / 512 < 3 ? 3 : (nvec + 511) / 512)));
 }
 
+// ((p0 + p1) + p2) + ... of NW per-lane partials, each first summed over the warp by the
+// canonical butterfly (v + v[lane ^ 16], then ^ 8, 4, 2, 1).  For NW = 2 and 4 the butterflies
+// are run as a reduce-scatter: at the xor-16 level (and for NW = 4 the xor-8 level) a lane
+// keeps half of the partials and trades the other half with its partner, so every addition
+// pairs the same two values as the butterfly (each sum is commutative) with 10 shuffles
+// instead of 20 (NW = 4); lane 0 then sums the totals left to right and broadcasts.
+template <int NW>
+__device__ __forceinline__ float warp_parts_sum(const float (&part)[NW]) {
+  const int lane = threadIdx.x & 31;
+  if constexpr (NW == 2) {
+    const bool hi = lane & 16;
+    const float keep = hi ? part[1] : part[0];
+    const float give = hi ? part[0] : part[1];
+    float m = __fadd_rn(keep, __shfl_xor_sync(0xFFFFFFFFu, give, 16));
+#pragma unroll
+    for (int off = 8; off >= 1; off >>= 1) m = __fadd_rn(m, __shfl_xor_sync(0xFFFFFFFFu, m, off));
+    const float ss = __fadd_rn(m, __shfl_xor_sync(0xFFFFFFFFu, m, 16));   // lane 0: p0 + p1
+    return __shfl_sync(0xFFFFFFFFu, ss, 0);
+  } else if constexpr (NW == 4) {
+    const bool b4 = lane & 16, b3 = lane & 8;
+    // xor 16: keep parts 2 b4, 2 b4 + 1
+    const float k0 = __fadd_rn(b4 ? part[2] : part[0], __shfl_xor_sync(0xFFFFFFFFu, b4 ? part[0] : part[2], 16));
+    const float k1 = __fadd_rn(b4 ? part[3] : part[1], __shfl_xor_sync(0xFFFFFFFFu, b4 ? part[1] : part[3], 16));
+    // xor 8: keep part 2 b4 + b3
+    float m = __fadd_rn(b3 ? k1 : k0, __shfl_xor_sync(0xFFFFFFFFu, b3 ? k0 : k1, 8));
+#pragma unroll
+    for (int off = 4; off >= 1; off >>= 1) m = __fadd_rn(m, __shfl_xor_sync(0xFFFFFFFFu, m, off));
+    // lane 0 holds p0; lanes 8, 16, 24 hold p1, p2, p3
+    const float p1 = __shfl_xor_sync(0xFFFFFFFFu, m, 8);
+    const float p2 = __shfl_xor_sync(0xFFFFFFFFu, m, 16);
+    const float p3 = __shfl_xor_sync(0xFFFFFFFFu, m, 24);
+    const float ss = __fadd_rn(__fadd_rn(__fadd_rn(m, p1), p2), p3);
+    return __shfl_sync(0xFFFFFFFFu, ss, 0);
+  } else {
+    float v[NW];
+#pragma unroll
+    for (int j = 0; j < NW; ++j) v[j] = part[j];
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) {
+#pragma unroll
+      for (int j = 0; j < NW; ++j) v[j] = __fadd_rn(v[j], __shfl_xor_sync(0xFFFFFFFFu, v[j], off));
+    }
+    float ss = v[0];
+#pragma unroll
+    for (int j = 1; j < NW; ++j) ss = __fadd_rn(ss, v[j]);
+    return ss;
+  }
+}
+
 // 1 / sqrt(mean(x^2) + eps) of a register-resident row of 256 NV elements, the sum of
 // squares in the canonical tree of a row group of T = row_group_threads threads: lane
 // l's vector 32 k + l belongs to group warp k mod (T / 32), in ascending k, exactly as
@@ -924,15 +966,7 @@ __device__ __forceinline__ float row_inv_reg(const RowRegs<NV>& r, float eps) {
   float part[NW];
 #pragma unroll
   for (int j = 0; j < NW; ++j) part[j] = __fadd_rn(acc[j].x, acc[j].y);
-#pragma unroll
-  for (int off = 16; off >= 1; off >>= 1) {
-#pragma unroll
-    for (int j = 0; j < NW; ++j) part[j] = __fadd_rn(part[j], __shfl_xor_sync(0xFFFFFFFFu, part[j], off));
-  }
-  float ss = part[0];
-#pragma unroll
-  for (int j = 1; j < NW; ++j) ss = __fadd_rn(ss, part[j]);
-  return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(8 * NVEC)), eps)));
+  return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(warp_parts_sum<NW>(part), static_cast<float>(8 * NVEC)), eps)));
 }
 
 // max(m, |a|, |b|) in one three-input max.
@@ -1449,29 +1483,57 @@ __global__ void __launch_bounds__(256) quant_given_amax_kernel(const QuantGivenA
 #pragma unroll
       for (int i = 0; i < 4; ++i) u[i] = ld_v4(hv + v + i * G);
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        float2 f[4];
-        unpack_pairs(u[i], f);
-        qv[v + i * G] = quant8<QK>(f, qr);
-      }
+      for (int i = 0; i < 4; ++i) qv[v + i * G] = quant8<QK>(u[i], qr);
     }
-    for (; v < total; v += G) {
-      float2 f[4];
-      unpack_pairs(ld_v4(hv + v), f);
-      qv[v] = quant8<QK>(f, qr);
-    }
+    for (; v < total; v += G) qv[v] = quant8<QK>(ld_v4(hv + v), qr);
   } else {
     // strided rows: warps over rows, lanes over a row's vectors
     const int lane = threadIdx.x & 31;
     for (int64_t row = t0 >> 5; row < a.S; row += G >> 5) {
       const __nv_bfloat16* hrow = a.h + row * a.ld_h;
       uint8_t* qrow = static_cast<uint8_t*>(a.q) + row * a.ld_q;
-      for (int c = lane; c < nvec; c += 32) {
-        float2 f[4];
-        unpack_pairs(ld_v4(hrow + 8 * c), f);
-        *reinterpret_cast<uint2*>(qrow + 8 * c) = quant8<QK>(f, qr);
-      }
+      for (int c = lane; c < nvec; c += 32) *reinterpret_cast<uint2*>(qrow + 8 * c) = quant8<QK>(ld_v4(hrow + 8 * c), qr);
     }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// per-token quantisation with the row maxima given (the fc1 GEMM's SwiGLU epilogue reports
+// max |act| per row): a pure stream, one row per warp, no reduction and no row kept whole.
+// q_scale[m] = max(amax[m] / qmax, 1e-12), q = the same quantiser as t8g_quant_rows, so
+// the result equals quant_rows(act) bit for bit.
+// ---------------------------------------------------------------------------
+struct QuantGivenRowsArgs {
+  const __nv_bfloat16* x;
+  int64_t ld_x;
+  const float* row_amax;
+  void* q;
+  int64_t ld_q;
+  float* q_scale;
+  int64_t S;
+  int D;
+};
+
+template <int QK>
+__global__ void __launch_bounds__(256) quant_rows_given_amax_kernel(const QuantGivenRowsArgs a) {
+  const int lane = threadIdx.x & 31;
+  const int nvec = a.D >> 3;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); row < a.S;
+       row += warps) {
+    const QuantRow qr = quant_row<QK>(__ldg(a.row_amax + row));
+    if (lane == 0) a.q_scale[row] = qr.scale;
+    const uint4* xr = reinterpret_cast<const uint4*>(a.x + row * a.ld_x);
+    uint2* qr_out = reinterpret_cast<uint2*>(static_cast<uint8_t*>(a.q) + row * a.ld_q);
+    int c = lane;
+    for (; c + 7 * 32 < nvec; c += 8 * 32) {
+      uint4 u[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) u[i] = ld_v4(xr + c + 32 * i);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) qr_out[c + 32 * i] = quant8<QK>(u[i], qr);
+    }
+    for (; c < nvec; c += 32) qr_out[c] = quant8<QK>(ld_v4(xr + c), qr);
   }
 }
 

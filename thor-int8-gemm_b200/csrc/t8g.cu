@@ -9,6 +9,7 @@
 #include <stdio.h>
 #include <stdlib.h>
 
+#include <algorithm>
 #include <atomic>
 #include <mutex>
 
@@ -226,30 +227,21 @@ int gemm_entry(int in_kind, const void* x, const void* w, const float* x_scale, 
   // kernel.
   const char* sm_env = getenv("T8G_GEMM_SM");
   const bool force_1sm = sm_env && sm_env[0] == '1';
-  // Tile width of the 2-SM kernel (2-byte outputs).  256 columns by default.  The persistent
-  // kernel deals tiles round robin, so with T tiles on P pairs the last wave is partly idle
-  // (busy fraction T / (ceil(T / P) * P)):
-  //  * few tiles (less than half the pairs busy, small M): 128 or 64 columns put more pairs on
-  //    the problem, each with a shorter tile;
-  //  * otherwise 192-column tiles when they fill the last wave much better (M = 8192,
-  //    N = 3072 on 74 pairs: 384 tiles of 256, 86.5 % busy; 512 of 192, 98.8 %).  A narrower
-  //    tile streams its activation panel for fewer output columns, which costs per tile
-  //    (128-column tiles measured 0.6x the 256-column rate at M = 8192), so only a clear
-  //    gain in the last wave switches.
-  // T8G_GEMM_TBN=256|192|128|64 forces a width (tuning).
+  // Tile width of the 2-SM kernel (2-byte outputs): 256 columns, or 128 / 64 when 256-wide
+  // tiles would leave more than half of the CTA pairs idle (small M): narrower tiles put more
+  // SMs on the problem, each with a shorter tile.  Otherwise 256: a narrower tile streams its
+  // activation panel for fewer output columns, and measured per tile at 0.81x (192 columns)
+  // and 0.55x (128) the 256-column rate at M = 8192 and 32768 -- more than any fuller last
+  // wave returns (M = 8192, N = 3072: 2678 TOPS at 256, 2446 at 192, 1685 at 128, L2-warm).
+  // T8G_GEMM_TBN=256|128|64 forces a width (tuning).
   const int64_t pairs_avail = info.sms / 2;
   const int64_t tiles_m = (M + P_BM - 1) / P_BM;
-  auto busy = [&](int w) {
-    const int64_t t = tiles_m * ((N + w - 1) / w);
-    return static_cast<double>(t) / static_cast<double>(((t + pairs_avail - 1) / pairs_avail) * pairs_avail);
-  };
   int tbn = BN;
   if (esz == 2) {
     while (tbn > 64 && tiles_m * ((N + tbn - 1) / tbn) * 2 < pairs_avail) tbn /= 2;
-    if (tbn == BN && busy(BN) < 0.92 && busy(192) >= busy(BN) + 0.08) tbn = 192;
     if (const char* force = getenv("T8G_GEMM_TBN")) {
       const int f = atoi(force);
-      if (f == 256 || f == 192 || f == 128 || f == 64) tbn = f;
+      if (f == 256 || f == 128 || f == 64) tbn = f;
     }
   }
   const bool pair = (M > BM || tbn < BN) && !force_1sm;
@@ -283,18 +275,12 @@ int gemm_entry(int in_kind, const void* x, const void* w, const float* x_scale, 
     // narrow tiles (2-byte outputs only)
     const bool f16 = out_dtype == T8G_OUT_F16;
     if (in_kind == kInI8) {
-      if (tbn == 192)
-        return f16 ? launch_gemm_pair<kInI8, kOutF16, 192>(ta, tb, to, args, dev, info.sms, st)
-                   : launch_gemm_pair<kInI8, kOutBF16, 192>(ta, tb, to, args, dev, info.sms, st);
       if (tbn == 128)
         return f16 ? launch_gemm_pair<kInI8, kOutF16, 128>(ta, tb, to, args, dev, info.sms, st)
                    : launch_gemm_pair<kInI8, kOutBF16, 128>(ta, tb, to, args, dev, info.sms, st);
       return f16 ? launch_gemm_pair<kInI8, kOutF16, 64>(ta, tb, to, args, dev, info.sms, st)
                  : launch_gemm_pair<kInI8, kOutBF16, 64>(ta, tb, to, args, dev, info.sms, st);
     }
-    if (tbn == 192)
-      return f16 ? launch_gemm_pair<kInE4M3, kOutF16, 192>(ta, tb, to, args, dev, info.sms, st)
-                 : launch_gemm_pair<kInE4M3, kOutBF16, 192>(ta, tb, to, args, dev, info.sms, st);
     if (tbn == 128)
       return f16 ? launch_gemm_pair<kInE4M3, kOutF16, 128>(ta, tb, to, args, dev, info.sms, st)
                  : launch_gemm_pair<kInE4M3, kOutBF16, 128>(ta, tb, to, args, dev, info.sms, st);
@@ -334,7 +320,8 @@ int gemm_entry(int in_kind, const void* x, const void* w, const float* x_scale, 
 // kernel (its 256-column tiles pair 128 gate with 128 up columns).
 int gemm_swiglu_entry(int in_kind, const void* x, const void* w, const float* x_scale, const float* w_scale,
                       int64_t w_scale_numel, const void* bias, int64_t bias_numel, void* act, int64_t M, int64_t F,
-                      int64_t K, int64_t ld_x, int64_t ld_w, int64_t ld_act, void* stream_) {
+                      int64_t K, int64_t ld_x, int64_t ld_w, int64_t ld_act, void* stream_,
+                      float* row_amax = nullptr) {
   using namespace t8g::gemm;
   g_last_error[0] = '\0';
   if (M < 0 || F < 0 || K < 1) return fail(T8G_ERR_INVALID_ARGUMENT, "bad sizes M=%lld F=%lld K=%lld", (long long)M, (long long)F, (long long)K);
@@ -375,7 +362,10 @@ int gemm_swiglu_entry(int in_kind, const void* x, const void* w, const float* x_
   args.M = static_cast<int>(M);
   args.N = static_cast<int>(N);
   args.K = static_cast<int>(K);
+  args.row_amax = row_amax;
   cudaStream_t st = static_cast<cudaStream_t>(stream_);
+  if (row_amax) T8G_CHECK_CUDA(cudaMemsetAsync(row_amax, 0, static_cast<size_t>(M) * sizeof(float), st),
+                               "cudaMemsetAsync(row_amax)");
   if (in_kind == kInI8) return launch_gemm_pair<kInI8, kOutSwiglu>(ta, tb, to, args, dev, info.sms, st);
   return launch_gemm_pair<kInE4M3, kOutSwiglu>(ta, tb, to, args, dev, info.sms, st);
 }
@@ -915,6 +905,45 @@ int noalloc_scratch(int dev, unsigned char** out) {
   return T8G_OK;
 }
 
+int swiglu_quant_entry(int in_kind, const void* x, const void* w, const float* x_scale, const float* w_scale,
+                       int64_t w_scale_numel, const void* bias, int64_t bias_numel, void* act, int64_t ld_act,
+                       float* act_amax, void* q, int64_t ld_q, float* q_scale, int64_t M, int64_t F, int64_t K,
+                       int64_t ld_x, int64_t ld_w, int quant_kind, void* stream) {
+  using namespace t8g::rows;
+  g_last_error[0] = '\0';
+  if (quant_kind != T8G_QUANT_INT8 && quant_kind != T8G_QUANT_FP8_E4M3)
+    return fail(T8G_ERR_INVALID_ARGUMENT, "unknown quant_kind %d", quant_kind);
+  if (M > 0 && F > 0) {
+    if (!act_amax || !aligned(act_amax, 4)) return fail(T8G_ERR_INVALID_ARGUMENT, "act_amax must be a 4-byte aligned [M] buffer");
+    if (!q_scale) return fail(T8G_ERR_INVALID_ARGUMENT, "q_scale is null");
+    int rc = check_q(q, ld_q, F);
+    if (rc) return rc;
+  }
+  int rc = gemm_swiglu_entry(in_kind, x, w, x_scale, w_scale, w_scale_numel, bias, bias_numel, act, M, F, K, ld_x,
+                             ld_w, ld_act, stream, act_amax);
+  if (rc || M == 0 || F == 0) return rc;
+  int dev;
+  DeviceInfo info;
+  if ((rc = current_device(&dev, &info))) return rc;
+  QuantGivenRowsArgs a;
+  a.x = static_cast<const __nv_bfloat16*>(act);
+  a.ld_x = ld_act;
+  a.row_amax = act_amax;
+  a.q = q;
+  a.ld_q = ld_q;
+  a.q_scale = q_scale;
+  a.S = M;
+  a.D = static_cast<int>(F);
+  const int64_t warps = static_cast<int64_t>(info.sms) * 64;   // 8 CTAs of 8 warps per SM
+  const int64_t ctas = (std::min<int64_t>(M, warps) + 7) / 8;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (quant_kind == T8G_QUANT_FP8_E4M3)
+    quant_rows_given_amax_kernel<kQuantFp8><<<static_cast<unsigned>(ctas), 256, 0, st>>>(a);
+  else
+    quant_rows_given_amax_kernel<kQuantInt8><<<static_cast<unsigned>(ctas), 256, 0, st>>>(a);
+  return launch_checked("quant of act launch");
+}
+
 }  // namespace
 
 extern "C" {
@@ -1001,6 +1030,22 @@ int t8g_gemm_fp8_swiglu(const void* x, const void* w, const float* x_scale, cons
                         int64_t K, int64_t ld_x, int64_t ld_w, int64_t ld_act, void* stream) {
   return gemm_swiglu_entry(t8g::gemm::kInE4M3, x, w, x_scale, w_scale, w_scale_numel, bias, bias_numel, act, M, F,
                            K, ld_x, ld_w, ld_act, stream);
+}
+
+int t8g_gemm_i8_swiglu_quant(const void* x, const void* w, const float* x_scale, const float* w_scale,
+                             int64_t w_scale_numel, const void* bias, int64_t bias_numel, void* act, int64_t ld_act,
+                             float* act_amax, void* q, int64_t ld_q, float* q_scale, int64_t M, int64_t F, int64_t K,
+                             int64_t ld_x, int64_t ld_w, int quant_kind, void* stream) {
+  return swiglu_quant_entry(t8g::gemm::kInI8, x, w, x_scale, w_scale, w_scale_numel, bias, bias_numel, act, ld_act,
+                            act_amax, q, ld_q, q_scale, M, F, K, ld_x, ld_w, quant_kind, stream);
+}
+
+int t8g_gemm_fp8_swiglu_quant(const void* x, const void* w, const float* x_scale, const float* w_scale,
+                              int64_t w_scale_numel, const void* bias, int64_t bias_numel, void* act, int64_t ld_act,
+                              float* act_amax, void* q, int64_t ld_q, float* q_scale, int64_t M, int64_t F, int64_t K,
+                              int64_t ld_x, int64_t ld_w, int quant_kind, void* stream) {
+  return swiglu_quant_entry(t8g::gemm::kInE4M3, x, w, x_scale, w_scale, w_scale_numel, bias, bias_numel, act, ld_act,
+                            act_amax, q, ld_q, q_scale, M, F, K, ld_x, ld_w, quant_kind, stream);
 }
 
 int t8g_gemm_i8_gated(const void* x, const void* w, const float* x_scale, const float* w_scale,

@@ -63,7 +63,8 @@ class DiTBlock:
         self.proj = QuantLinear(w(hidden, hidden), b(hidden), kind)
         self.fc1 = QuantLinear(w(2 * ffn, hidden), b(2 * ffn), kind)
         self.fc2 = QuantLinear(w(hidden, ffn), b(hidden), kind)
-        # fused_mlp: fc1 with the SwiGLU in its epilogue (gate / up rows interleaved once)
+        # fused_mlp: fc1 with the SwiGLU in its epilogue (gate / up rows interleaved once), which
+        # also reports each row's max |act| so that act is quantised as a plain stream
         self.fused_mlp = fused_mlp
         # fused_gate: proj and fc2 apply the gated residual in their epilogue (gemm_gated)
         self.fused_gate = fused_gate
@@ -109,7 +110,7 @@ class DiTBlock:
         q2, s2 = self.norm_quant(x, shift_mlp, scale_mlp, T)
         if self.fused_mlp:
             w_il, ws_il, b_il = self.fc1_il
-            q3, s3 = ops.quant_rows(ops.gemm_swiglu(q2, w_il, s2, ws_il, b_il), self.kind)
+            q3, s3, _ = ops.gemm_swiglu_quant(q2, w_il, s2, ws_il, b_il, kind=self.kind)
         else:
             y = self.fc1(q2, s2)
             q3, s3 = ops.swiglu_quant_fc1(y, kind=self.kind)

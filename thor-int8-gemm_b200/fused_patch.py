@@ -19,9 +19,9 @@ What the fused forward runs (the block's call order is the stock one, :153-172):
     quantisation;
   cluster 2 (on / c2): when fc1 and fc2 hold comfy fp8 QuantizedTensor weights (e4m3 codes
     with one scale, or one per output channel), the whole MLP and the block's gated residual
-    run on this library's fp8 GEMMs: fc1 with the SwiGLU in its epilogue
-    (t8g_gemm_fp8_swiglu; its weight, scale and bias interleaved in 128-row gate / up blocks
-    once per weight and cached), per-token fp8 quantisation of act (t8g_quant_rows), and fc2
+    run on this library's fp8 GEMMs: fc1 with the SwiGLU in its epilogue and per-token fp8
+    quantisation of act (t8g_gemm_fp8_swiglu_quant; fc1's weight, scale and bias interleaved
+    in 128-row gate / up blocks once per weight and cached), and fc2
     with x + gate_mlp * y in its epilogue (t8g_gemm_fp8_gated) -- neither fc1's [S, 2F]
     output nor fc2's output reaches memory, and comfy's own fp8 matmul is not called.
     Otherwise (another weight format) fc1 runs as comfy's linear and its bf16 output takes
@@ -189,8 +189,7 @@ class _Runtime:
             a, a_scale = self.ops.quant_rows(h.contiguous(), "fp8_e4m3")
         if a.dtype != torch.float8_e4m3fn or tuple(a.shape) != (S, w1.shape[1]) or w2.shape[1] != w1.shape[0] // 2:
             return None
-        act = self.ops.gemm_swiglu(a.contiguous(), w1, a_scale, s1, b1)
-        q, q_scale = self.ops.quant_rows(act, "fp8_e4m3")
+        q, q_scale, _act = self.ops.gemm_swiglu_quant(a.contiguous(), w1, a_scale, s1, b1, kind="fp8_e4m3")
         return self.ops.gemm_gated(q, w2, q_scale, s2, b2, x, gate.to(torch.bfloat16).contiguous(), gate_index=rows)
 
     # ------------------------------------------------------------------ block

@@ -215,6 +215,50 @@ def gemm_swiglu(x: torch.Tensor, w_il: torch.Tensor, x_scale: torch.Tensor, w_sc
     return out
 
 
+def gemm_swiglu_quant(x: torch.Tensor, w_il: torch.Tensor, x_scale: torch.Tensor, w_scale_il: torch.Tensor,
+                      bias_il: torch.Tensor | None = None, kind: str = "int8", act: torch.Tensor | None = None,
+                      stream=None):
+    """fc1 + SwiGLU + per-token quantisation of act in one call -> (q, q_scale, act): the SwiGLU
+    epilogue also reports each row's max |act|, so the quantiser streams act once (equal bit
+    for bit to quant_rows(gemm_swiglu(...)))."""
+    _need_cuda("x", x, (torch.int8, torch.float8_e4m3fn), 2)
+    _need_cuda("w", w_il, x.dtype, 2)
+    M, K = x.shape
+    N = w_il.shape[0]
+    if w_il.shape[1] != K:
+        raise ValueError(f"w has K={w_il.shape[1]}, x has K={K}")
+    if N % (2 * SWIGLU_BLOCK):
+        raise ValueError(f"w must have 2F rows with F a multiple of {SWIGLU_BLOCK}")
+    F = N // 2
+    _need_cuda("x_scale", x_scale, torch.float32)
+    _need_cuda("w_scale", w_scale_il, torch.float32)
+    if x_scale.numel() != M or not x_scale.is_contiguous():
+        raise ValueError("x_scale must be a contiguous float32 tensor with M elements")
+    if w_scale_il.numel() not in (1, N) or not w_scale_il.is_contiguous():
+        raise ValueError("w_scale must be a contiguous float32 tensor with 1 or 2F elements")
+    if act is None:
+        act = torch.empty(M, F, dtype=torch.bfloat16, device=x.device)
+    _need_cuda("act", act, torch.bfloat16, 2)
+    if tuple(act.shape) != (M, F):
+        raise ValueError(f"act has shape {tuple(act.shape)}, expected {(M, F)}")
+    nb = 0 if bias_il is None else bias_il.numel()
+    if nb:
+        _need_cuda("bias", bias_il, torch.bfloat16)
+        if nb != N or not bias_il.is_contiguous():
+            raise ValueError("bias must be contiguous bf16 with 2F elements")
+    amax = torch.empty(M, dtype=torch.float32, device=x.device)
+    q = torch.empty(M, F, dtype=QUANT_DTYPE[kind], device=x.device)
+    q_scale = torch.empty(M, dtype=torch.float32, device=x.device)
+    lib = _lib.load()
+    fn = lib.t8g_gemm_i8_swiglu_quant if x.dtype == torch.int8 else lib.t8g_gemm_fp8_swiglu_quant
+    with _on(x.device):
+        rc = fn(_ptr(x), _ptr(w_il), _ptr(x_scale), _ptr(w_scale_il), w_scale_il.numel(),
+                _ptr(bias_il) if nb else None, nb, _ptr(act), act.stride(0), _ptr(amax), _ptr(q), q.stride(0),
+                _ptr(q_scale), M, F, K, x.stride(0), w_il.stride(0), QUANT_CODE[kind], _stream_handle(x.device, stream))
+    _lib.check(rc)
+    return q, q_scale, act
+
+
 def gemm_gated(x: torch.Tensor, w: torch.Tensor, x_scale: torch.Tensor, w_scale: torch.Tensor,
                bias: torch.Tensor | None, res: torch.Tensor, gate: torch.Tensor, *,
                rows_per_gate: int | None = None, gate_index: torch.Tensor | None = None,
