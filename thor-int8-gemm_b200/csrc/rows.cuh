@@ -183,19 +183,26 @@ __device__ __forceinline__ float block_sum(const RowGroup& grp, float v, float* 
   return t;
 }
 
+// Max over the warp of non-negative, non-NaN floats (running maxima of |x| that start at
+// +0), by the integer order of their bit patterns: one redux instead of a five-step
+// butterfly of shuffles and compares.
+__device__ __forceinline__ float warp_max_nonneg(float v) {
+  uint32_t r;
+  asm volatile("redux.sync.max.u32 %0, %1, 0xffffffff;" : "=r"(r) : "r"(__float_as_uint(v)));
+  return __uint_as_float(r);
+}
+
 // Max of non-negative values over the row group (order-free: every lane of every warp
 // folds the warp partials with one more butterfly).
 __device__ __forceinline__ float block_max(const RowGroup& grp, float v, float* red) {
-#pragma unroll
-  for (int off = 16; off >= 1; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xFFFFFFFFu, v, off));
+  v = warp_max_nonneg(v);
   const int nw = grp.T >> 5;
   if (nw == 1) return v;
   const int lane = grp.t & 31;
   if (lane == 0) red[grp.t >> 5] = v;
   group_sync(grp);
   float t = lane < nw ? red[lane] : 0.f;
-#pragma unroll
-  for (int off = 16; off >= 1; off >>= 1) t = fmaxf(t, __shfl_xor_sync(0xFFFFFFFFu, t, off));
+  t = warp_max_nonneg(t);
   return t;
 }
 
@@ -207,8 +214,7 @@ __device__ __forceinline__ void atomic_max_nonneg(float* addr, float v) {
 // Folds each thread's running max of its rows into the tensor's amax word with one atomic
 // per warp, after the warp's last row (an atomic per row serialises on the single word).
 __device__ __forceinline__ void flush_amax(float* amax, float m) {
-#pragma unroll
-  for (int off = 16; off >= 1; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, off));
+  m = warp_max_nonneg(m);
   if ((threadIdx.x & 31) == 0 && m > 0.f) atomic_max_nonneg(amax, m);
 }
 
@@ -553,8 +559,7 @@ __global__ void __launch_bounds__(1024) quant_rows_warp_kernel(const QuantRowsAr
 #pragma unroll 4
     for (int c = lane; c < nvec; c += 32) m2 = absmax4(m2, lds_v4(slot + 16 * c));
     float m = pair_max(m2);
-#pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, off));
+    m = warp_max_nonneg(m);
     const QuantRow qr = quant_row<QK>(m);
     if (lane == 0) a.q_scale[row] = qr.scale;
     uint8_t* qrow = static_cast<uint8_t*>(a.q) + row * a.ld_q;
@@ -756,8 +761,7 @@ __global__ void __launch_bounds__(1024) rms_mod_warp_kernel(const RmsArgs a, con
       *reinterpret_cast<uint4*>(slot + 16 * c) = hu;
     }
     float mx = pair_max(m2);
-#pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, off));
+    mx = warp_max_nonneg(mx);
     const QuantRow qr = quant_row<QK>(mx);
     if (lane == 0) a.q_scale[row] = qr.scale;
     uint8_t* qrow = static_cast<uint8_t*>(a.q) + row * a.ld_q;
@@ -865,8 +869,7 @@ __global__ void __launch_bounds__(512, 1) quant_rows_warp_reg_kernel(const Quant
 #pragma unroll
         for (int k = 0; k < NV; ++k) m2 = absmax4(m2, r.v[k]);
         float m = pair_max(m2);
-#pragma unroll
-        for (int off = 16; off >= 1; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, off));
+        m = warp_max_nonneg(m);
         const QuantRow qr = quant_row<QK>(m);
         if (lane == 0) a.q_scale[row] = qr.scale;
         uint8_t* qrow = static_cast<uint8_t*>(a.q) + row * a.ld_q;
@@ -1072,8 +1075,7 @@ __global__ void __launch_bounds__(512, 1) rms_mod_simple_kernel(const RmsArgs a,
 #pragma unroll
           for (int k = 0; k < NV; ++k) r.v[k] = rms_h_simple_global8(srow, brow, 32 * k + lane, r.v[k], inv, &amax);
         }
-#pragma unroll
-        for (int off = 16; off >= 1; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, off));
+        amax = warp_max_nonneg(amax);
         // max |bf16(h)| = bf16(max |h|): rounding is monotone and symmetric
         const QuantRow qr = quant_row<QK>(__bfloat162float(__float2bfloat16_rn(amax)));
         if (lane == 0) a.q_scale[row] = qr.scale;
@@ -1152,8 +1154,7 @@ __global__ void __launch_bounds__(512, 1) rms_mod_warp_reg_kernel(const RmsArgs 
           if ((k & 3) == 3) asm volatile("" ::: "memory");
         }
         float mx = pair_max(m2);
-#pragma unroll
-        for (int off = 16; off >= 1; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, off));
+        mx = warp_max_nonneg(mx);
         const QuantRow qr = quant_row<QK>(mx);
         if (lane == 0) a.q_scale[row] = qr.scale;
         uint8_t* qrow = static_cast<uint8_t*>(a.q) + row * a.ld_q;
