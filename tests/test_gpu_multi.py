@@ -4,7 +4,7 @@ its slice against the oracle, and the all-gathered slices equal the one-GPU resu
 bit.  Covers the int8 GEMM (per-token quantisation in front of it) and the config-3 style
 norm/mod/quant with a slice that straddles the boundary between two batch elements.
 Skipped with fewer than two GPUs.  NVLink SHARP is off (NCCL_NVLS_ENABLE=0): nothing here
-needs it, and a rank that fails an assertion then leaves no multicast binding behind."""
+needs it, and a rank that fails an assertion then leaves no switch-side state behind."""
 import datetime
 import os
 import socket
