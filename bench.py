@@ -67,8 +67,8 @@ def parse_args():
     ap.add_argument("--scaling", choices=("weak", "strong"), default="weak",
                     help="weak: every rank runs the full sweep on its own tokens; strong: the sweep's "
                          "tokens are split across the ranks")
-    ap.add_argument("--profile", choices=("gemm_i8", "gemm_fp8", "gemm_gated", "gemm_swiglu", "rms_fp8", "rms_int8",
-                                          "swiglu_int8", "quant_int8"),
+    ap.add_argument("--profile", choices=("gemm_i8", "gemm_fp8", "gemm_gated", "gemm_swiglu", "gemm_swiglu_quant",
+                                          "rms_fp8", "rms_int8", "rms_tw_fp8", "swiglu_int8", "quant_int8"),
                     help="run one kernel a few times on a mid-size case (for ncu captures) and exit")
     ap.add_argument("--gate", action="store_true",
                     help="exit with status 1 when a figure falls below the recorded floor (tests/perf_floor.json)")
@@ -92,7 +92,18 @@ def run_profile_case(args):
     gen = torch.Generator(device=dev)
     gen.manual_seed(5)
     n = args.warmup + args.steps
-    if args.profile == "gemm_swiglu":
+    if args.profile == "gemm_swiglu_quant":
+        # fc1 with the SwiGLU epilogue reporting each row's max |act|, then the streaming
+        # per-token int8 quantiser of act: x [M, 3072] -> codes [M, N / 2]
+        x, xs = ops.quant_rows(torch.randn(args.M, K_DIM, generator=gen, device=dev).to(torch.bfloat16), "int8")
+        w, ws = ops.quant_rows((torch.randn(args.N, K_DIM, generator=gen, device=dev) * 0.02).to(torch.bfloat16), "int8")
+        bias = (torch.randn(args.N, generator=gen, device=dev) * 0.01).to(torch.bfloat16)
+        il = ops.interleave_gate_up
+        w, ws, bias = il(w), il(ws), il(bias)
+        act = torch.empty(args.M, args.N // 2, dtype=torch.bfloat16, device=dev)
+        for _ in range(n):
+            ops.gemm_swiglu_quant(x, w, xs, ws, bias, kind="int8", act=act)
+    elif args.profile == "gemm_swiglu":
         # fc1 of the MLP with the SwiGLU epilogue: x [M, 3072] -> act [M, N / 2] (N = 2F)
         x, xs = ops.quant_rows(torch.randn(args.M, K_DIM, generator=gen, device=dev).to(torch.bfloat16), "int8")
         w, ws = ops.quant_rows((torch.randn(args.N, K_DIM, generator=gen, device=dev) * 0.02).to(torch.bfloat16), "int8")
@@ -118,6 +129,13 @@ def run_profile_case(args):
         out = torch.empty(args.M, args.N, dtype=torch.bfloat16, device=dev)
         for _ in range(n):
             ops.gemm_dequant(x, w, xs, ws, bias, out=out)
+    elif args.profile == "rms_tw_fp8":
+        # the reference's form: tensorwise fp8 scale, h and res written (phase A), codes (phase B)
+        x = torch.randn(2 * 56320, 3072, generator=gen, device=dev).to(torch.bfloat16)
+        sh = (torch.randn(2, 3072, generator=gen, device=dev) * 0.1).to(torch.bfloat16)
+        sc = (torch.randn(2, 3072, generator=gen, device=dev) * 0.1).to(torch.bfloat16)
+        for _ in range(n):
+            ops.rms_mod_quant_tensorwise(x, sh, sc, rows_per_mod=56320, eps=1e-6, kind="fp8_e4m3")
     elif args.profile.startswith("rms"):
         kind = "int8" if args.profile == "rms_int8" else "fp8_e4m3"
         x = torch.randn(2 * 56320, 3072, generator=gen, device=dev).to(torch.bfloat16)
