@@ -849,8 +849,11 @@ def run_ours(args):
         items8 = None
         del items8
         f8 = build_gemm_set(torch, ops, dev, "fp8_e4m3", seed=99 + rank)
+        f8_clocks = ClockSampler(gpu_smi_id(torch, dev))
+        f8_clocks.start()
         f8_ms, f8_shape = time_gemm_sweep(torch, ops, f8, max(3, args.steps // 2), args.warmup, stream)
         extras["fp8_gemm_sweep_tops"] = round(step_ops * max(3, args.steps // 2) / (f8_ms / 1e3) / 1e12, 1)
+        extras["fp8_gemm_sweep_clocks"] = f8_clocks.stop()
         del f8
         torch.cuda.empty_cache()
         # the row kernels are issue-bound, so their rate follows the SM clock: a 2 s idle lets
