@@ -246,6 +246,41 @@ def test_rms_mod_quant_tensorwise_bit_exact(ops, kind, S, D, n_mod, with_w):
     np.testing.assert_array_equal(qbits(q, kind), q_ref)
 
 
+@pytest.mark.parametrize("kind", ["fp8_e4m3", "int8"])
+@pytest.mark.parametrize("B,T,D,want_res", [(3, 5000, 3072, True), (2, 1500, 4096, True), (5, 97, 1024, False),
+                                            (4, 2001, 2048, True), (2, 333, 1536, False), (1, 149, 3072, True)])
+def test_rms_mod_quant_tensorwise_dit_form(ops, kind, B, T, D, want_res):
+    """The tensorwise form in the DiT layout (no norm weight, s = bf16(1 + scale), batch-major
+    tokens): the kernel that caches one batch element's modulation per CTA block, with blocks
+    that straddle batch elements (their other rows read the modulation from global memory),
+    against the oracle -- h, res, the scale and every code, bit for bit."""
+    rng = np.random.default_rng(B * T + D)
+    S = B * T
+    x = O.round_bf16((rng.standard_normal((S, D)) * 1.5).astype(np.float32))
+    x[S // 3, : min(D, 16)] *= 40.0
+    x = O.round_bf16(x)
+    shift = O.round_bf16((rng.standard_normal((B, D)) * 0.1).astype(np.float32))
+    scale = O.round_bf16((rng.standard_normal((B, D)) * 0.1).astype(np.float32))
+    q, qs, h, res = ops.rms_mod_quant_tensorwise(
+        bf16_dev(to_bf16_bits(x)), bf16_dev(to_bf16_bits(shift)), bf16_dev(to_bf16_bits(scale)), rows_per_mod=T,
+        eps=1e-6, kind=kind, want_res=want_res)
+    mod_index = np.arange(S) // T
+    x32 = x.astype(np.float32)
+    inv = O.rms_inv(O.rms_sum_squares_reference(x32), D, 1e-6)
+    h_ref32 = O.rms_mod_h(x32, inv, None, O.mod_multiplier(scale, False)[mod_index], shift[mod_index])
+    amax = np.float32(np.max(np.abs(h_ref32)))
+    h_ref = O.f32_to_bf16(h_ref32)
+    np.testing.assert_array_equal(bits16(h), h_ref)
+    if want_res:
+        np.testing.assert_array_equal(bits16(res), O.f32_to_bf16((h_ref32 + x32).astype(np.float32)))
+    else:
+        assert res is None
+    q_ref, s_ref = O.quant_tensorwise_given(O.bf16_to_f32(h_ref), amax, KINDS[kind])
+    assert np.float32(qs.item()) == s_ref
+    np.testing.assert_array_equal(qbits(q, kind), q_ref)
+    assert ops.device_status() == 0
+
+
 @pytest.mark.parametrize("kind", ["int8", "fp8_e4m3"])
 @pytest.mark.parametrize("M,F", [(8, 512), (33, 1536), (64, 12288), (5, 16384), (3, 24576)])
 def test_swiglu_quant_per_token(ops, kind, M, F):

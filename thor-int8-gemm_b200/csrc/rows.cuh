@@ -1260,22 +1260,79 @@ __global__ void __launch_bounds__(1024) rms_mod_tw_warp_kernel(const RmsArgs a, 
   flush_amax(a.amax, tw_max);
 }
 
-// Phase A of the tensorwise norm for rows of 256 NV elements (every option of the entry
-// point: norm weight, mod_index, scale as multiplier, res): the warp sums the squares in the
-// reference's order from the padded slot, copies the row into registers (lane l holding
-// vectors 32 k + l) and refills the slot at once, then computes h from the registers.
+// A register-resident row and its sum of squares in the reference's order.
 template <int NV>
 struct RowRegsSS {
   uint4 v[NV];
   float ss;
 };
 
-template <int NV>
-__global__ void __launch_bounds__(512, 1) rms_mod_tw_reg_kernel(const RmsArgs a, const WarpRingGeom g) {
+// h and res of one vector from x, inv, the norm weight (HAS_W), the fp32 multiplier pairs s
+// and the packed bf16 shift: h = RN(RN(RN(RN(x * inv) * w) * s) + b), the product with w left
+// out without a weight (the order of rms_h8), res = bf16(h + x); folds the float32 |h| into
+// amax.
+template <bool HAS_W>
+__device__ __forceinline__ uint4 rms_h_res8(const uint4& xu, float2 inv2, const uint4& wu, const float2 (&s)[4],
+                                            const uint4& bu, float& amax, uint4& res) {
+  const uint32_t xw[4] = {xu.x, xu.y, xu.z, xu.w};
+  const uint32_t ww[4] = {wu.x, wu.y, wu.z, wu.w};
+  const uint32_t bw[4] = {bu.x, bu.y, bu.z, bu.w};
+  uint32_t hw[4], rw[4];
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    const float2 x = bf2_to_f2(xw[p]);
+    float2 t = mul2_rn(x, inv2);
+    if constexpr (HAS_W) t = mul2_rn(t, bf2_to_f2(ww[p]));
+    const float2 h = add_f32_bf16x2(mul2_rn(t, s[p]), bw[p]);
+    amax = max3_abs(amax, h.x, h.y);
+    hw[p] = f2_to_bf2(h);
+    rw[p] = f2_to_bf2(add2_rn(h, x));
+  }
+  res = make_uint4(rw[0], rw[1], rw[2], rw[3]);
+  return make_uint4(hw[0], hw[1], hw[2], hw[3]);
+}
+
+// Phase A of the tensorwise norm for rows of 256 NV elements (every option of the entry
+// point: norm weight when HAS_W, mod_index or batch-major rows_per_mod, scale as multiplier or
+// s = bf16(1 + scale), res when asked): the warp sums the squares in the reference's order from
+// the padded slot, copies the row into registers (lane l holding vectors 32 k + l) and refills
+// the slot at once, then computes h from the registers.  Each CTA owns a contiguous block of
+// rows and keeps in shared memory the modulation of the block's middle row (s as fp32, the
+// shift as bf16) and the norm weight; rows with another modulation row read theirs from
+// global memory.
+template <int NV, bool HAS_W>
+__global__ void __launch_bounds__(512, 1) rms_mod_tw_cached_kernel(const RmsArgs a, const WarpRingGeom g) {
   extern __shared__ __align__(1024) uint8_t smem[];
   constexpr int D = 256 * NV;
   constexpr int NCH = (D + kRefBlock - 1) / kRefBlock;
+  constexpr int NVEC = 32 * NV;
   const int lane = threadIdx.x & 31;
+  const int W = blockDim.x >> 5;
+  float4* cache_lo = reinterpret_cast<float4*>(smem + kWarpRingHeader + static_cast<size_t>(W) * g.stages * g.slot_bytes);
+  float4* cache_hi = cache_lo + NVEC;
+  uint4* cache_b = reinterpret_cast<uint4*>(cache_hi + NVEC);
+  uint4* cache_w = cache_b + NVEC;   // HAS_W only
+  const int64_t r0 = static_cast<int64_t>(blockIdx.x) * g.cta_rows;
+  const int64_t r1 = min(a.S, r0 + g.cta_rows);
+  int64_t cm = -1;
+  if (r0 < r1) {
+    const int64_t mid = (r0 + r1 - 1) >> 1;
+    cm = a.mod_index ? static_cast<int64_t>(__ldg(a.mod_index + mid)) : mid / a.rows_per_mod;
+  }
+  if (cm >= 0) {
+    for (int c = threadIdx.x; c < NVEC; c += blockDim.x) {
+      uint4 su = ld_v4(a.scale + cm * a.ld_mod + 8 * c);
+      if (!a.scale_is_multiplier)
+        su = make_uint4(one_plus_bf16x2(su.x), one_plus_bf16x2(su.y), one_plus_bf16x2(su.z), one_plus_bf16x2(su.w));
+      float2 sf[4];
+      unpack_pairs(su, sf);
+      cache_lo[c] = make_float4(sf[0].x, sf[0].y, sf[1].x, sf[1].y);
+      cache_hi[c] = make_float4(sf[2].x, sf[2].y, sf[3].x, sf[3].y);
+      cache_b[c] = ld_v4(a.shift + cm * a.ld_mod + 8 * c);
+      if constexpr (HAS_W) cache_w[c] = ld_v4(a.w + 8 * c);
+    }
+  }
+  __syncthreads();
   int64_t cur_m = -1, seg_end = -1;
   float tw_max = 0.f;
   auto src = [&](int64_t r) -> const void* { return a.x + r * a.ld_x; };
@@ -1292,44 +1349,35 @@ __global__ void __launch_bounds__(512, 1) rms_mod_tw_reg_kernel(const RmsArgs a,
         const float inv = rms_inv_of(r.ss, static_cast<float>(D), a.eps);
         const float2 inv2 = make_float2(inv, inv);
         const int64_t m = mod_row_of(a, row, cur_m, seg_end);
-        const __nv_bfloat16* srow = a.scale + m * a.ld_mod;
-        const __nv_bfloat16* brow = a.shift + m * a.ld_mod;
+        __nv_bfloat16* hrow = a.h + row * a.ld_h;
+        __nv_bfloat16* rrow = a.res ? a.res + row * a.ld_res : nullptr;
 #pragma unroll
         for (int k = 0; k < NV; ++k) {
           const int c = 32 * k + lane;
-          uint4 su = ld_v4(srow + 8 * c);
-          const uint4 bu = ld_v4(brow + 8 * c);
-          if (!a.scale_is_multiplier)
-            su = make_uint4(one_plus_bf16x2(su.x), one_plus_bf16x2(su.y), one_plus_bf16x2(su.z),
-                            one_plus_bf16x2(su.w));
-          const uint32_t xw[4] = {r.v[k].x, r.v[k].y, r.v[k].z, r.v[k].w};
-          const uint32_t sw[4] = {su.x, su.y, su.z, su.w};
-          const uint32_t bw[4] = {bu.x, bu.y, bu.z, bu.w};
+          float2 sf[4];
+          uint4 bu;
+          if (m == cm) {
+            const float4 s0 = cache_lo[c];
+            const float4 s1 = cache_hi[c];
+            sf[0] = make_float2(s0.x, s0.y);
+            sf[1] = make_float2(s0.z, s0.w);
+            sf[2] = make_float2(s1.x, s1.y);
+            sf[3] = make_float2(s1.z, s1.w);
+            bu = cache_b[c];
+          } else {
+            uint4 su = ld_v4(a.scale + m * a.ld_mod + 8 * c);
+            if (!a.scale_is_multiplier)
+              su = make_uint4(one_plus_bf16x2(su.x), one_plus_bf16x2(su.y), one_plus_bf16x2(su.z),
+                              one_plus_bf16x2(su.w));
+            unpack_pairs(su, sf);
+            bu = ld_v4(a.shift + m * a.ld_mod + 8 * c);
+          }
           uint4 wu = make_uint4(0, 0, 0, 0);
-          if (a.w) wu = ld_v4(a.w + 8 * c);
-          const uint32_t ww[4] = {wu.x, wu.y, wu.z, wu.w};
-          float2 h[4], x[4];
-#pragma unroll
-          for (int p = 0; p < 4; ++p) {
-            x[p] = bf2_to_f2(xw[p]);
-            float2 t = mul2_rn(x[p], inv2);
-            if (a.w) t = mul2_rn(t, bf2_to_f2(ww[p]));
-            t = mul2_rn(t, bf2_to_f2(sw[p]));
-            h[p] = add_f32_bf16x2(t, bw[p]);
-          }
-          tw_max = absmax_f2x4(tw_max, h);
-          if (a.res) {
-            uint4 ru;
-            ru.x = f2_to_bf2(add2_rn(h[0], x[0]));
-            ru.y = f2_to_bf2(add2_rn(h[1], x[1]));
-            ru.z = f2_to_bf2(add2_rn(h[2], x[2]));
-            ru.w = f2_to_bf2(add2_rn(h[3], x[3]));
-            *reinterpret_cast<uint4*>(a.res + row * a.ld_res + 8 * c) = ru;
-          }
-          *reinterpret_cast<uint4*>(a.h + row * a.ld_h + 8 * c) =
-              make_uint4(f2_to_bf2(h[0]), f2_to_bf2(h[1]), f2_to_bf2(h[2]), f2_to_bf2(h[3]));
-          // keep the modulation loads of at most four vectors in flight (register budget)
-          if ((k & 3) == 3) asm volatile("" ::: "memory");
+          if constexpr (HAS_W) wu = cache_w[c];
+          uint4 ru;
+          const uint4 hu = rms_h_res8<HAS_W>(r.v[k], inv2, wu, sf, bu, tw_max, ru);
+          if (rrow) *reinterpret_cast<uint4*>(rrow + 8 * c) = ru;
+          *reinterpret_cast<uint4*>(hrow + 8 * c) = hu;
         }
       });
   flush_amax(a.amax, tw_max);

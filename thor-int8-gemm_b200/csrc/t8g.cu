@@ -574,7 +574,8 @@ int launch_rows(K kern, int T, const A& args, t8g::rows::RingGeom g, int64_t row
 }
 
 // Launch a warp-ring row kernel (one row per warp): kWarpStages slots per warp and as
-// many warps per CTA as ~216 KB of shared memory holds (at most 32), one CTA per SM.
+// many warps per CTA as the shared-memory budget holds (216 KB by default; at most 32), one
+// CTA per SM.
 constexpr int kWarpStages = 2;
 
 // `tail_bytes` of shared memory follow the rings (a kernel's own table); with
@@ -585,6 +586,7 @@ struct WarpLaunch {
   size_t tail_bytes = 0;
   bool contiguous = false;
   bool padded = false;   // rows in 256-byte pieces at the padded pitch (reference-order reduction)
+  size_t smem_budget = 216 * 1024;   // rings + tail
 };
 
 template <typename K, typename A, typename... Extra>
@@ -598,7 +600,7 @@ int launch_warp_rows(K kern, const A& args, uint32_t row_bytes, int64_t rows, in
   g.padded = opt.padded ? 1 : 0;
   g.slot_bytes = ((opt.padded ? padded_row_bytes(row_bytes) : row_bytes) + 127u) & ~127u;
   g.stages = kWarpStages;
-  const int64_t budget = static_cast<int64_t>(216 * 1024 - kWarpRingHeader) - static_cast<int64_t>(opt.tail_bytes);
+  const int64_t budget = static_cast<int64_t>(opt.smem_budget - kWarpRingHeader) - static_cast<int64_t>(opt.tail_bytes);
   int64_t warps = budget / (static_cast<int64_t>(g.stages) * g.slot_bytes);
   if (warps > opt.max_warps) warps = opt.max_warps;
   if (warps < 1) return fail(T8G_ERR_UNSUPPORTED, "%s: row too long for a warp ring", what);
@@ -754,10 +756,19 @@ int rms_common(bool tensorwise, const void* x, int64_t ld_x, const void* w, cons
     // phase A sums the squares in the reference's order (rows in the padded layout)
     T8G_CHECK_CUDA(cudaMemsetAsync(amax, 0, sizeof(float), st), "cudaMemsetAsync(amax)");
     if (nv) {
+      // the block's modulation row and the norm weight cached per CTA
       WarpLaunch o = reg_launch;
       o.padded = true;
-      T8G_DISPATCH_NV(nv, rc = launch_warp_rows(rms_mod_tw_reg_kernel<NV>, a, row_bytes, S, dev, info.sms, st, o,
-                                                "rms_mod phase A"));
+      o.contiguous = true;
+      o.tail_bytes = static_cast<size_t>((w ? 8 : 6) * D);   // fp32 multiplier + bf16 shift (+ bf16 weight)
+      o.smem_budget = kRowSmemLimit;
+      if (w) {
+        T8G_DISPATCH_NV(nv, rc = launch_warp_rows(rms_mod_tw_cached_kernel<NV, true>, a, row_bytes, S, dev, info.sms,
+                                                  st, o, "rms_mod phase A"));
+      } else {
+        T8G_DISPATCH_NV(nv, rc = launch_warp_rows(rms_mod_tw_cached_kernel<NV, false>, a, row_bytes, S, dev, info.sms,
+                                                  st, o, "rms_mod phase A"));
+      }
     } else if (warp_rows) {
       WarpLaunch o;
       o.padded = true;
