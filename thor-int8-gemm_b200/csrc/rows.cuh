@@ -1085,84 +1085,6 @@ __global__ void __launch_bounds__(512, 1) rms_mod_simple_kernel(const RmsArgs a,
       });
 }
 
-// RMSNorm + modulation + per-token quantisation (every option of the entry point: norm
-// weight, mod_index, scale as multiplier, h / res outputs) for rows of 256 NV elements held
-// in registers.
-template <int NV, int QK>
-__global__ void __launch_bounds__(512, 1) rms_mod_warp_reg_kernel(const RmsArgs a, const WarpRingGeom g) {
-  extern __shared__ __align__(1024) uint8_t smem[];
-  const int lane = threadIdx.x & 31;
-  int64_t cur_m = -1;
-  int64_t seg_end = -1;
-  auto src = [&](int64_t r) -> const void* { return a.x + r * a.ld_x; };
-  warp_row_loop_reg(
-      smem, g, a.S, src, [&](const uint8_t* slot) { return load_row_regs<NV>(slot, lane); },
-      [&](int64_t row, RowRegs<NV>& r) {
-        const float inv = row_inv_reg<NV>(r, a.eps);
-        const float2 inv2 = make_float2(inv, inv);
-        int64_t m;
-        if (a.mod_index) {
-          m = static_cast<int64_t>(__ldg(a.mod_index + row));
-        } else if (row < seg_end) {
-          m = cur_m;
-        } else {
-          m = row / a.rows_per_mod;
-          seg_end = (m + 1) * a.rows_per_mod;
-        }
-        cur_m = m;
-        const __nv_bfloat16* srow = a.scale + m * a.ld_mod;
-        const __nv_bfloat16* brow = a.shift + m * a.ld_mod;
-        uint32_t m2 = 0;
-#pragma unroll
-        for (int k = 0; k < NV; ++k) {
-          const int c = 32 * k + lane;
-          uint4 su = ld_v4(srow + 8 * c);
-          const uint4 bu = ld_v4(brow + 8 * c);
-          if (!a.scale_is_multiplier)
-            su = make_uint4(one_plus_bf16x2(su.x), one_plus_bf16x2(su.y), one_plus_bf16x2(su.z),
-                            one_plus_bf16x2(su.w));
-          const uint32_t xw[4] = {r.v[k].x, r.v[k].y, r.v[k].z, r.v[k].w};
-          const uint32_t sw[4] = {su.x, su.y, su.z, su.w};
-          const uint32_t bw[4] = {bu.x, bu.y, bu.z, bu.w};
-          uint4 wu = make_uint4(0, 0, 0, 0);
-          if (a.w) wu = ld_v4(a.w + 8 * c);
-          const uint32_t ww[4] = {wu.x, wu.y, wu.z, wu.w};
-          float2 h[4], x[4];
-#pragma unroll
-          for (int p = 0; p < 4; ++p) {
-            x[p] = bf2_to_f2(xw[p]);
-            float2 t = mul2_rn(x[p], inv2);
-            if (a.w) t = mul2_rn(t, bf2_to_f2(ww[p]));
-            t = mul2_rn(t, bf2_to_f2(sw[p]));
-            h[p] = add_f32_bf16x2(t, bw[p]);
-          }
-          const uint4 hu = make_uint4(f2_to_bf2(h[0]), f2_to_bf2(h[1]), f2_to_bf2(h[2]), f2_to_bf2(h[3]));
-          {
-            if (a.res) {
-              uint4 ru;
-              ru.x = f2_to_bf2(add2_rn(h[0], x[0]));
-              ru.y = f2_to_bf2(add2_rn(h[1], x[1]));
-              ru.z = f2_to_bf2(add2_rn(h[2], x[2]));
-              ru.w = f2_to_bf2(add2_rn(h[3], x[3]));
-              *reinterpret_cast<uint4*>(a.res + row * a.ld_res + 8 * c) = ru;
-            }
-            if (a.h) *reinterpret_cast<uint4*>(a.h + row * a.ld_h + 8 * c) = hu;
-          }
-          m2 = absmax4(m2, hu);
-          r.v[k] = hu;
-          // keep the modulation loads of at most four vectors in flight (register budget)
-          if ((k & 3) == 3) asm volatile("" ::: "memory");
-        }
-        float mx = pair_max(m2);
-        mx = warp_max_nonneg(mx);
-        const QuantRow qr = quant_row<QK>(mx);
-        if (lane == 0) a.q_scale[row] = qr.scale;
-        uint8_t* qrow = static_cast<uint8_t*>(a.q) + row * a.ld_q;
-#pragma unroll
-        for (int k = 0; k < NV; ++k) store_q<QK>(qrow, 32 * k + lane, r.v[k], qr);
-      });
-}
-
 // ---------------------------------------------------------------- tensorwise (reference) norm
 // The reference's fused_rms_mod_quant and its per-segment driver (src/ck_fused_mod_norm_quant.py:
 // 23-55, src/ck_fused_patch.py:105-136) derive one scale for the whole tensor from the
@@ -1269,11 +1191,11 @@ struct RowRegsSS {
 
 // h and res of one vector from x, inv, the norm weight (HAS_W), the fp32 multiplier pairs s
 // and the packed bf16 shift: h = RN(RN(RN(RN(x * inv) * w) * s) + b), the product with w left
-// out without a weight (the order of rms_h8), res = bf16(h + x); folds the float32 |h| into
-// amax.
+// out without a weight (the order of rms_h8), res = bf16(h + x) when asked; folds the float32
+// |h| into amax.
 template <bool HAS_W>
 __device__ __forceinline__ uint4 rms_h_res8(const uint4& xu, float2 inv2, const uint4& wu, const float2 (&s)[4],
-                                            const uint4& bu, float& amax, uint4& res) {
+                                            const uint4& bu, float& amax, bool want_res, uint4& res) {
   const uint32_t xw[4] = {xu.x, xu.y, xu.z, xu.w};
   const uint32_t ww[4] = {wu.x, wu.y, wu.z, wu.w};
   const uint32_t bw[4] = {bu.x, bu.y, bu.z, bu.w};
@@ -1286,10 +1208,74 @@ __device__ __forceinline__ uint4 rms_h_res8(const uint4& xu, float2 inv2, const 
     const float2 h = add_f32_bf16x2(mul2_rn(t, s[p]), bw[p]);
     amax = max3_abs(amax, h.x, h.y);
     hw[p] = f2_to_bf2(h);
-    rw[p] = f2_to_bf2(add2_rn(h, x));
+    if (want_res) rw[p] = f2_to_bf2(add2_rn(h, x));
   }
-  res = make_uint4(rw[0], rw[1], rw[2], rw[3]);
+  if (want_res) res = make_uint4(rw[0], rw[1], rw[2], rw[3]);
   return make_uint4(hw[0], hw[1], hw[2], hw[3]);
+}
+
+// Shared memory after the warp rings of the cached norm kernels: the multiplier s of the cached
+// modulation row as fp32 (elements 8c..8c+3 at [c], 8c+4..8c+7 at [NVEC + c], lane-contiguous
+// 16-byte reads), its shift as bf16 ([2 NVEC + c]) and, with a weight, the norm weight as bf16
+// ([3 NVEC + c]): 6 D bytes, 8 D with a weight.
+template <int NV>
+__device__ __forceinline__ float4* mod_cache_of(uint8_t* smem, const WarpRingGeom& g) {
+  return reinterpret_cast<float4*>(smem + kWarpRingHeader +
+                                   static_cast<size_t>(blockDim.x >> 5) * g.stages * g.slot_bytes);
+}
+
+// Fills the CTA's modulation cache (and norm weight) for the modulation row of its block's
+// middle row; returns that row, -1 for an empty block.  The caller synchronises the CTA.
+template <int NV, bool HAS_W>
+__device__ __forceinline__ int64_t fill_mod_cache(const RmsArgs& a, const WarpRingGeom& g, float4* cache) {
+  constexpr int NVEC = 32 * NV;
+  const int64_t r0 = static_cast<int64_t>(blockIdx.x) * g.cta_rows;
+  const int64_t r1 = min(a.S, r0 + g.cta_rows);
+  if (r0 >= r1) return -1;
+  const int64_t mid = (r0 + r1 - 1) >> 1;
+  const int64_t cm = a.mod_index ? static_cast<int64_t>(__ldg(a.mod_index + mid)) : mid / a.rows_per_mod;
+  uint4* cache_b = reinterpret_cast<uint4*>(cache + 2 * NVEC);
+  for (int c = threadIdx.x; c < NVEC; c += blockDim.x) {
+    uint4 su = ld_v4(a.scale + cm * a.ld_mod + 8 * c);
+    if (!a.scale_is_multiplier)
+      su = make_uint4(one_plus_bf16x2(su.x), one_plus_bf16x2(su.y), one_plus_bf16x2(su.z), one_plus_bf16x2(su.w));
+    float2 sf[4];
+    unpack_pairs(su, sf);
+    cache[c] = make_float4(sf[0].x, sf[0].y, sf[1].x, sf[1].y);
+    cache[NVEC + c] = make_float4(sf[2].x, sf[2].y, sf[3].x, sf[3].y);
+    cache_b[c] = ld_v4(a.shift + cm * a.ld_mod + 8 * c);
+    if constexpr (HAS_W) cache_b[NVEC + c] = ld_v4(a.w + 8 * c);
+  }
+  return cm;
+}
+
+// s (fp32 pairs) and the packed shift of vector c of modulation row m: from the cache when m is
+// the cached row, else from global memory.
+template <int NV>
+__device__ __forceinline__ void mod_of(const RmsArgs& a, const float4* cache, bool cached, int64_t m, int c,
+                                       float2 (&sf)[4], uint4& bu) {
+  constexpr int NVEC = 32 * NV;
+  if (cached) {
+    const float4 s0 = cache[c];
+    const float4 s1 = cache[NVEC + c];
+    sf[0] = make_float2(s0.x, s0.y);
+    sf[1] = make_float2(s0.z, s0.w);
+    sf[2] = make_float2(s1.x, s1.y);
+    sf[3] = make_float2(s1.z, s1.w);
+    bu = reinterpret_cast<const uint4*>(cache + 2 * NVEC)[c];
+  } else {
+    uint4 su = ld_v4(a.scale + m * a.ld_mod + 8 * c);
+    if (!a.scale_is_multiplier)
+      su = make_uint4(one_plus_bf16x2(su.x), one_plus_bf16x2(su.y), one_plus_bf16x2(su.z), one_plus_bf16x2(su.w));
+    unpack_pairs(su, sf);
+    bu = ld_v4(a.shift + m * a.ld_mod + 8 * c);
+  }
+}
+
+// The cached norm weight's vector c.
+template <int NV>
+__device__ __forceinline__ uint4 weight_of(const float4* cache, int c) {
+  return reinterpret_cast<const uint4*>(cache + 2 * 32 * NV)[32 * NV + c];
 }
 
 // Phase A of the tensorwise norm for rows of 256 NV elements (every option of the entry
@@ -1305,33 +1291,9 @@ __global__ void __launch_bounds__(512, 1) rms_mod_tw_cached_kernel(const RmsArgs
   extern __shared__ __align__(1024) uint8_t smem[];
   constexpr int D = 256 * NV;
   constexpr int NCH = (D + kRefBlock - 1) / kRefBlock;
-  constexpr int NVEC = 32 * NV;
   const int lane = threadIdx.x & 31;
-  const int W = blockDim.x >> 5;
-  float4* cache_lo = reinterpret_cast<float4*>(smem + kWarpRingHeader + static_cast<size_t>(W) * g.stages * g.slot_bytes);
-  float4* cache_hi = cache_lo + NVEC;
-  uint4* cache_b = reinterpret_cast<uint4*>(cache_hi + NVEC);
-  uint4* cache_w = cache_b + NVEC;   // HAS_W only
-  const int64_t r0 = static_cast<int64_t>(blockIdx.x) * g.cta_rows;
-  const int64_t r1 = min(a.S, r0 + g.cta_rows);
-  int64_t cm = -1;
-  if (r0 < r1) {
-    const int64_t mid = (r0 + r1 - 1) >> 1;
-    cm = a.mod_index ? static_cast<int64_t>(__ldg(a.mod_index + mid)) : mid / a.rows_per_mod;
-  }
-  if (cm >= 0) {
-    for (int c = threadIdx.x; c < NVEC; c += blockDim.x) {
-      uint4 su = ld_v4(a.scale + cm * a.ld_mod + 8 * c);
-      if (!a.scale_is_multiplier)
-        su = make_uint4(one_plus_bf16x2(su.x), one_plus_bf16x2(su.y), one_plus_bf16x2(su.z), one_plus_bf16x2(su.w));
-      float2 sf[4];
-      unpack_pairs(su, sf);
-      cache_lo[c] = make_float4(sf[0].x, sf[0].y, sf[1].x, sf[1].y);
-      cache_hi[c] = make_float4(sf[2].x, sf[2].y, sf[3].x, sf[3].y);
-      cache_b[c] = ld_v4(a.shift + cm * a.ld_mod + 8 * c);
-      if constexpr (HAS_W) cache_w[c] = ld_v4(a.w + 8 * c);
-    }
-  }
+  float4* cache = mod_cache_of<NV>(smem, g);
+  const int64_t cm = fill_mod_cache<NV, HAS_W>(a, g, cache);
   __syncthreads();
   int64_t cur_m = -1, seg_end = -1;
   float tw_max = 0.f;
@@ -1356,31 +1318,63 @@ __global__ void __launch_bounds__(512, 1) rms_mod_tw_cached_kernel(const RmsArgs
           const int c = 32 * k + lane;
           float2 sf[4];
           uint4 bu;
-          if (m == cm) {
-            const float4 s0 = cache_lo[c];
-            const float4 s1 = cache_hi[c];
-            sf[0] = make_float2(s0.x, s0.y);
-            sf[1] = make_float2(s0.z, s0.w);
-            sf[2] = make_float2(s1.x, s1.y);
-            sf[3] = make_float2(s1.z, s1.w);
-            bu = cache_b[c];
-          } else {
-            uint4 su = ld_v4(a.scale + m * a.ld_mod + 8 * c);
-            if (!a.scale_is_multiplier)
-              su = make_uint4(one_plus_bf16x2(su.x), one_plus_bf16x2(su.y), one_plus_bf16x2(su.z),
-                              one_plus_bf16x2(su.w));
-            unpack_pairs(su, sf);
-            bu = ld_v4(a.shift + m * a.ld_mod + 8 * c);
-          }
+          mod_of<NV>(a, cache, m == cm, m, c, sf, bu);
           uint4 wu = make_uint4(0, 0, 0, 0);
-          if constexpr (HAS_W) wu = cache_w[c];
+          if constexpr (HAS_W) wu = weight_of<NV>(cache, c);
           uint4 ru;
-          const uint4 hu = rms_h_res8<HAS_W>(r.v[k], inv2, wu, sf, bu, tw_max, ru);
+          const uint4 hu = rms_h_res8<HAS_W>(r.v[k], inv2, wu, sf, bu, tw_max, rrow != nullptr, ru);
           if (rrow) *reinterpret_cast<uint4*>(rrow + 8 * c) = ru;
           *reinterpret_cast<uint4*>(hrow + 8 * c) = hu;
         }
       });
   flush_amax(a.amax, tw_max);
+}
+
+// RMSNorm + modulation + per-token quantisation with every option of the entry point (norm
+// weight when HAS_W, mod_index or batch-major rows_per_mod, scale as multiplier, h / res
+// outputs) for rows of 256 NV elements held in registers: the canonical sum of squares
+// (row_inv_reg), the CTA's cached modulation row and norm weight (fill_mod_cache), and the
+// quantiser of rms_mod_simple_kernel.
+template <int NV, int QK, bool HAS_W>
+__global__ void __launch_bounds__(512, 1) rms_mod_cached_kernel(const RmsArgs a, const WarpRingGeom g) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const int lane = threadIdx.x & 31;
+  float4* cache = mod_cache_of<NV>(smem, g);
+  const int64_t cm = fill_mod_cache<NV, HAS_W>(a, g, cache);
+  __syncthreads();
+  int64_t cur_m = -1, seg_end = -1;
+  auto src = [&](int64_t r) -> const void* { return a.x + r * a.ld_x; };
+  warp_row_loop_reg(
+      smem, g, a.S, src, [&](const uint8_t* slot) { return load_row_regs<NV>(slot, lane); },
+      [&](int64_t row, RowRegs<NV>& r) {
+        const float inv = row_inv_reg<NV>(r, a.eps);
+        const float2 inv2 = make_float2(inv, inv);
+        const int64_t m = mod_row_of(a, row, cur_m, seg_end);
+        __nv_bfloat16* hrow = a.h ? a.h + row * a.ld_h : nullptr;
+        __nv_bfloat16* rrow = a.res ? a.res + row * a.ld_res : nullptr;
+        float amax = 0.f;
+#pragma unroll
+        for (int k = 0; k < NV; ++k) {
+          const int c = 32 * k + lane;
+          float2 sf[4];
+          uint4 bu;
+          mod_of<NV>(a, cache, m == cm, m, c, sf, bu);
+          uint4 wu = make_uint4(0, 0, 0, 0);
+          if constexpr (HAS_W) wu = weight_of<NV>(cache, c);
+          uint4 ru;
+          const uint4 hu = rms_h_res8<HAS_W>(r.v[k], inv2, wu, sf, bu, amax, rrow != nullptr, ru);
+          if (rrow) *reinterpret_cast<uint4*>(rrow + 8 * c) = ru;
+          if (hrow) *reinterpret_cast<uint4*>(hrow + 8 * c) = hu;
+          r.v[k] = hu;
+        }
+        amax = warp_max_nonneg(amax);
+        // max |bf16(h)| = bf16(max |h|): rounding is monotone and symmetric
+        const QuantRow qr = quant_row<QK>(__bfloat162float(__float2bfloat16_rn(amax)));
+        if (lane == 0) a.q_scale[row] = qr.scale;
+        uint8_t* qrow = static_cast<uint8_t*>(a.q) + row * a.ld_q;
+#pragma unroll
+        for (int k = 0; k < NV; ++k) store_q<QK>(qrow, 32 * k + lane, r.v[k], qr);
+      });
 }
 
 // The same for longer rows, one CTA (row group of T threads) per row: its first warp sums

@@ -808,12 +808,25 @@ int rms_common(bool tensorwise, const void* x, int64_t ld_x, const void* w, cons
         T8G_DISPATCH_NV(nv, rc = launch_warp_rows(rms_mod_simple_kernel<NV, kQuantInt8>, a, row_bytes, S, dev,
                                                   info.sms, st, o, "rms_mod_quant"));
       }
-    } else if (fp8) {
-      T8G_DISPATCH_NV(nv, rc = launch_warp_rows(rms_mod_warp_reg_kernel<NV, kQuantFp8>, a, row_bytes, S, dev,
-                                                info.sms, st, reg_launch, "rms_mod_quant"));
     } else {
-      T8G_DISPATCH_NV(nv, rc = launch_warp_rows(rms_mod_warp_reg_kernel<NV, kQuantInt8>, a, row_bytes, S, dev,
-                                                info.sms, st, reg_launch, "rms_mod_quant"));
+      // every other option: the block's modulation row and the norm weight cached per CTA
+      WarpLaunch o = reg_launch;
+      o.contiguous = true;
+      o.tail_bytes = static_cast<size_t>((w ? 8 : 6) * D);   // fp32 multiplier + bf16 shift (+ bf16 weight)
+      o.smem_budget = kRowSmemLimit;
+      if (fp8 && w) {
+        T8G_DISPATCH_NV(nv, rc = launch_warp_rows(rms_mod_cached_kernel<NV, kQuantFp8, true>, a, row_bytes, S, dev,
+                                                  info.sms, st, o, "rms_mod_quant"));
+      } else if (fp8) {
+        T8G_DISPATCH_NV(nv, rc = launch_warp_rows(rms_mod_cached_kernel<NV, kQuantFp8, false>, a, row_bytes, S, dev,
+                                                  info.sms, st, o, "rms_mod_quant"));
+      } else if (w) {
+        T8G_DISPATCH_NV(nv, rc = launch_warp_rows(rms_mod_cached_kernel<NV, kQuantInt8, true>, a, row_bytes, S, dev,
+                                                  info.sms, st, o, "rms_mod_quant"));
+      } else {
+        T8G_DISPATCH_NV(nv, rc = launch_warp_rows(rms_mod_cached_kernel<NV, kQuantInt8, false>, a, row_bytes, S, dev,
+                                                  info.sms, st, o, "rms_mod_quant"));
+      }
     }
     return rc;
   }
