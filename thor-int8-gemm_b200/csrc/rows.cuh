@@ -819,7 +819,7 @@ __device__ __forceinline__ void warp_row_loop_reg(uint8_t* smem, const WarpRingG
     const bool ok = mbar_wait(&full[st], ph, kStatusTimeoutProducer);
     if (__any_sync(0xFFFFFFFFu, !ok)) break;
     uint8_t* slot = slots + static_cast<size_t>(st) * g.slot_bytes;
-    auto regs = load(slot);
+    auto regs = load(slot, row);
     __syncwarp();
     {
       const int64_t r = row + ahead;
@@ -863,7 +863,7 @@ __global__ void __launch_bounds__(512, 1) quant_rows_warp_reg_kernel(const Quant
   const int lane = threadIdx.x & 31;
   auto src = [&](int64_t r) -> const void* { return a.x + r * a.ld_x; };
   warp_row_loop_reg(
-      smem, g, a.S, src, [&](const uint8_t* slot) { return load_row_regs<NV>(slot, lane); },
+      smem, g, a.S, src, [&](const uint8_t* slot, int64_t) { return load_row_regs<NV>(slot, lane); },
       [&](int64_t row, const RowRegs<NV>& r) {
         uint32_t m2 = 0;
 #pragma unroll
@@ -1046,7 +1046,7 @@ __global__ void __launch_bounds__(512, 1) rms_mod_simple_kernel(const RmsArgs a,
   int64_t seg_end = -1;
   auto src = [&](int64_t r) -> const void* { return a.x + r * a.ld_x; };
   warp_row_loop_reg(
-      smem, g, a.S, src, [&](const uint8_t* slot) { return load_row_regs<NV>(slot, lane); },
+      smem, g, a.S, src, [&](const uint8_t* slot, int64_t) { return load_row_regs<NV>(slot, lane); },
       [&](int64_t row, RowRegs<NV>& r) {
         const float inv = row_inv_reg<NV>(r, a.eps);
         int64_t m;
@@ -1300,7 +1300,7 @@ __global__ void __launch_bounds__(512, 1) rms_mod_tw_cached_kernel(const RmsArgs
   auto src = [&](int64_t r) -> const void* { return a.x + r * a.ld_x; };
   warp_row_loop_reg(
       smem, g, a.S, src,
-      [&](const uint8_t* slot) {
+      [&](const uint8_t* slot, int64_t) {
         RowRegsSS<NV> r;
         r.ss = ref_sumsq_warp<NCH>(slot, D, lane);
 #pragma unroll
@@ -1345,11 +1345,11 @@ __global__ void __launch_bounds__(512, 1) rms_mod_cached_kernel(const RmsArgs a,
   int64_t cur_m = -1, seg_end = -1;
   auto src = [&](int64_t r) -> const void* { return a.x + r * a.ld_x; };
   warp_row_loop_reg(
-      smem, g, a.S, src, [&](const uint8_t* slot) { return load_row_regs<NV>(slot, lane); },
+      smem, g, a.S, src, [&](const uint8_t* slot, int64_t) { return load_row_regs<NV>(slot, lane); },
       [&](int64_t row, RowRegs<NV>& r) {
+        const int64_t m = mod_row_of(a, row, cur_m, seg_end);   // issued before the sum, which hides its latency
         const float inv = row_inv_reg<NV>(r, a.eps);
         const float2 inv2 = make_float2(inv, inv);
-        const int64_t m = mod_row_of(a, row, cur_m, seg_end);
         __nv_bfloat16* hrow = a.h ? a.h + row * a.ld_h : nullptr;
         __nv_bfloat16* rrow = a.res ? a.res + row * a.ld_res : nullptr;
         float amax = 0.f;
