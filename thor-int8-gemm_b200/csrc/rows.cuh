@@ -56,13 +56,6 @@ struct QMax<kQuantFp8> {
 // ---------------------------------------------------------------- bf16 helpers
 __device__ __forceinline__ float bf_lo(uint32_t u) { return __uint_as_float(u << 16); }
 __device__ __forceinline__ float bf_hi(uint32_t u) { return __uint_as_float(u & 0xFFFF0000u); }
-__device__ __forceinline__ void unpack8(const uint4& v, float (&f)[8]) {
-  f[0] = bf_lo(v.x); f[1] = bf_hi(v.x); f[2] = bf_lo(v.y); f[3] = bf_hi(v.y);
-  f[4] = bf_lo(v.z); f[5] = bf_hi(v.z); f[6] = bf_lo(v.w); f[7] = bf_hi(v.w);
-}
-__device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
-  return make_uint4(pack_bf16(f[0], f[1]), pack_bf16(f[2], f[3]), pack_bf16(f[4], f[5]), pack_bf16(f[6], f[7]));
-}
 // bf16(1 + s) for a packed pair: a correctly rounded bf16 add, equal to the
 // reference's fp32 add then bf16 rounding (src/ck_fused_patch.py:120).
 __device__ __forceinline__ uint32_t one_plus_bf16x2(uint32_t s) {
