@@ -80,3 +80,10 @@ def test_compiled_fused_block_tail_matches_eager(mods):
     args = (q, qs, w1i, ws1i, w2, ws2, x, gate)
     compiled = torch.compile(tail, backend="aot_eager", fullgraph=True)
     assert torch.equal(compiled(*args), eager(*args))
+
+    def tail_q(q, qs, w1i, ws1i, w2, ws2, x, gate):
+        a, as_ = torch.ops.t8g.gemm_swiglu_quant(q, w1i, qs, ws1i, None, "int8")
+        return torch.ops.t8g.gemm_gated(a, w2, as_, ws2, None, x, gate, T // 2)
+
+    compiled_q = torch.compile(tail_q, backend="aot_eager", fullgraph=True)
+    assert torch.equal(compiled_q(*args), eager(*args))

@@ -42,6 +42,8 @@ def test_fake_shapes(t8g):
             torch.ops.t8g.gemm_dequant(x8, _fake(mode, (9216, 1024), torch.int8), xs, ws, None, torch.bfloat16)
         a = torch.ops.t8g.gemm_swiglu(x8, w8, xs, ws, None)
         assert a.shape == (300, 4608) and a.dtype == torch.bfloat16
+        q, s = torch.ops.t8g.gemm_swiglu_quant(x8, w8, xs, ws, None, "fp8_e4m3")
+        assert q.shape == (300, 4608) and q.dtype == torch.float8_e4m3fn and s.shape == (300,)
         res = _fake(mode, (300, 9216), torch.bfloat16)
         g = torch.ops.t8g.gemm_gated(x8, w8, xs, ws, None, res, _fake(mode, (2, 9216), torch.bfloat16), 150)
         assert g.shape == (300, 9216) and g.dtype == torch.bfloat16

@@ -111,6 +111,20 @@ def _(x, w_il, x_scale, w_scale_il, bias_il):
     return x.new_empty((x.shape[0], w_il.shape[0] // 2), dtype=torch.bfloat16)
 
 
+@torch.library.custom_op("t8g::gemm_swiglu_quant", mutates_args=())
+def gemm_swiglu_quant(x: torch.Tensor, w_il: torch.Tensor, x_scale: torch.Tensor, w_scale_il: torch.Tensor,
+                      bias_il: Optional[torch.Tensor], kind: str) -> tuple[torch.Tensor, torch.Tensor]:
+    q, q_scale, _act = ops.gemm_swiglu_quant(x, w_il, x_scale, w_scale_il, bias_il, kind=kind)
+    return q, q_scale
+
+
+@gemm_swiglu_quant.register_fake
+def _(x, w_il, x_scale, w_scale_il, bias_il, kind):
+    torch._check(x.dim() == 2 and w_il.dim() == 2 and x.shape[1] == w_il.shape[1], lambda: "x [M, K], w [2F, K]")
+    return x.new_empty((x.shape[0], w_il.shape[0] // 2), dtype=_qdtype(kind)), \
+        x.new_empty((x.shape[0],), dtype=torch.float32)
+
+
 @torch.library.custom_op("t8g::gemm_gated", mutates_args=())
 def gemm_gated(x: torch.Tensor, w: torch.Tensor, x_scale: torch.Tensor, w_scale: torch.Tensor,
                bias: Optional[torch.Tensor], res: torch.Tensor, gate: torch.Tensor, rows_per_gate: int) -> torch.Tensor:
