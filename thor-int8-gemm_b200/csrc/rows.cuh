@@ -1265,6 +1265,29 @@ __device__ __forceinline__ void mod_of(const RmsArgs& a, const float4* cache, bo
   }
 }
 
+// h (and res, when asked) of vector c of a row whose modulation row m is not the CTA's cached
+// one: the modulation read from global memory.  Out of line (rare), with the row's vector passed
+// by value, so that the caller's row stays in registers; stores h / res when their rows are
+// given and folds |h| into *amax.
+template <bool HAS_W>
+__device__ __noinline__ uint4 rms_h_res_global8(const __nv_bfloat16* srow, const __nv_bfloat16* brow, int multiplier,
+                                                int c, uint4 xu, float inv, uint4 wu, float* amax,
+                                                __nv_bfloat16* rrow, __nv_bfloat16* hrow) {
+  uint4 su = ld_v4(srow + 8 * c);
+  if (!multiplier)
+    su = make_uint4(one_plus_bf16x2(su.x), one_plus_bf16x2(su.y), one_plus_bf16x2(su.z), one_plus_bf16x2(su.w));
+  float2 sf[4];
+  unpack_pairs(su, sf);
+  const uint4 bu = ld_v4(brow + 8 * c);
+  float mx = *amax;
+  uint4 ru;
+  const uint4 hu = rms_h_res8<HAS_W>(xu, make_float2(inv, inv), wu, sf, bu, mx, rrow != nullptr, ru);
+  *amax = mx;
+  if (rrow) *reinterpret_cast<uint4*>(rrow + 8 * c) = ru;
+  if (hrow) *reinterpret_cast<uint4*>(hrow + 8 * c) = hu;
+  return hu;
+}
+
 // The cached norm weight's vector c.
 template <int NV>
 __device__ __forceinline__ uint4 weight_of(const float4* cache, int c) {
@@ -1306,6 +1329,8 @@ __global__ void __launch_bounds__(512, 1) rms_mod_tw_cached_kernel(const RmsArgs
         const int64_t m = mod_row_of(a, row, cur_m, seg_end);
         __nv_bfloat16* hrow = a.h + row * a.ld_h;
         __nv_bfloat16* rrow = a.res ? a.res + row * a.ld_res : nullptr;
+        // (the per-vector cached / global choice measured faster here than one branch per row
+        // with an out-of-line global path, which the per-token kernel below uses)
 #pragma unroll
         for (int k = 0; k < NV; ++k) {
           const int c = 32 * k + lane;
@@ -1346,19 +1371,30 @@ __global__ void __launch_bounds__(512, 1) rms_mod_cached_kernel(const RmsArgs a,
         __nv_bfloat16* hrow = a.h ? a.h + row * a.ld_h : nullptr;
         __nv_bfloat16* rrow = a.res ? a.res + row * a.ld_res : nullptr;
         float amax = 0.f;
+        if (m == cm) {
 #pragma unroll
-        for (int k = 0; k < NV; ++k) {
-          const int c = 32 * k + lane;
-          float2 sf[4];
-          uint4 bu;
-          mod_of<NV>(a, cache, m == cm, m, c, sf, bu);
-          uint4 wu = make_uint4(0, 0, 0, 0);
-          if constexpr (HAS_W) wu = weight_of<NV>(cache, c);
-          uint4 ru;
-          const uint4 hu = rms_h_res8<HAS_W>(r.v[k], inv2, wu, sf, bu, amax, rrow != nullptr, ru);
-          if (rrow) *reinterpret_cast<uint4*>(rrow + 8 * c) = ru;
-          if (hrow) *reinterpret_cast<uint4*>(hrow + 8 * c) = hu;
-          r.v[k] = hu;
+          for (int k = 0; k < NV; ++k) {
+            const int c = 32 * k + lane;
+            float2 sf[4];
+            uint4 bu;
+            mod_of<NV>(a, cache, true, m, c, sf, bu);
+            uint4 wu = make_uint4(0, 0, 0, 0);
+            if constexpr (HAS_W) wu = weight_of<NV>(cache, c);
+            uint4 ru;
+            const uint4 hu = rms_h_res8<HAS_W>(r.v[k], inv2, wu, sf, bu, amax, rrow != nullptr, ru);
+            if (rrow) *reinterpret_cast<uint4*>(rrow + 8 * c) = ru;
+            if (hrow) *reinterpret_cast<uint4*>(hrow + 8 * c) = hu;
+            r.v[k] = hu;
+          }
+        } else {
+#pragma unroll
+          for (int k = 0; k < NV; ++k) {
+            const int c = 32 * k + lane;
+            uint4 wu = make_uint4(0, 0, 0, 0);
+            if constexpr (HAS_W) wu = weight_of<NV>(cache, c);
+            r.v[k] = rms_h_res_global8<HAS_W>(a.scale + m * a.ld_mod, a.shift + m * a.ld_mod, a.scale_is_multiplier,
+                                              c, r.v[k], inv, wu, &amax, rrow, hrow);
+          }
         }
         amax = warp_max_nonneg(amax);
         // max |bf16(h)| = bf16(max |h|): rounding is monotone and symmetric
