@@ -281,6 +281,22 @@ def test_rms_mod_quant_tensorwise_dit_form(ops, kind, B, T, D, want_res):
     assert ops.device_status() == 0
 
 
+@pytest.mark.parametrize("kind", ["fp8_e4m3", "int8"])
+def test_tensorwise_forms_on_empty_input_give_the_floor_scale(ops, kind):
+    """No rows: amax is 0, so the one scale is the 1e-12 floor (the reference's amax and quant
+    kernels on an empty tensor); nothing else is written."""
+    x = torch.empty(0, 3072, dtype=torch.bfloat16, device="cuda")
+    mod = torch.zeros(1, 3072, dtype=torch.bfloat16, device="cuda")
+    q, qs, h, res = ops.rms_mod_quant_tensorwise(x, mod, mod, eps=1e-6, kind=kind)
+    assert q.shape == (0, 3072) and h.shape == (0, 3072)
+    assert np.float32(qs.item()) == O.scale_from_amax(np.float32(0.0), KINDS[kind])
+    y = torch.empty(0, 2 * 1024, dtype=torch.bfloat16, device="cuda")
+    q, qs, act = ops.swiglu_quant_tensorwise(y[:, :1024], y[:, 1024:], kind=kind)
+    assert q.shape == (0, 1024) and act.shape == (0, 1024)
+    assert np.float32(qs.item()) == O.scale_from_amax(np.float32(0.0), KINDS[kind])
+    assert ops.device_status() == 0
+
+
 @pytest.mark.parametrize("kind", ["int8", "fp8_e4m3"])
 @pytest.mark.parametrize("M,F", [(8, 512), (33, 1536), (64, 12288), (5, 16384), (3, 24576)])
 def test_swiglu_quant_per_token(ops, kind, M, F):

@@ -699,6 +699,26 @@ int launch_quant_given(const t8g::rows::QuantGivenArgs& b, int quant_kind, int s
   return launch_checked("quant phase B launch");
 }
 
+// The tensorwise forms on an empty tensor: amax = 0, so the scale is the floor 1e-12, as the
+// reference's amax and quant kernels give for no elements (src/ck_fused_mod_norm_quant.py:
+// 92-111); phase B with no rows writes just the scale.
+int empty_tensorwise(float* amax, float* scale_out, int quant_kind, void* stream_) {
+  using namespace t8g::rows;
+  if (!amax) return fail(T8G_ERR_INVALID_ARGUMENT, "amax scratch word is null");
+  cudaStream_t st = static_cast<cudaStream_t>(stream_);
+  T8G_CHECK_CUDA(cudaMemsetAsync(amax, 0, sizeof(float), st), "cudaMemsetAsync(amax)");
+  QuantGivenArgs b{};
+  b.amax = amax;
+  b.scale_out = scale_out;
+  b.S = 0;
+  b.D = 8;
+  if (quant_kind == T8G_QUANT_FP8_E4M3)
+    quant_given_amax_kernel<kQuantFp8><<<1, 32, 0, st>>>(b);
+  else
+    quant_given_amax_kernel<kQuantInt8><<<1, 32, 0, st>>>(b);
+  return launch_checked("empty tensorwise scale");
+}
+
 int rms_common(bool tensorwise, const void* x, int64_t ld_x, const void* w, const void* shift, const void* scale,
                int64_t ld_mod, const int32_t* mod_index, int64_t rows_per_mod, int scale_is_multiplier, float eps,
                void* q, int64_t ld_q, float* q_scale, void* h, int64_t ld_h, void* res, int64_t ld_res,
@@ -707,7 +727,7 @@ int rms_common(bool tensorwise, const void* x, int64_t ld_x, const void* w, cons
   g_last_error[0] = '\0';
   int rc = check_row_shape("rms_mod_quant", S, D, quant_kind, 1);
   if (rc) return rc;
-  if (S == 0 || D == 0) return T8G_OK;
+  if (S == 0 || D == 0) return tensorwise ? empty_tensorwise(amax, scale_out, quant_kind, stream_) : T8G_OK;
   if ((rc = check_bf16_matrix("x", x, ld_x, D, true))) return rc;
   if ((rc = check_bf16_matrix("shift", shift, ld_mod, D, true))) return rc;
   if ((rc = check_bf16_matrix("scale", scale, ld_mod, D, true))) return rc;
@@ -850,7 +870,7 @@ int swiglu_common(bool tensorwise, const void* gate, const void* up, int64_t ld_
   g_last_error[0] = '\0';
   int rc = check_row_shape("swiglu_quant", M, F, quant_kind, 2);
   if (rc) return rc;
-  if (M == 0 || F == 0) return T8G_OK;
+  if (M == 0 || F == 0) return tensorwise ? empty_tensorwise(amax, scale_out, quant_kind, stream_) : T8G_OK;
   if ((rc = check_bf16_matrix("gate", gate, ld_in, F, true))) return rc;
   if ((rc = check_bf16_matrix("up", up, ld_in, F, true))) return rc;
   if ((rc = check_bf16_matrix("act", act, ld_act, F, tensorwise))) return rc;
