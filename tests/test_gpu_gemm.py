@@ -208,6 +208,28 @@ def test_gemm_rejects_bad_arguments(ops):
         ops.gemm_dequant(x8[:, :32], w8[:, :16], xs, ws)
 
 
+@pytest.mark.parametrize("out_dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("with_bias", [True, False])
+def test_gemm_empty_k_is_the_epilogue_of_a_zero_sum(ops, out_dtype, with_bias):
+    """K = 0 passes the proxy's eligibility (K % 16 == 0): the sum is empty, so out =
+    cast(((0 * xs[m]) * ws[n]) + bias[n]) -- the bias, or NaN where a scale is not finite."""
+    M, N = 300, 136
+    g = torch.Generator(device="cuda").manual_seed(9)
+    x = torch.empty(M, 0, dtype=torch.int8, device="cuda")
+    w = torch.empty(N, 0, dtype=torch.int8, device="cuda")
+    xs = torch.rand(M, generator=g, device="cuda") + 0.5
+    xs[3] = float("inf")
+    ws = torch.rand(N, generator=g, device="cuda") + 0.5
+    bias = torch.randn(N, generator=g, device="cuda").to(out_dtype) if with_bias else None
+    out = ops.gemm_dequant(x, w, xs, ws, bias, out_dtype=out_dtype)
+    ref = (0.0 * xs[:, None]) * ws[None, :]
+    if with_bias:
+        ref = ref + bias.float()[None, :]
+    torch.testing.assert_close(out, ref.to(out_dtype), rtol=0, atol=0, equal_nan=True)
+    assert torch.isnan(out[3]).all() and not torch.isnan(out[:3]).any()
+    assert ops.device_status() == 0
+
+
 def test_gemm_i8_output_beyond_2_31_elements(ops):
     """M*N > 2^31 (the audit range of the reference's int64-offset fix): the last
     rows land where the oracle says."""

@@ -192,16 +192,54 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap&
   return T8G_OK;
 }
 
+// K = 0: the sum over k is empty and the accumulator 0, so out = cast(((0 * xs[m]) * ws[n]) +
+// bias[n]) in the epilogue's order (a NaN or infinite scale gives NaN, as it does there).
+__global__ void gemm_k0_kernel(const float* xs, const float* ws, int64_t ws_numel, const void* bias, void* out,
+                               int out_dtype, int64_t M, int64_t N, int64_t ld_out) {
+  const int64_t total = M * N;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t m = i / N, n = i - m * N;
+    float v = __fmul_rn(__fmul_rn(0.0f, xs[m]), ws[ws_numel == 1 ? 0 : n]);
+    if (out_dtype == T8G_OUT_BF16) {
+      if (bias) v = __fadd_rn(v, __bfloat162float(static_cast<const __nv_bfloat16*>(bias)[n]));
+      static_cast<__nv_bfloat16*>(out)[m * ld_out + n] = __float2bfloat16_rn(v);
+    } else if (out_dtype == T8G_OUT_F16) {
+      if (bias) v = __fadd_rn(v, __half2float(static_cast<const __half*>(bias)[n]));
+      static_cast<__half*>(out)[m * ld_out + n] = __float2half_rn(v);
+    } else {
+      if (bias) v = __fadd_rn(v, static_cast<const float*>(bias)[n]);
+      static_cast<float*>(out)[m * ld_out + n] = v;
+    }
+  }
+}
+
 int gemm_entry(int in_kind, const void* x, const void* w, const float* x_scale, const float* w_scale,
                int64_t w_scale_numel, const void* bias, int64_t bias_numel, void* out, int out_dtype, int64_t M,
                int64_t N, int64_t K, int64_t ld_x, int64_t ld_w, int64_t ld_out, void* stream_) {
   using namespace t8g::gemm;
   g_last_error[0] = '\0';
-  if (M < 0 || N < 0 || K < 1) return fail(T8G_ERR_INVALID_ARGUMENT, "bad sizes M=%lld N=%lld K=%lld", (long long)M, (long long)N, (long long)K);
+  if (M < 0 || N < 0 || K < 0) return fail(T8G_ERR_INVALID_ARGUMENT, "bad sizes M=%lld N=%lld K=%lld", (long long)M, (long long)N, (long long)K);
   if (M >= (int64_t(1) << 31) || N >= (int64_t(1) << 31) || K >= (int64_t(1) << 31))
     return fail(T8G_ERR_UNSUPPORTED, "M, N and K must each be below 2^31");
   if (out_dtype < T8G_OUT_BF16 || out_dtype > T8G_OUT_F32) return fail(T8G_ERR_INVALID_ARGUMENT, "unknown out_dtype %d", out_dtype);
   if (M == 0 || N == 0) return T8G_OK;
+  if (K == 0) {
+    // an empty sum: no operand is read, the epilogue alone runs
+    if (!x_scale || !w_scale || !out) return fail(T8G_ERR_INVALID_ARGUMENT, "null operand pointer");
+    if (w_scale_numel != 1 && w_scale_numel != N)
+      return fail(T8G_ERR_INVALID_ARGUMENT, "w_scale numel %lld is neither 1 nor N=%lld", (long long)w_scale_numel, (long long)N);
+    if (bias_numel != 0 && bias_numel != N)
+      return fail(T8G_ERR_INVALID_ARGUMENT, "bias numel %lld is neither 0 nor N=%lld", (long long)bias_numel, (long long)N);
+    if (bias_numel == N && !bias) return fail(T8G_ERR_INVALID_ARGUMENT, "bias numel is N but bias is null");
+    if (ld_out < N) return fail(T8G_ERR_INVALID_ARGUMENT, "row stride smaller than the row");
+    const int64_t total = M * N;
+    const unsigned grid = static_cast<unsigned>(std::min<int64_t>((total + 255) / 256, 148 * 8));
+    gemm_k0_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream_)>>>(
+        x_scale, w_scale, w_scale_numel, bias_numel ? bias : nullptr, out, out_dtype, M, N, ld_out);
+    T8G_CHECK_CUDA(cudaGetLastError(), "gemm (K = 0) launch");
+    return T8G_OK;
+  }
   if (!x || !w || !x_scale || !w_scale || !out) return fail(T8G_ERR_INVALID_ARGUMENT, "null operand pointer");
   if (w_scale_numel != 1 && w_scale_numel != N)
     return fail(T8G_ERR_INVALID_ARGUMENT, "w_scale numel %lld is neither 1 nor N=%lld", (long long)w_scale_numel, (long long)N);
