@@ -57,7 +57,7 @@ def _gemm(**kw):
 
 
 @pytest.mark.parametrize("kw,needle", [
-    (dict(K=0), "bad sizes"),
+    (dict(K=-1), "bad sizes"),
     (dict(dt=7), "out_dtype"),
     (dict(ws_n=5), "w_scale numel"),
     (dict(bias_n=3), "bias numel"),
