@@ -78,8 +78,9 @@ int t8g_set_device(int device);
  *   bias     [bias_numel] in the output type, numel 0 (then may be NULL) or N
  *   out      [M, N] of out_dtype (T8G_OUT_*), row stride ld_out
  * Requirements: x, w, out 16-byte aligned; ld_x, ld_w multiples of 16;
- * ld_out * element size a multiple of 16; 1 <= K; M, N, K < 2^31.
- * M == 0 or N == 0 is a no-op.
+ * ld_out * element size a multiple of 16; 0 <= K; M, N, K < 2^31.
+ * M == 0 or N == 0 is a no-op.  K == 0 (which the proxy's K % 16 rule lets through) is an
+ * empty sum: out = cast(((0 * x_scale[m]) * w_scale[n]) + bias[n]), x and w are not read.
  */
 int t8g_gemm_i8_dequant(const void* x, const void* w, const float* x_scale, const float* w_scale,
                         int64_t w_scale_numel, const void* bias, int64_t bias_numel, void* out, int out_dtype,
