@@ -712,11 +712,16 @@ def cpu_gemm_sample(O, torch, min_seconds=10.0, max_seconds=30.0):
     import numpy as np
     rng = np.random.default_rng(0)
     m_slice = 2048
-    w = {N: rng.integers(-127, 128, (N, K_DIM)).astype(np.int8) for N in N_SWEEP}
-    ws = {N: (rng.random(N).astype(np.float32) + 0.5) * 1e-3 for N in N_SWEEP}
+    # the GPU arm's distributions: N(0, 0.02) weights per channel, N(0, 1) activations with 1 %
+    # of channels x20 per token, bf16 N(0, 0.01) bias, quantised to int8 by the oracle
+    w, ws = {}, {}
+    for N in N_SWEEP:
+        w[N], ws[N] = O.quant_rows(O.round_bf16((rng.standard_normal((N, K_DIM)) * 0.02).astype(np.float32)),
+                                   O.QUANT_INT8)
     bias = {N: O.round_bf16((rng.standard_normal(N) * 0.01).astype(np.float32)) for N in N_SWEEP}
-    x = rng.integers(-127, 128, (m_slice, K_DIM)).astype(np.int8)
-    xs = (rng.random(m_slice).astype(np.float32) + 0.5) * 1e-3
+    xf = rng.standard_normal((m_slice, K_DIM)).astype(np.float32)
+    xf[:, rng.permutation(K_DIM)[: K_DIM // 100]] *= 20.0
+    x, xs = O.quant_rows(O.round_bf16(xf), O.QUANT_INT8)
     ops_done = 0.0
     t0 = time.perf_counter()
     reps = 0
@@ -733,6 +738,18 @@ def cpu_gemm_sample(O, torch, min_seconds=10.0, max_seconds=30.0):
             "sample": f"{reps} x M-slices of {m_slice} tokens for N in {list(N_SWEEP)}, K={K_DIM}; "
                       f"torch._int_mm + float32 epilogue ({el:.1f} s)",
             "slice_ms": round(el * 1e3 / (reps * len(N_SWEEP)), 2), "slice_tokens": m_slice}
+
+
+def sweep_config(world, strong):
+    """The workload of both arms' lines (the same dict, so the two lines compare)."""
+    return {"workload": WORKLOAD, "shapes_MNK": SHAPES,
+            "activations": "bf16 N(0,1), 1% channels x20, per-token int8 (amax/127, RNE, clamp 127)",
+            "weights": "N(0,0.02) per-channel int8", "bias": "bf16 N(0,0.01)", "out": "bf16",
+            "parallelism": f"token-sharded x{world} (weights replicated, no data-path collective)"
+                           + ("; each rank runs 1/N of every shape's tokens" if strong else
+                              "; each rank runs the full sweep on its own tokens"),
+            "l2": "inputs larger than L2: one step touches 0.47 GB of activations and writes "
+                  "3.8 GB of outputs, so each shape's inputs are evicted before it repeats"}
 
 
 # --------------------------------------------------------------------- arms
@@ -762,10 +779,10 @@ def run_reference(args):
                                "shapes": [[step_s[-1]["slice_tokens"], N, K_DIM] for N in N_SWEEP]},
             "higher_is_better": True,
             "scaling": args.scaling, "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "shapes_MNK": SHAPES,
-                       "sample": "each step times whole M-slices of 2048 tokens (both N) on the host cores for a "
-                                 "bounded time; value is their TOPS, and full_sweep_ms_extrapolated is one full "
-                                 "sweep at that rate (not run)"},
+            "config": sweep_config(world, args.scaling == "strong"),
+            "sample": "each step times whole M-slices of 2048 tokens (both N) on the host cores for a bounded "
+                      "time; value is their TOPS, and full_sweep_ms_extrapolated is one full sweep at that rate "
+                      "(not run)",
             "cpu_baseline": {"value": round(v, 4), "unit": "TOPS", "cores": torch.get_num_threads(), "kind": "port",
                              "sample": step_s[-1]["sample"]},
             "e2e": {"value": round(v, 4), "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -922,14 +939,7 @@ def run_ours(args):
             "metric": METRIC, "value": round(value, 2), "unit": "TOPS", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 4), "higher_is_better": True,
             "scaling": args.scaling, "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "shapes_MNK": SHAPES,
-                       "activations": "bf16 N(0,1), 1% channels x20, per-token int8 (amax/127, RNE, clamp 127)",
-                       "weights": "N(0,0.02) per-channel int8", "bias": "bf16 N(0,0.01)", "out": "bf16",
-                       "parallelism": f"token-sharded x{world} (weights replicated, no data-path collective)"
-                                      + ("; each rank runs 1/N of every shape's tokens" if strong else
-                                         "; each rank runs the full sweep on its own tokens"),
-                       "l2": "inputs larger than L2: one step touches 0.47 GB of activations and writes "
-                             "3.8 GB of outputs, so each shape's inputs are evicted before it repeats"},
+            "config": sweep_config(world, strong),
             "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(int8_peak, 1),
                          "unit": "TFLOP/s", "frac": round(achieved / int8_peak, 4),
                          "traffic": traffic.get("gemm_i8_sweep_per_step_bytes"),
